@@ -1,0 +1,385 @@
+#!/usr/bin/env python
+"""Decode benchmark: tokens/s of the B200 decode path (default: Llama-2-7B shape,
+Q4_0, batch 1, KV cache prefilled to 512 positions) on N GPUs.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+                    [--workload NAME] [--ctx C]
+
+N > 1 runs under torchrun, one rank per GPU, tensor parallel over NCCL. Prints
+one JSON line (rank 0). The reference arm (--impl reference) times the
+reference's own CPU ForwardToken (oracle/_ref, built from the reference's
+sources) on the same synthetic model.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+from mini_llama_b200 import configs as C  # noqa: E402
+
+SEED = 20261201
+# dram__bytes_read.sum + dram__bytes_write.sum of one gate/up GEMV launch
+# (22016 x 4096 Q4_0) from the ncu capture summarised in
+# profiles/gemv_q4_0_gateup_22016x4096.md; None until that capture exists.
+GEMV_TRAFFIC_BYTES = None
+
+
+def parse_args():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=64)
+    p.add_argument("--warmup", type=int, default=8)
+    p.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    p.add_argument("--workload", choices=sorted(C.WORKLOADS), default="llama2-7b-q4_0")
+    p.add_argument("--ctx", type=int, default=512, help="KV positions filled before timing")
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    return p.parse_args()
+
+
+def dist_env():
+    return (int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)),
+            int(os.environ.get("LOCAL_RANK", 0)))
+
+
+def measured_peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+# ----------------------------------------------------------------- clocks
+
+class Clocks:
+    """nvidia-smi samples during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpus):
+        self.gpus = gpus
+        self.proc = None
+        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                 "-i", ",".join(str(g) for g in self.gpus), "-lms", "200"],
+                stdout=self.f, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        self.f.flush()
+        self.f.seek(0)
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.f.read().splitlines():
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx.append(float(parts[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        os.unlink(self.f.name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# -------------------------------------------------------------- CPU legs
+
+def cpu_threads():
+    return len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
+
+
+def build_cpu_model(cfg, qtype, bias):
+    """The reference's own CPU implementation when built (oracle/_ref), else the
+    C restatement; both get the generator's exact bytes."""
+    import oracle
+
+    if oracle.ref_available():
+        r = oracle.ref()
+        r.set_threads(cpu_threads())
+        kind, lib, threads = "reference", r, r.threads()
+    else:
+        kind, lib, threads = "port", oracle.port(), 1
+    m = lib.model(cfg)
+    for k, layer, qt, rows, cols, arr in C.host_weights(cfg, qtype, SEED, bias,
+                                                        threads=cpu_threads()):
+        m.set_weight(k, layer, qt, rows, cols, arr)
+    return m, kind, threads
+
+
+def time_cpu_tokens(m, cfg, n_warm, n_max, budget_s):
+    """Greedy CPU decode from position 0: n_warm untimed, then up to n_max timed
+    tokens or until budget_s of CPU time."""
+    tok = C.prompt_ids(SEED, 1, cfg["vocab_size"])[0]
+    pos = 0
+    for _ in range(n_warm):
+        tok = int(np.argmax(m.forward_token(tok, pos)))
+        pos += 1
+    t0 = time.perf_counter()
+    n = 0
+    while n < n_max:
+        tok = int(np.argmax(m.forward_token(tok, pos)))
+        pos += 1
+        n += 1
+        if time.perf_counter() - t0 > budget_s:
+            break
+    return n, time.perf_counter() - t0
+
+
+def run_reference(args, cfg, qtype, bias, world, rank):
+    if rank != 0:
+        return
+    metric = "decode tok/s"
+    try:
+        m, kind, threads = build_cpu_model(cfg, qtype, bias)
+    except Exception as e:  # pragma: no cover
+        print(json.dumps({"impl": "reference", "unavailable": f"reference CPU build failed: {e}"}))
+        return
+    t_first = time.perf_counter()
+    n_w, _ = time_cpu_tokens(m, cfg, 0, 1, 1e9)
+    per_tok = time.perf_counter() - t_first
+    budget = 150.0
+    steps = max(1, min(args.steps, int(budget / max(per_tok, 1e-3))))
+    warm = max(0, min(args.warmup - 1, 2))
+    n, secs = time_cpu_tokens(m, cfg, warm, steps, budget)
+    v = n / secs
+    sample = (f"{n} greedy decode tokens of the full model from position {warm + 1} "
+              f"(bounded to ~{int(budget)} s), {threads} threads")
+    print(json.dumps({
+        "impl": "reference", "metric": metric, "value": v, "unit": "tok/s", "n_gpus": world,
+        "steps": n, "warmup": warm + 1, "ms_per_step": 1000.0 * secs / n,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": C.QTYPE_NAMES[qtype] + "/fp32", "data": "synthetic (seeded N(0,0.02) weights)",
+        "config": {"workload": args.workload, "batch": 1, "ctx": "0..%d" % (warm + n),
+                   "parallelism": "cpu threads"},
+        "cpu_baseline": {"value": v, "unit": "tok/s", "cores": threads, "kind": kind,
+                         "sample": sample},
+        "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }))
+
+
+# ---------------------------------------------------------------- GPU arm
+
+def gemv_roofline(torch, mlb, cfg, qtype, world, peak):
+    """Live per-launch timing of the dominant kernel: the fused gate/up GEMV of
+    this rank's shard, rotating over copies that together exceed L2."""
+    F = cfg["hidden_dim"] // world
+    n, k = 2 * F, cfg["dim"]
+    nbytes = n * ((k + 31) // 32) * C.BLOCK_BYTES[qtype] + k * 4 + (n // 2) * 4
+    copies = max(2, int(np.ceil(400e6 / nbytes)))
+    mats = [mlb.QMatrix.synthesize(qtype, n, k, SEED, 900 + i, raw=False) for i in range(copies)]
+    x = torch.randn(1, k, device="cuda")
+    y = torch.empty(1, n, device="cuda")
+    stream = torch.cuda.current_stream()
+    for m in mats:
+        m.gemv(x, y)
+    torch.cuda.synchronize()
+    evs = []
+    for i in range(8 * copies):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        mats[i % copies].gemv(x, y)
+        b.record(stream)
+        evs.append((a, b))
+    torch.cuda.synchronize()
+    ms = statistics.mean(a.elapsed_time(b) for a, b in evs)
+    achieved = nbytes / (ms * 1e-3) / 1e9
+    return {"bound": "hbm", "achieved": achieved, "peak": peak[0], "unit": "GB/s",
+            "frac": achieved / peak[0], "traffic": GEMV_TRAFFIC_BYTES,
+            "kernel": f"gemv_sb_kernel<{C.QTYPE_NAMES[qtype]}> {n}x{k}",
+            "bytes_per_launch": nbytes, "us_per_launch": ms * 1e3,
+            "peak_source": peak[1] + " (MEASURED_PEAKS.json hbm_gbs, burst)"}
+
+
+def run_gpu(args, cfg, qtype, bias, rank, world, local):
+    import torch
+
+    import mini_llama_b200 as mlb
+
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=180))
+    nccl_id = None
+    if world > 1:
+        obj = [mlb.nccl_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        nccl_id = obj[0]
+    model = mlb.CudaModel(cfg, device_id=local, tp_rank=rank, tp_size=world, nccl_id=nccl_id)
+    model.synthesize(qtype, SEED, with_bias=bias)
+    resident, step_weights = model.bytes()
+    ctx = model.context(mlb.ATTN_CPU_COMPAT)
+    stream = torch.cuda.ExternalStream(ctx.stream())
+    tok0 = C.prompt_ids(SEED, 1, cfg["vocab_size"])[0]
+    if args.ctx + args.warmup + 2 * args.steps + 2 > cfg["max_seq_len"]:
+        raise SystemExit("context too long for max_seq_len")
+
+    def barrier():
+        torch.cuda.synchronize()
+        if dist:
+            dist.barrier()
+
+    def max_over_ranks(v):
+        if not dist:
+            return v
+        t = torch.tensor([v], dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # fill the KV cache to ctx positions (greedy decode from position 0)
+    pos = 0
+    toks = ctx.decode_greedy(tok0, pos, args.ctx) if args.ctx else [tok0]
+    pos += args.ctx
+    tok = toks[-1]
+    # warm-up
+    toks = ctx.decode_greedy(tok, pos, args.warmup)
+    pos += args.warmup
+    tok = toks[-1] if toks else tok
+    barrier()
+
+    # timed: device-resident greedy decode, one graph launch per token
+    with Clocks([local]) as clk:
+        barrier()
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ev0.record(stream)
+        toks = ctx.decode_greedy(tok, pos, args.steps)
+        ev1.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+    ms = max_over_ranks(ev0.elapsed_time(ev1))
+    ctx_end = pos + args.steps
+    pos += args.steps
+    tok = toks[-1]
+    clocks = clk.summary()
+
+    # e2e: ForwardToken through the C ABI, host logits every step
+    for _ in range(2):
+        tok = int(np.argmax(ctx.forward_token(tok, pos)))
+        pos += 1
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        lg = ctx.forward_token(tok, pos)
+        tok = int(np.argmax(lg))
+        pos += 1
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1))
+
+    peak = measured_peaks()
+    roof = gemv_roofline(torch, mlb, cfg, qtype, world, peak)
+    # whole-step HBM roofline: weights + fp32 KV read at the timed context
+    kv_per_pos = 2 * cfg["n_layers"] * (cfg["n_kv_heads"] // world) * cfg["head_dim"] * 4
+    mid_ctx = (args.ctx + args.warmup + ctx_end) / 2
+    step_bytes = step_weights + kv_per_pos * mid_ctx
+    step_s = ms / 1e3 / args.steps
+    kpl = ctx.kernels_per_step()
+
+    cpu = None
+    if world == 1 and rank == 0 and not args.no_cpu_baseline:
+        try:
+            m, kind, threads = build_cpu_model(cfg, qtype, bias)
+            n, secs = time_cpu_tokens(m, cfg, 1, 64, 20.0)
+            cpu = {"value": n / secs, "unit": "tok/s", "cores": threads, "kind": kind,
+                   "sample": f"{n} greedy decode tokens of the full model at positions 1..{n} "
+                             f"(~20 s of CPU time); the timed GPU run is at context "
+                             f"{args.ctx}..{ctx_end}, where attention adds "
+                             f"{kv_per_pos * mid_ctx / 1e9:.2f} GB/token on top of "
+                             f"{step_weights / 1e9:.2f} GB of weights"}
+            del m
+        except Exception as e:
+            cpu = {"value": None, "unit": "tok/s", "cores": 0, "kind": "unavailable",
+                   "sample": str(e)[:200]}
+
+    if rank == 0:
+        value = args.steps / (ms / 1e3)
+        line = {
+            "metric": "decode tok/s", "value": value, "unit": "tok/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": C.QTYPE_NAMES[qtype] + "/fp32",
+            "data": "synthetic (seeded N(0,0.02) weights quantised like the reference; "
+                    "random prompt id)",
+            "config": {"workload": args.workload, "batch": 1, "ctx": args.ctx,
+                       "ctx_end": ctx_end,
+                       "parallelism": f"tp{world}" if world > 1 else "single gpu",
+                       "l2": "no flush: each step streams %.2f GB of weights (> 126 MB L2)"
+                             % (step_weights / 1e9),
+                       "attention": "cpu-compat (reference CPU path V sum)"},
+            "e2e": {"value": args.steps / (e2e_ms / 1e3), "unit": "tok/s",
+                    "h2d_bytes_per_step": 12, "d2h_bytes_per_step": cfg["vocab_size"] * 4,
+                    "api": "mlb_forward_token (host logits)"},
+            "roofline": roof,
+            "step_roofline": {"bound": "hbm", "bytes_per_step": step_bytes,
+                              "achieved": step_bytes / step_s / 1e9, "peak": peak[0],
+                              "unit": "GB/s", "frac": step_bytes / step_s / 1e9 / peak[0],
+                              "note": "GGUF weight bytes of this rank + fp32 KV read per token"},
+            "cpu_baseline": cpu,
+            "clocks": clocks,
+            "gpu_launches": kpl * args.steps,
+            "kernels_per_step": kpl,
+            "resident_bytes": resident,
+        }
+        print(json.dumps(line))
+    ctx.close()
+    model.close()
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    args = parse_args()
+    rank, world, local = dist_env()
+    if world != args.gpus and world > 1:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE {world}")
+    cfg, qtype, bias = C.WORKLOADS[args.workload]
+    if args.impl == "reference":
+        run_reference(args, cfg, qtype, bias, world, rank)
+        return
+    run_gpu(args, cfg, qtype, bias, rank, world, local)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,249 @@
+/*
+ * mlb200.h — C ABI of the B200 (sm_100a) decode forward path.
+ *
+ * This is the drop-in boundary under mini-llama's device branch. Each entry
+ * point names the reference interface it replaces (file:line in the
+ * reference project). All functions return MLB_OK (0) or a negative status;
+ * mlb_last_error() gives the message for the calling thread. MLB_ERR_RANGE
+ * corresponds to the reference's std::out_of_range (bad token, position,
+ * layer or head index) and MLB_ERR_INVALID to its std::runtime_error, so a C++
+ * shim can rethrow with the same exception types and messages.
+ *
+ * Pointers named *_dev are device pointers on `device_id`; `stream` is a
+ * cudaStream_t (NULL means the legacy default stream). No signature carries a
+ * framework type. Weights use the GGUF block layouts of the reference
+ * (include/mini_llama/quantized_tensor.h:26-44): Q8_0 = {fp16 d; int8 qs[32]}
+ * (34 B), Q4_0 = {fp16 d; uint8 qs[16]} (18 B), Q4_1 = {fp16 d; fp16 m; uint8
+ * qs[16]} (20 B), row-major [out_features, in_features] with each row padded
+ * to whole 32-element blocks; F32 weights are plain row-major floats.
+ */
+#ifndef MLB200_H
+#define MLB200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define MLB_OK 0
+#define MLB_ERR_INVALID (-1)  /* reference: std::runtime_error */
+#define MLB_ERR_RANGE (-2)    /* reference: std::out_of_range */
+#define MLB_ERR_CUDA (-3)     /* a CUDA runtime call failed */
+#define MLB_ERR_NCCL (-4)     /* an NCCL call failed */
+#define MLB_ERR_TIMEOUT (-5)  /* a bounded device wait gave up */
+
+/* QuantType order of include/mini_llama/quantized_tensor.h:18-23. */
+#define MLB_F32 0
+#define MLB_Q8_0 1
+#define MLB_Q4_0 2
+#define MLB_Q4_1 3
+
+/* RopeType, include/mini_llama/model.h:11-14. */
+#define MLB_ROPE_NORMAL 0
+#define MLB_ROPE_NEOX 1
+
+/* Weight kinds in the upload order of UploadModelWeightsToCuda,
+ * src/model.cc:353-369. */
+#define MLB_W_TOKEN_EMBEDDING 0
+#define MLB_W_FINAL_NORM 1
+#define MLB_W_LM_HEAD 2
+#define MLB_W_ATTENTION_NORM 3
+#define MLB_W_WQ 4
+#define MLB_W_WK 5
+#define MLB_W_WV 6
+#define MLB_W_BQ 7
+#define MLB_W_BK 8
+#define MLB_W_BV 9
+#define MLB_W_WO 10
+#define MLB_W_FFN_NORM 11
+#define MLB_W_GATE 12
+#define MLB_W_UP 13
+#define MLB_W_DOWN 14
+
+/* Attention modes of a decode context. CPU_COMPAT reproduces the reference
+ * CPU path, whose V sum stops before the current position while the softmax
+ * covers it (src/forward.cc:501-518); STANDARD sums V over t <= pos like the
+ * reference GPU kernel (src/cuda_attention.cu:192-203). */
+#define MLB_ATTN_CPU_COMPAT 0
+#define MLB_ATTN_STANDARD 1
+
+/* Thread-local message of the last failed call on this thread. */
+const char* mlb_last_error(void);
+
+/* Replaces CudaQuantBuilt/CudaOpsBuilt/CudaAttentionBuilt/CudaRuntimeBuilt
+ * (include/mini_llama/cuda_quant.h:10, cuda_ops.h:9, cuda_attention.h:9,
+ * cuda_runtime.h:26): 1 when the sm_100a kernels are compiled in. */
+int mlb_built(void);
+
+/* Replaces CudaDeviceCount (include/mini_llama/cuda_runtime.h:27). */
+int mlb_device_count(int* count);
+
+/* ------------------------------------------------------------------ linear
+ * y[rows, out] = x[rows, in] * W^T over raw GGUF blocks on the device.
+ * Replaces CudaQ80LinearDeviceInput / CudaQ40LinearDeviceInput /
+ * CudaQ41LinearDeviceInput (include/mini_llama/cuda_quant.h:18,24,30) and,
+ * for qtype MLB_F32, CudaLinearDeviceInput (include/mini_llama/cuda_matmul.h:18).
+ * block_count must equal out * ceil(in / 32) (F32: out * in), the check of
+ * src/cuda_quant.cu:206-223. */
+int mlb_linear(int qtype, const float* x_dev, int rows, int in_features,
+               const void* w_dev, size_t block_count, int out_features,
+               float* y_dev, int device_id, void* stream);
+
+/* Host activations and host weights, optional host bias (may be NULL):
+ * replaces CudaQ80Linear / CudaQ40Linear / CudaQ41Linear
+ * (include/mini_llama/cuda_quant.h:12,20,26) and CudaLinear
+ * (include/mini_llama/cuda_matmul.h:14). Synchronous. */
+int mlb_linear_host(int qtype, const float* x, int rows, int in_features,
+                    const void* w, size_t block_count, int out_features,
+                    const float* bias, float* y, int device_id);
+
+/* Host activations, device weights, optional host bias: replaces
+ * CudaQ80LinearDeviceWeight / CudaQ40LinearDeviceWeight /
+ * CudaQ41LinearDeviceWeight (include/mini_llama/cuda_quant.h:14,22,28) and
+ * CudaLinearDeviceWeight (include/mini_llama/cuda_matmul.h:16). Synchronous. */
+int mlb_linear_device_weight(int qtype, const float* x, int rows,
+                             int in_features, const void* w_dev,
+                             size_t block_count, int out_features,
+                             const float* bias, float* y, int device_id);
+
+/* -------------------------------------------------------- elementwise ops
+ * Replace the device-input ops of include/mini_llama/cuda_ops.h:21-37. */
+/* CudaRmsNormDeviceWeight (cuda_ops.h:27): y = x / sqrt(mean(x^2)+eps) * w. */
+int mlb_rmsnorm(const float* x_dev, const float* w_dev, int n, float eps,
+                float* y_dev, int device_id, void* stream);
+/* CudaSiluDeviceInput (cuda_ops.h:29). */
+int mlb_silu(const float* x_dev, int n, float* y_dev, int device_id, void* stream);
+/* CudaElementwiseMulDeviceInput (cuda_ops.h:31). */
+int mlb_mul(const float* a_dev, const float* b_dev, int n, float* y_dev,
+            int device_id, void* stream);
+/* CudaElementwiseAddDeviceInput / DeviceWeight (cuda_ops.h:33,35). */
+int mlb_add(const float* a_dev, const float* b_dev, int n, float* y_dev,
+            int device_id, void* stream);
+/* CudaSoftmax (cuda_ops.h:19), on device data. */
+int mlb_softmax(const float* x_dev, int n, float* y_dev, int device_id, void* stream);
+/* CudaEmbeddingLookupDeviceWeight (cuda_ops.h:23): y = table[token, :]. */
+int mlb_embedding(const float* table_dev, int vocab, int dim, int token,
+                  float* y_dev, int device_id, void* stream);
+/* CudaRopeDeviceInput (cuda_ops.h:37): in-place RoPE of q [n_heads, D] and
+ * k [n_kv_heads, D]; the angles are evaluated on the host exactly as the
+ * reference CPU path does (src/ops.cc:143-178). */
+int mlb_rope(float* q_dev, float* k_dev, int n_heads, int n_kv_heads,
+             int head_dim, int pos, float theta, int rope_type, int device_id,
+             void* stream);
+/* Index of the largest logit, lowest index on ties (ArgMax, src/ops.cc:220). */
+int mlb_argmax(const float* x_dev, int n, int* index_host, int device_id, void* stream);
+
+/* ------------------------------------------------------ KV cache + attention
+ * The cache is two fp32 arrays [n_layers][max_seq_len][n_kv_heads][head_dim]
+ * (keys, values), the layout of CudaKvCache (src/cuda_kv_cache.cc:328-333). */
+/* CudaKvCache::WriteDevice (include/mini_llama/cuda_kv_cache.h:28). */
+int mlb_kv_write(float* keys_dev, float* values_dev, int n_layers,
+                 int max_seq_len, int n_kv_heads, int head_dim, int layer,
+                 int pos, const float* k_dev, const float* v_dev, int device_id,
+                 void* stream);
+/* CudaAttentionDecodeDeviceInput (include/mini_llama/cuda_attention.h:13):
+ * out[n_heads, D] = softmax(q K^T / sqrt(D)) V over positions [0, pos] of
+ * `layer`, GQA head map h / (n_heads / n_kv_heads). mode is MLB_ATTN_*. */
+int mlb_attention_decode(const float* q_dev, const float* keys_dev,
+                         const float* values_dev, int n_layers, int max_seq_len,
+                         int layer, int pos, int n_heads, int n_kv_heads,
+                         int head_dim, int mode, float* out_dev, int device_id,
+                         void* stream);
+
+/* --------------------------------------------------------- prepared weights
+ * A weight repacked once into the B200 GEMV layout (what the decode path
+ * streams). No reference counterpart as an API: it is the device-resident
+ * form UploadModelWeightsToCuda keeps (src/model.cc:345-374). */
+typedef struct mlb_qmatrix mlb_qmatrix;
+int mlb_qmatrix_create(int qtype, const void* w, int w_is_host,
+                       int out_features, int in_features, int device_id,
+                       mlb_qmatrix** out);
+/* Fills a prepared weight with the seeded synthetic generator (GGUF blocks of
+ * N(0,1) * scale quantised like the reference, or raw random blocks when
+ * raw != 0); bit-identical to the host generator. */
+int mlb_qmatrix_synthesize(int qtype, int out_features, int in_features,
+                           uint64_t seed, uint64_t stream_id, int raw,
+                           int device_id, mlb_qmatrix** out);
+/* y[rows, out] = x[rows, in] * W^T, device pointers, on `stream`. */
+int mlb_qmatrix_gemv(mlb_qmatrix* m, const float* x_dev, int rows, float* y_dev,
+                     void* stream);
+/* Algorithmic GGUF bytes of the weight (what a GEMV must stream). */
+size_t mlb_qmatrix_bytes(const mlb_qmatrix* m);
+int mlb_qmatrix_destroy(mlb_qmatrix* m);
+
+/* ---------------------------------------------------- model and decode step
+ * mlb_config mirrors ModelConfig (include/mini_llama/model.h:21-33). */
+typedef struct {
+  int vocab_size, dim, hidden_dim, n_layers, n_heads, n_kv_heads, head_dim,
+      max_seq_len;
+  float rope_theta, rms_norm_eps;
+  int rope_type;
+} mlb_config;
+
+typedef struct mlb_model mlb_model;
+typedef struct mlb_context mlb_context;
+
+/* Replaces UploadModelWeightsToCuda (include/mini_llama/model.h:103) together
+ * with mlb_model_set_weight / mlb_model_finalize. With tp_size > 1 the model
+ * holds this rank's tensor-parallel shard (wq/wk/wv/w_gate/w_up split by
+ * output rows, wo/w_down by input columns, lm_head by vocabulary rows) and
+ * joins an NCCL communicator built from nccl_id (128 bytes from
+ * mlb_nccl_unique_id on rank 0); tp_size == 1 ignores nccl_id. */
+int mlb_model_create(const mlb_config* cfg, int device_id, int tp_rank,
+                     int tp_size, const void* nccl_id, mlb_model** out);
+/* Uploads one weight given in full (unsharded) reference layout from host
+ * memory; the model keeps only its shard, repacked. kind is MLB_W_*, layer is
+ * ignored for the three global tensors. 1-D tensors use rows = 1. */
+int mlb_model_set_weight(mlb_model* m, int kind, int layer, int qtype, int rows,
+                         int cols, const void* host_data, size_t bytes);
+/* Generates every weight on the device with the seeded synthetic generator:
+ * linear weights N(0,0.02) quantised to qtype, norms 1.0, embedding
+ * N(0,0.02) fp32, and q/k/v biases N(0,0.02) when with_bias != 0. */
+int mlb_model_synthesize(mlb_model* m, int qtype, uint64_t seed, int with_bias);
+/* Checks that every weight is present and builds the decode plan. */
+int mlb_model_finalize(mlb_model* m);
+int mlb_model_destroy(mlb_model* m);
+/* Resident bytes of the weights on this device (ModelCudaMemoryBytes,
+ * include/mini_llama/model.h:119) and algorithmic GGUF bytes one decode step
+ * streams from HBM on this rank. */
+int mlb_model_bytes(const mlb_model* m, size_t* resident, size_t* per_step_weights);
+
+/* Replaces MiniLlamaContext's CUDA KV cache (include/mini_llama/context.h:13,
+ * CudaKvCache::Reset src/cuda_kv_cache.cc:60-92): allocates and zeroes the
+ * fp32 KV cache for max_seq_len positions and all decode buffers once. */
+int mlb_context_create(mlb_model* m, int attention_mode, mlb_context** out);
+int mlb_context_destroy(mlb_context* c);
+/* Clears the KV cache (CudaKvCache::Clear, src/cuda_kv_cache.cc:96-110). */
+int mlb_context_reset(mlb_context* c);
+
+/* Replaces ForwardToken's device branch (src/forward.cc:776-794): runs one
+ * decode step for `token` at `pos` and copies the vocab_size logits to host
+ * memory. Validation follows ValidateForwardInputs (src/forward.cc:53-79). */
+int mlb_forward_token(mlb_context* c, int token, int pos, float* logits_host);
+/* Same step with the logits left on the device; returns the device pointer
+ * in *logits_dev (valid until the next step). Asynchronous on the context's
+ * stream; mlb_context_sync waits for it. */
+int mlb_forward_token_device(mlb_context* c, int token, int pos,
+                             const float** logits_dev);
+int mlb_context_sync(mlb_context* c);
+/* Greedy decode kept on the device: step 0 feeds `token` at `pos`, each later
+ * step feeds the previous step's argmax (ArgMax tie rule). Writes n_steps
+ * token ids (the argmax of each step) to tokens_host. One CUDA graph launch
+ * per step, no host round trip between steps. */
+int mlb_decode_greedy(mlb_context* c, int token, int pos, int n_steps,
+                      int* tokens_host);
+/* The context's stream (cudaStream_t), for timing with events. */
+void* mlb_context_stream(mlb_context* c);
+/* Number of kernels one decode step launches on this rank. */
+int mlb_context_kernels_per_step(const mlb_context* c);
+
+/* 128-byte NCCL unique id for building a tensor-parallel communicator. */
+int mlb_nccl_unique_id(void* out128);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif

@@ -1,0 +1,469 @@
+"""mini_llama_b200 — B200 (sm_100a) decode forward path of mini-llama.
+
+Python mirror of the reference's device-branch interface, over the C ABI of
+include/mlb200.h (libmlb200.so). Names follow the reference
+(include/mini_llama/cuda_quant.h, cuda_matmul.h, cuda_ops.h, cuda_attention.h,
+cuda_kv_cache.h, forward.h); device memory is held in torch CUDA tensors,
+which here are plumbing only -- every computation runs in this package's own
+kernels. Errors raise ``MlbError`` (the reference's std::runtime_error) or
+``MlbRangeError`` (std::out_of_range) with the reference's messages.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+
+from . import configs
+from ._lib import MlbConfig, MlbError, MlbRangeError, check, lib, synth_lib
+from .configs import (F32, Q4_0, Q4_1, Q8_0, W_BK, W_BQ, W_BV, W_DOWN, W_FFN_NORM,
+                      W_FINAL_NORM, W_GATE, W_LM_HEAD, W_TOKEN_EMBEDDING, W_UP, W_WK, W_WO,
+                      W_WQ, W_WV, W_ATTENTION_NORM)
+
+ROPE_NORMAL, ROPE_NEOX = 0, 1
+ATTN_CPU_COMPAT, ATTN_STANDARD = 0, 1
+
+__all__ = [
+    "F32", "Q8_0", "Q4_0", "Q4_1", "ROPE_NORMAL", "ROPE_NEOX", "ATTN_CPU_COMPAT",
+    "ATTN_STANDARD", "MlbError", "MlbRangeError", "CudaQuantBuilt", "CudaDeviceCount",
+    "CudaQ80LinearDeviceInput", "CudaQ40LinearDeviceInput", "CudaQ41LinearDeviceInput",
+    "CudaLinearDeviceInput", "CudaQ80Linear", "CudaQ40Linear", "CudaQ41Linear", "CudaLinear",
+    "CudaRmsNormDeviceWeight", "CudaSiluDeviceInput", "CudaElementwiseMulDeviceInput",
+    "CudaElementwiseAddDeviceInput", "CudaSoftmax", "CudaEmbeddingLookupDeviceWeight",
+    "CudaRopeDeviceInput", "CudaArgMax", "CudaKvCache", "CudaAttentionDecodeDeviceInput",
+    "QMatrix", "CudaModel", "Context", "ForwardToken", "configs",
+]
+
+
+def _torch():
+    import torch  # device memory and streams only
+
+    return torch
+
+
+def _ptr(t):
+    return ctypes.c_void_p(t.data_ptr())
+
+
+def _stream(stream):
+    torch = _torch()
+    if stream is None:
+        return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    return ctypes.c_void_p(stream)
+
+
+def CudaQuantBuilt() -> bool:
+    """CudaQuantBuilt (include/mini_llama/cuda_quant.h:10)."""
+    return bool(lib().mlb_built())
+
+
+def CudaDeviceCount() -> int:
+    """CudaDeviceCount (include/mini_llama/cuda_runtime.h:27)."""
+    n = ctypes.c_int(0)
+    check(lib().mlb_device_count(ctypes.byref(n)))
+    return n.value
+
+
+# ------------------------------------------------------------------ linear
+
+def _linear_device_input(qtype, x, w_dev, block_count, weight_shape, device_id, stream=None):
+    torch = _torch()
+    if len(weight_shape) != 2:
+        raise MlbError(-1, "expected weight shape [out_features, in_features]")
+    out_f, in_f = int(weight_shape[0]), int(weight_shape[1])
+    if x.dim() not in (1, 2):
+        raise MlbError(-1, "expected x shape [in_features] or [batch, in_features]")
+    if x.shape[-1] != in_f:
+        raise MlbError(-1, f"dimension mismatch x={list(x.shape)} weight=[{out_f}, {in_f}]")
+    rows = 1 if x.dim() == 1 else x.shape[0]
+    x = x.contiguous()
+    y = torch.empty((out_f,) if x.dim() == 1 else (rows, out_f), dtype=torch.float32,
+                    device=x.device)
+    check(lib().mlb_linear(qtype, _ptr(x), rows, in_f, _ptr(w_dev), block_count, out_f, _ptr(y),
+                           device_id, _stream(stream)))
+    return y
+
+
+def CudaQ80LinearDeviceInput(x, w_dev, block_count, weight_shape, device_id=0, stream=None):
+    """CudaQ80LinearDeviceInput (include/mini_llama/cuda_quant.h:18)."""
+    return _linear_device_input(Q8_0, x, w_dev, block_count, weight_shape, device_id, stream)
+
+
+def CudaQ40LinearDeviceInput(x, w_dev, block_count, weight_shape, device_id=0, stream=None):
+    """CudaQ40LinearDeviceInput (include/mini_llama/cuda_quant.h:24)."""
+    return _linear_device_input(Q4_0, x, w_dev, block_count, weight_shape, device_id, stream)
+
+
+def CudaQ41LinearDeviceInput(x, w_dev, block_count, weight_shape, device_id=0, stream=None):
+    """CudaQ41LinearDeviceInput (include/mini_llama/cuda_quant.h:30), with the CPU
+    path's d*q + m dequantisation (src/quant.cc:455)."""
+    return _linear_device_input(Q4_1, x, w_dev, block_count, weight_shape, device_id, stream)
+
+
+def CudaLinearDeviceInput(x, w_dev, weight_shape, device_id=0, stream=None):
+    """CudaLinearDeviceInput (include/mini_llama/cuda_matmul.h:18), F32 weights."""
+    return _linear_device_input(F32, x, w_dev, int(weight_shape[0]) * int(weight_shape[1]),
+                                weight_shape, device_id, stream)
+
+
+def _linear_host(qtype, x, blocks, weight_shape, bias, device_id):
+    x = np.ascontiguousarray(x, np.float32)
+    blocks = np.ascontiguousarray(blocks)
+    out_f, in_f = int(weight_shape[0]), int(weight_shape[1])
+    rows = 1 if x.ndim == 1 else x.shape[0]
+    nblk = out_f * in_f if qtype == F32 else out_f * ((in_f + 31) // 32)
+    y = np.zeros((rows, out_f), np.float32)
+    b = None if bias is None else np.ascontiguousarray(bias, np.float32)
+    check(lib().mlb_linear_host(qtype, x.ctypes.data, rows, in_f, blocks.ctypes.data, nblk, out_f,
+                                None if b is None else b.ctypes.data, y.ctypes.data, device_id))
+    return y[0] if x.ndim == 1 else y
+
+
+def CudaQ80Linear(x, blocks, weight_shape, bias=None, device_id=0):
+    """CudaQ80Linear (include/mini_llama/cuda_quant.h:12): host in, host out."""
+    return _linear_host(Q8_0, x, blocks, weight_shape, bias, device_id)
+
+
+def CudaQ40Linear(x, blocks, weight_shape, bias=None, device_id=0):
+    """CudaQ40Linear (include/mini_llama/cuda_quant.h:20)."""
+    return _linear_host(Q4_0, x, blocks, weight_shape, bias, device_id)
+
+
+def CudaQ41Linear(x, blocks, weight_shape, bias=None, device_id=0):
+    """CudaQ41Linear (include/mini_llama/cuda_quant.h:26)."""
+    return _linear_host(Q4_1, x, blocks, weight_shape, bias, device_id)
+
+
+def CudaLinear(x, weight, bias=None, device_id=0):
+    """CudaLinear (include/mini_llama/cuda_matmul.h:14): F32 weight [out, in]."""
+    weight = np.ascontiguousarray(weight, np.float32)
+    return _linear_host(F32, x, weight, weight.shape, bias, device_id)
+
+
+# ------------------------------------------------------------- elementwise
+
+def _empty_like(x):
+    return _torch().empty_like(x)
+
+
+def CudaRmsNormDeviceWeight(x, w, eps, device_id=0, stream=None):
+    """CudaRmsNormDeviceWeight (include/mini_llama/cuda_ops.h:27)."""
+    if x.dim() != 1 or w.dim() != 1:
+        raise MlbError(-1, "RmsNorm: expected 1D tensors")
+    if x.shape[0] != w.shape[0]:
+        raise MlbError(-1, "RmsNorm: dimension mismatch")
+    y = _empty_like(x)
+    check(lib().mlb_rmsnorm(_ptr(x), _ptr(w), x.numel(), eps, _ptr(y), device_id, _stream(stream)))
+    return y
+
+
+def CudaSiluDeviceInput(x, device_id=0, stream=None):
+    """CudaSiluDeviceInput (include/mini_llama/cuda_ops.h:29)."""
+    y = _empty_like(x)
+    check(lib().mlb_silu(_ptr(x), x.numel(), _ptr(y), device_id, _stream(stream)))
+    return y
+
+
+def CudaElementwiseMulDeviceInput(a, b, device_id=0, stream=None):
+    """CudaElementwiseMulDeviceInput (include/mini_llama/cuda_ops.h:31)."""
+    if a.shape != b.shape:
+        raise MlbError(-1, f"ElementwiseMul: shape mismatch {list(a.shape)} vs {list(b.shape)}")
+    y = _empty_like(a)
+    check(lib().mlb_mul(_ptr(a), _ptr(b), a.numel(), _ptr(y), device_id, _stream(stream)))
+    return y
+
+
+def CudaElementwiseAddDeviceInput(a, b, device_id=0, stream=None):
+    """CudaElementwiseAddDeviceInput (include/mini_llama/cuda_ops.h:33)."""
+    if a.numel() != b.numel():
+        raise MlbError(-1, f"ElementwiseAdd: shape mismatch {list(a.shape)} vs {list(b.shape)}")
+    y = _empty_like(a)
+    check(lib().mlb_add(_ptr(a), _ptr(b), a.numel(), _ptr(y), device_id, _stream(stream)))
+    return y
+
+
+def CudaSoftmax(x, device_id=0, stream=None):
+    """CudaSoftmax (include/mini_llama/cuda_ops.h:19) on device data."""
+    if x.dim() != 1:
+        raise MlbError(-1, "Softmax: expected 1D tensor")
+    y = _empty_like(x)
+    check(lib().mlb_softmax(_ptr(x), x.numel(), _ptr(y), device_id, _stream(stream)))
+    return y
+
+
+def CudaEmbeddingLookupDeviceWeight(table, token_id, device_id=0, stream=None):
+    """CudaEmbeddingLookupDeviceWeight (include/mini_llama/cuda_ops.h:23)."""
+    vocab, dim = table.shape
+    y = _torch().empty(dim, dtype=table.dtype, device=table.device)
+    check(lib().mlb_embedding(_ptr(table), vocab, dim, int(token_id), _ptr(y), device_id,
+                              _stream(stream)))
+    return y
+
+
+def CudaRopeDeviceInput(q, k, n_heads, n_kv_heads, head_dim, pos, theta,
+                        rope_type=ROPE_NORMAL, device_id=0, stream=None):
+    """CudaRopeDeviceInput (include/mini_llama/cuda_ops.h:37): in place."""
+    check(lib().mlb_rope(_ptr(q), _ptr(k), n_heads, n_kv_heads, head_dim, pos, theta, rope_type,
+                         device_id, _stream(stream)))
+
+
+def CudaArgMax(x, device_id=0, stream=None) -> int:
+    """ArgMax (src/ops.cc:220) on device logits; lowest index wins ties."""
+    out = ctypes.c_int(0)
+    check(lib().mlb_argmax(_ptr(x), x.numel(), ctypes.byref(out), device_id, _stream(stream)))
+    return out.value
+
+
+# -------------------------------------------------------- KV cache, attention
+
+class CudaKvCache:
+    """CudaKvCache (include/mini_llama/cuda_kv_cache.h:9-57): fp32 keys and values
+    [n_layers, max_seq_len, n_kv_heads, head_dim] on one device."""
+
+    def __init__(self, n_layers=0, max_seq_len=0, n_kv_heads=0, head_dim=0, device_id=0):
+        self.keys = self.values = None
+        self._shape = (0, 0, 0, 0)
+        self.device_id = device_id
+        if n_layers:
+            self.Reset(n_layers, max_seq_len, n_kv_heads, head_dim, device_id)
+
+    def Reset(self, n_layers, max_seq_len, n_kv_heads, head_dim, device_id=0):
+        torch = _torch()
+        for name, v in (("n_layers", n_layers), ("max_seq_len", max_seq_len),
+                        ("n_kv_heads", n_kv_heads), ("head_dim", head_dim)):
+            if v <= 0:
+                raise MlbError(-1, f"CudaKvCache: {name} must be positive")
+        self.device_id = device_id
+        self._shape = (n_layers, max_seq_len, n_kv_heads, head_dim)
+        dev = torch.device("cuda", device_id)
+        self.keys = torch.zeros(self._shape, dtype=torch.float32, device=dev)
+        self.values = torch.zeros(self._shape, dtype=torch.float32, device=dev)
+
+    def Clear(self):
+        if self.keys is not None:
+            self.keys.zero_()
+            self.values.zero_()
+
+    def empty(self):
+        return self.keys is None
+
+    def n_layers(self):
+        return self._shape[0]
+
+    def max_seq_len(self):
+        return self._shape[1]
+
+    def n_kv_heads(self):
+        return self._shape[2]
+
+    def head_dim(self):
+        return self._shape[3]
+
+    def bytes(self):
+        return 0 if self.keys is None else self.keys.numel() * 4
+
+    def WriteDevice(self, layer, pos, k, v, stream=None):
+        L, S, KV, D = self._shape
+        check(lib().mlb_kv_write(_ptr(self.keys) if self.keys is not None else None,
+                                 _ptr(self.values) if self.values is not None else None,
+                                 L, S, KV, D, layer, pos, _ptr(k.contiguous()),
+                                 _ptr(v.contiguous()), self.device_id, _stream(stream)))
+
+    def ReadKeyHead(self, layer, pos, kv_head):
+        return self.keys[layer, pos, kv_head].cpu().numpy()
+
+    def ReadValueHead(self, layer, pos, kv_head):
+        return self.values[layer, pos, kv_head].cpu().numpy()
+
+
+def CudaAttentionDecodeDeviceInput(q, kv_cache: CudaKvCache, layer, pos, n_heads, n_kv_heads,
+                                   head_dim, device_id=0, mode=ATTN_STANDARD, stream=None):
+    """CudaAttentionDecodeDeviceInput (include/mini_llama/cuda_attention.h:13).
+    mode ATTN_STANDARD matches the reference GPU kernel; ATTN_CPU_COMPAT the CPU path."""
+    torch = _torch()
+    if q.numel() != n_heads * head_dim:
+        raise MlbError(-1, "CudaAttentionDecodeDeviceInput: q shape mismatch")
+    if kv_cache.empty():
+        raise MlbError(-1, "CudaAttentionDecodeDeviceInput: CUDA KV cache is empty")
+    if kv_cache.n_kv_heads() != n_kv_heads or kv_cache.head_dim() != head_dim:
+        raise MlbError(-1, "CudaAttentionDecodeDeviceInput: KV cache shape or device does not "
+                           "match attention shape")
+    out = torch.empty(n_heads * head_dim, dtype=torch.float32, device=q.device)
+    L, S, _, _ = kv_cache._shape
+    check(lib().mlb_attention_decode(_ptr(q.contiguous()), _ptr(kv_cache.keys),
+                                     _ptr(kv_cache.values), L, S, layer, pos, n_heads, n_kv_heads,
+                                     head_dim, mode, _ptr(out), device_id, _stream(stream)))
+    return out
+
+
+# ------------------------------------------------------ prepared weight GEMV
+
+class QMatrix:
+    """A weight repacked into the B200 GEMV layout (the decode path's format)."""
+
+    def __init__(self, handle, qtype, out_features, in_features):
+        self.h = handle
+        self.qtype, self.out_features, self.in_features = qtype, out_features, in_features
+
+    @classmethod
+    def from_gguf(cls, qtype, blocks, out_features, in_features, device_id=0):
+        """blocks: host numpy uint8/float32 array, or a CUDA tensor, in GGUF layout."""
+        h = ctypes.c_void_p()
+        if isinstance(blocks, np.ndarray):
+            blocks = np.ascontiguousarray(blocks)
+            check(lib().mlb_qmatrix_create(qtype, blocks.ctypes.data, 1, out_features, in_features,
+                                           device_id, ctypes.byref(h)))
+        else:
+            check(lib().mlb_qmatrix_create(qtype, _ptr(blocks), 0, out_features, in_features,
+                                           device_id, ctypes.byref(h)))
+        return cls(h, qtype, out_features, in_features)
+
+    @classmethod
+    def synthesize(cls, qtype, out_features, in_features, seed, stream_id=0, raw=False,
+                   device_id=0):
+        h = ctypes.c_void_p()
+        check(lib().mlb_qmatrix_synthesize(qtype, out_features, in_features, seed, stream_id,
+                                           int(raw), device_id, ctypes.byref(h)))
+        return cls(h, qtype, out_features, in_features)
+
+    def gemv(self, x, y=None, stream=None):
+        torch = _torch()
+        rows = 1 if x.dim() == 1 else x.shape[0]
+        if y is None:
+            y = torch.empty((rows, self.out_features) if x.dim() == 2 else (self.out_features,),
+                            dtype=torch.float32, device=x.device)
+        check(lib().mlb_qmatrix_gemv(self.h, _ptr(x), rows, _ptr(y), _stream(stream)))
+        return y
+
+    def gguf_bytes(self):
+        return lib().mlb_qmatrix_bytes(self.h)
+
+    def __del__(self):
+        try:
+            if self.h:
+                lib().mlb_qmatrix_destroy(self.h)
+                self.h = None
+        except Exception:
+            pass
+
+
+# ------------------------------------------------------------ model, context
+
+class CudaModel:
+    """Device-resident model: UploadModelWeightsToCuda (src/model.cc:345-374) as
+    set_weight/finalize, or seeded on-device synthesis. tp_size > 1 keeps this
+    rank's tensor-parallel shard (nccl_id: 128 bytes from nccl_unique_id())."""
+
+    def __init__(self, cfg: dict, device_id=0, tp_rank=0, tp_size=1, nccl_id: bytes | None = None):
+        self.cfg = dict(cfg)
+        self.device_id = device_id
+        c = MlbConfig(**{k: cfg[k] for k, _ in MlbConfig._fields_})
+        h = ctypes.c_void_p()
+        idbuf = None if nccl_id is None else ctypes.create_string_buffer(bytes(nccl_id), 128)
+        check(lib().mlb_model_create(ctypes.byref(c), device_id, tp_rank, tp_size, idbuf,
+                                     ctypes.byref(h)))
+        self.h = h
+
+    def set_weight(self, kind, layer, qtype, rows, cols, data: np.ndarray):
+        data = np.ascontiguousarray(data)
+        check(lib().mlb_model_set_weight(self.h, kind, layer, qtype, rows, cols, data.ctypes.data,
+                                         data.nbytes))
+
+    def load(self, weights):
+        """weights: iterable of (kind, layer, qtype, rows, cols, array)."""
+        for kind, layer, qtype, rows, cols, arr in weights:
+            self.set_weight(kind, layer, qtype, rows, cols, arr)
+        self.finalize()
+        return self
+
+    def synthesize(self, qtype, seed, with_bias=False):
+        check(lib().mlb_model_synthesize(self.h, qtype, seed, int(with_bias)))
+        return self
+
+    def finalize(self):
+        check(lib().mlb_model_finalize(self.h))
+        return self
+
+    def bytes(self):
+        r, s = ctypes.c_size_t(), ctypes.c_size_t()
+        check(lib().mlb_model_bytes(self.h, ctypes.byref(r), ctypes.byref(s)))
+        return r.value, s.value
+
+    def context(self, attention_mode=ATTN_CPU_COMPAT):
+        return Context(self, attention_mode)
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().mlb_model_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class Context:
+    """MiniLlamaContext with its CUDA KV cache (include/mini_llama/context.h)."""
+
+    def __init__(self, model: CudaModel, attention_mode=ATTN_CPU_COMPAT):
+        self.model = model
+        h = ctypes.c_void_p()
+        check(lib().mlb_context_create(model.h, attention_mode, ctypes.byref(h)))
+        self.h = h
+        self.pos = 0
+        self.token_history = []
+
+    def forward_token(self, token: int, pos: int) -> np.ndarray:
+        """ForwardToken's device branch (src/forward.cc:776-794): host logits."""
+        out = np.empty(self.model.cfg["vocab_size"], np.float32)
+        check(lib().mlb_forward_token(self.h, int(token), int(pos), out.ctypes.data))
+        return out
+
+    def forward_token_device(self, token: int, pos: int) -> int:
+        """Asynchronous step; returns the device address of the logits."""
+        p = ctypes.c_void_p()
+        check(lib().mlb_forward_token_device(self.h, int(token), int(pos), ctypes.byref(p)))
+        return p.value
+
+    def sync(self):
+        check(lib().mlb_context_sync(self.h))
+
+    def decode_greedy(self, token: int, pos: int, n_steps: int) -> list:
+        out = np.empty(max(n_steps, 1), np.int32)
+        check(lib().mlb_decode_greedy(self.h, int(token), int(pos), int(n_steps), out.ctypes.data))
+        return [int(t) for t in out[:n_steps]]
+
+    def reset(self):
+        check(lib().mlb_context_reset(self.h))
+        self.pos = 0
+        self.token_history = []
+
+    def stream(self) -> int:
+        return lib().mlb_context_stream(self.h) or 0
+
+    def kernels_per_step(self) -> int:
+        return lib().mlb_context_kernels_per_step(self.h)
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().mlb_context_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def ForwardToken(ctx: Context, token: int) -> np.ndarray:
+    """ForwardToken(ctx, model, token) (include/mini_llama/forward.h:11) at ctx.pos."""
+    return ctx.forward_token(token, ctx.pos)
+
+
+def nccl_unique_id() -> bytes:
+    buf = ctypes.create_string_buffer(128)
+    check(lib().mlb_nccl_unique_id(buf))
+    return buf.raw

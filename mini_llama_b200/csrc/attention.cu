@@ -1,0 +1,363 @@
+// attention.cu — split-K flash-decode attention over the fp32 KV cache.
+//
+// Reference: CudaAttentionDecodeDeviceInput (src/cuda_attention.cu:263-309:
+// a score kernel writing [n_heads, pos+1] to global memory, then a per-head
+// softmax + V-sum kernel, each followed by cudaDeviceSynchronize) and the CPU
+// AttentionForward (src/forward.cc:487-545).
+//
+// Here one CTA handles one KV head and one slice of the positions [0, pos]:
+// all q heads of the GQA group (h / (H/KV) == kv head) share each K/V tile,
+// which is staged in shared memory with cp.async, scores and an online
+// softmax (running max m, sum l) stay on chip, and the CTA writes (m, l, O)
+// for its slice. The last CTA of a KV head to finish (arrival counter)
+// combines the slices in slice order, so results are deterministic.
+//
+// include_current_v = 0 reproduces the reference CPU path (its V sum stops at
+// t < pos while the softmax covers t <= pos, src/forward.cc:501-518);
+// include_current_v = 1 is standard attention, as the reference GPU kernel.
+#include <algorithm>
+#include <cfloat>
+
+#include "attention.cuh"
+
+namespace mlb {
+
+constexpr int kAttnThreads = 128;
+constexpr int kAttnTile = 32;  // positions per shared-memory tile
+
+struct AttnKArgs {
+  const float* q;
+  const float* keys;    // layer base [max_seq][KV][D]
+  const float* values;
+  const int* pos_dev;
+  int pos_host;
+  int H, KV, D, nsplit;
+  float scale;
+  int include_current_v;
+  float* ws;            // [KV][nsplit][G][D + 2]
+  int* counters;        // [KV]
+  float* out;           // [H][D]
+};
+
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(smem)), "l"(gmem)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+__global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnKArgs a) {
+  extern __shared__ __align__(16) float sm[];
+  const int D = a.D, G = a.H / a.KV, KV = a.KV;
+  const int pitch = D + 4;  // floats per staged row (no bank conflicts on 16-byte loads)
+  const int kvh = blockIdx.x, split = blockIdx.y;
+  float* kt = sm;                              // [2][tile][pitch]
+  float* vt = kt + 2 * kAttnTile * pitch;      // [2][tile][pitch]
+  const int hstep_ = kAttnThreads / (D / 4);
+  const int region = max(4 * kAttnTile * pitch, hstep_ * G * D);  // K/V tiles, later group sums
+  float* qs = sm + region;                     // [G][D]
+  float* ps = qs + G * D;                      // [G][tile] probabilities
+  float* st = ps + G * kAttnTile;              // [G] m, [G] l, [G] alpha
+  float* mrun = st, *lrun = st + G, *alpha = st + 2 * G;
+  __shared__ int last_flag;
+
+  pdl_wait();
+  const int pos = a.pos_dev ? *a.pos_dev : a.pos_host;
+  const int n = pos + 1;
+  // slice of positions, in whole tiles
+  const int tiles = (n + kAttnTile - 1) / kAttnTile;
+  const int tiles_per = (tiles + a.nsplit - 1) / a.nsplit;
+  const int t_begin = split * tiles_per * kAttnTile;
+  const int t_end = min(n, (split + 1) * tiles_per * kAttnTile);
+  const int v_end = a.include_current_v ? n : pos;  // V rows < v_end are summed
+
+  for (int i = threadIdx.x; i < G * D; i += kAttnThreads)
+    qs[i] = a.q[(size_t)(kvh * G) * D + i];
+  for (int i = threadIdx.x; i < G; i += kAttnThreads) {
+    mrun[i] = -INFINITY;
+    lrun[i] = 0.0f;
+  }
+  const size_t row_stride = (size_t)KV * D;
+  auto load_tile = [&](int t0, int buf) {
+    const int vec = D / 4;
+    for (int i = threadIdx.x; i < kAttnTile * vec; i += kAttnThreads) {
+      int p = i / vec, c = i - p * vec;
+      int t = t0 + p;
+      float* kd = kt + (buf * kAttnTile + p) * pitch + c * 4;
+      float* vd = vt + (buf * kAttnTile + p) * pitch + c * 4;
+      if (t < t_end) {
+        const size_t off = (size_t)t * row_stride + (size_t)kvh * D + c * 4;
+        cp_async16(kd, a.keys + off);
+        cp_async16(vd, a.values + off);
+      } else {
+        *reinterpret_cast<float4*>(kd) = make_float4(0.f, 0.f, 0.f, 0.f);
+        *reinterpret_cast<float4*>(vd) = make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    }
+    cp_async_commit();
+  };
+
+  // thread layout for scores: lane = position in tile, heads h = warp, warp+4, ...
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // thread layout for P.V: 4 consecutive d per thread; the hstep thread groups
+  // split the positions of a tile and are summed once at the end (fixed order)
+  const int dvec = D / 4;
+  const int d4 = threadIdx.x % dvec, hg = threadIdx.x / dvec;
+  const int hstep = kAttnThreads / dvec;
+  const bool pv_active = hg < hstep;
+  constexpr int kMaxG = 16;
+  float4 o[kMaxG];
+#pragma unroll
+  for (int i = 0; i < kMaxG; ++i) o[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+
+  if (t_begin < t_end) load_tile(t_begin, 0);
+  __syncthreads();
+  int buf = 0;
+  for (int t0 = t_begin; t0 < t_end; t0 += kAttnTile, buf ^= 1) {
+    if (t0 + kAttnTile < t_end) {
+      load_tile(t0 + kAttnTile, buf ^ 1);
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
+    __syncthreads();
+    // scores and per-head tile statistics
+    const float* krow = kt + (buf * kAttnTile + lane) * pitch;
+    for (int h = warp; h < G; h += 4) {
+      float dot = 0.0f;
+      const float* qh = qs + h * D;
+      for (int d = 0; d < D; d += 4) {
+        float4 kv = *reinterpret_cast<const float4*>(krow + d);
+        float4 qv = *reinterpret_cast<const float4*>(qh + d);
+        dot = fmaf(qv.x, kv.x, dot);
+        dot = fmaf(qv.y, kv.y, dot);
+        dot = fmaf(qv.z, kv.z, dot);
+        dot = fmaf(qv.w, kv.w, dot);
+      }
+      const int t = t0 + lane;
+      float s = t < t_end ? __fmul_rn(dot, a.scale) : -INFINITY;
+      float tmax = warp_max(s);
+      float mold = mrun[h];
+      float mnew = fmaxf(mold, tmax);
+      float p = t < t_end ? expf(s - mnew) : 0.0f;
+      float psum = warp_sum(p);
+      if (t >= v_end) p = 0.0f;  // softmax weight counted, V row not summed
+      ps[h * kAttnTile + lane] = p;
+      if (lane == 0) {
+        float al = mold == -INFINITY ? 0.0f : expf(mold - mnew);
+        alpha[h] = al;
+        lrun[h] = lrun[h] * al + psum;
+        mrun[h] = mnew;
+      }
+    }
+    __syncthreads();
+    // O = O * alpha + P . V  (this thread: d4, positions hg, hg + hstep, ...)
+    const int tn = min(kAttnTile, t_end - t0);
+    if (pv_active) {
+#pragma unroll
+      for (int h = 0; h < kMaxG; ++h) {
+        if (h < G) {
+          const float al = alpha[h];
+          o[h].x *= al; o[h].y *= al; o[h].z *= al; o[h].w *= al;
+        }
+      }
+      for (int p = hg; p < tn; p += hstep) {
+        const float4 vv =
+            *reinterpret_cast<const float4*>(vt + (buf * kAttnTile + p) * pitch + d4 * 4);
+#pragma unroll
+        for (int h = 0; h < kMaxG; ++h) {
+          if (h < G) {
+            const float pv = ps[h * kAttnTile + p];
+            o[h].x = fmaf(pv, vv.x, o[h].x);
+            o[h].y = fmaf(pv, vv.y, o[h].y);
+            o[h].z = fmaf(pv, vv.z, o[h].z);
+            o[h].w = fmaf(pv, vv.w, o[h].w);
+          }
+        }
+      }
+    }
+    __syncthreads();
+  }
+  pdl_launch_dependents();
+
+  // sum the position groups (fixed order) through shared memory, then write
+  // this slice's (m, l, O)
+  float* gsum = kt;  // [hstep][G][D], reuses the K tiles
+  if (pv_active) {
+#pragma unroll
+    for (int h = 0; h < kMaxG; ++h)
+      if (h < G) *reinterpret_cast<float4*>(gsum + ((size_t)hg * G + h) * D + d4 * 4) = o[h];
+  }
+  __syncthreads();
+  const int rec = D + 2;
+  float* wsk = a.ws + ((size_t)kvh * a.nsplit + split) * G * rec;
+  for (int i = threadIdx.x; i < G * D; i += kAttnThreads) {
+    int h = i / D, d = i - h * D;
+    float s = 0.0f;
+    for (int gi = 0; gi < hstep; ++gi) s += gsum[((size_t)gi * G + h) * D + d];
+    wsk[h * rec + 2 + d] = s;
+  }
+  for (int h = threadIdx.x; h < G; h += kAttnThreads) {
+    wsk[h * rec] = mrun[h];
+    wsk[h * rec + 1] = lrun[h];
+  }
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) last_flag = atomicAdd(&a.counters[kvh], 1) == a.nsplit - 1;
+  __syncthreads();
+  if (!last_flag) return;
+  __threadfence();
+  // combine the slices of this KV head in slice order
+  for (int i = threadIdx.x; i < G * D; i += kAttnThreads) {
+    int h = i / D, d = i - h * D;
+    float m = -INFINITY;
+    for (int s = 0; s < a.nsplit; ++s)
+      m = fmaxf(m, __ldcg(a.ws + (((size_t)kvh * a.nsplit + s) * G + h) * rec));
+    float l = 0.0f, acc = 0.0f;
+    for (int s = 0; s < a.nsplit; ++s) {
+      const float* r = a.ws + (((size_t)kvh * a.nsplit + s) * G + h) * rec;
+      float ms = __ldcg(r);
+      if (ms == -INFINITY) continue;
+      float e = expf(ms - m);
+      l = fmaf(__ldcg(r + 1), e, l);
+      acc = fmaf(__ldcg(r + 2 + d), e, acc);
+    }
+    a.out[(size_t)(kvh * G + h) * D + d] = __fdiv_rn(acc, l);
+  }
+  if (threadIdx.x == 0) a.counters[kvh] = 0;
+}
+
+// Generic path for shapes the tiled kernel does not take (head_dim not a
+// multiple of 4, or more than 16 query heads per KV head): one CTA per query
+// head, scores in shared memory, one pass per output element.
+__global__ void attn_decode_generic_kernel(const AttnKArgs a) {
+  extern __shared__ float sc[];  // [pos + 1]
+  __shared__ float red[32];
+  __shared__ float bc;
+  const int h = blockIdx.x, G = a.H / a.KV, kvh = h / G, D = a.D;
+  const int pos = a.pos_dev ? *a.pos_dev : a.pos_host;
+  const int n = pos + 1, v_end = a.include_current_v ? n : pos;
+  const size_t stride = (size_t)a.KV * D;
+  const float* qh = a.q + (size_t)h * D;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  float m = -INFINITY;
+  for (int t = threadIdx.x; t < n; t += blockDim.x) {
+    const float* k = a.keys + (size_t)t * stride + (size_t)kvh * D;
+    float dot = 0.0f;
+    for (int d = 0; d < D; ++d) dot = fmaf(qh[d], k[d], dot);
+    float s = __fmul_rn(dot, a.scale);
+    sc[t] = s;
+    m = fmaxf(m, s);
+  }
+  m = warp_max(m);
+  if (lane == 0) red[warp] = m;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float t = red[0];
+    for (int i = 1; i < nw; ++i) t = fmaxf(t, red[i]);
+    bc = t;
+  }
+  __syncthreads();
+  m = bc;
+  float l = 0.0f;
+  for (int t = threadIdx.x; t < n; t += blockDim.x) {
+    float e = expf(sc[t] - m);
+    sc[t] = e;
+    l += e;
+  }
+  l = warp_sum(l);
+  __syncthreads();
+  if (lane == 0) red[warp] = l;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float t = 0.0f;
+    for (int i = 0; i < nw; ++i) t += red[i];
+    bc = t;
+  }
+  __syncthreads();
+  l = bc;
+  for (int d = threadIdx.x; d < D; d += blockDim.x) {
+    float acc = 0.0f;
+    for (int t = 0; t < v_end; ++t)
+      acc = fmaf(sc[t], a.values[(size_t)t * stride + (size_t)kvh * D + d], acc);
+    a.out[(size_t)h * D + d] = __fdiv_rn(acc, l);
+  }
+}
+
+bool attn_tiled_ok(int H, int KV, int D) {
+  return D % 4 == 0 && D <= 512 && H / KV <= 16 && attn_smem_bytes(H / KV, D) <= 200 * 1024;
+}
+
+size_t attn_smem_bytes(int G, int D) {
+  const int pitch = D + 4;
+  const int hstep = kAttnThreads / (D / 4);
+  const int region = std::max(4 * kAttnTile * pitch, hstep * G * D);
+  return (size_t)(region + G * D + G * kAttnTile + 3 * G) * sizeof(float);
+}
+
+int attn_splits(int KV, int sms, int max_seq) {
+  int tiles = (max_seq + kAttnTile - 1) / kAttnTile;
+  int want = (3 * sms + KV - 1) / KV;
+  int s = want < tiles ? want : tiles;
+  return s < 1 ? 1 : s;
+}
+
+void attn_check(int H, int KV, int D) {
+  if (H <= 0 || KV <= 0 || D <= 0) invalid("attention: head counts and head_dim must be positive");
+  if (H % KV != 0) invalid("attention: n_heads must be divisible by n_kv_heads");
+}
+
+void attn_check_tiled(int H, int KV, int D) {
+  attn_check(H, KV, D);
+  if (!attn_tiled_ok(H, KV, D))
+    invalid("decode step: head_dim must be a multiple of 4 (<= 512) with <= 16 query heads per "
+            "KV head");
+}
+
+void attn_launch(const AttnLaunch& l, cudaStream_t stream, bool pdl) {
+  AttnKArgs a;
+  a.q = l.q;
+  a.keys = l.keys;
+  a.values = l.values;
+  a.pos_dev = l.pos_dev;
+  a.pos_host = l.pos_host;
+  a.H = l.H;
+  a.KV = l.KV;
+  a.D = l.D;
+  a.nsplit = l.nsplit;
+  a.scale = l.scale;
+  a.include_current_v = l.include_current_v;
+  a.ws = l.ws;
+  a.counters = l.counters;
+  a.out = l.out;
+  int dev = 0;
+  MLB_CUDA(cudaGetDevice(&dev));
+  if (!attn_tiled_ok(l.H, l.KV, l.D)) {
+    const int pos = l.pos_host;
+    if (l.pos_dev) invalid("attention: the generic path takes a host position");
+    const size_t gsm = (size_t)(pos + 1) * sizeof(float);
+    if (gsm > 200 * 1024) invalid("attention: position too large for this head shape");
+    if (gsm > 48 * 1024)
+      MLB_CUDA(cudaFuncSetAttribute(attn_decode_generic_kernel,
+                                    cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gsm));
+    launch_pdl(attn_decode_generic_kernel, dim3(l.H), dim3(kAttnThreads), gsm, stream, pdl, a);
+    return;
+  }
+  const size_t smem = attn_smem_bytes(l.H / l.KV, l.D);
+  static size_t smem_set[64] = {};
+  if (dev < 64 && smem > 48 * 1024 && smem_set[dev] < smem) {
+    MLB_CUDA(cudaFuncSetAttribute(attn_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  (int)smem));
+    smem_set[dev] = smem;
+  }
+  launch_pdl(attn_decode_kernel, dim3(l.KV, l.nsplit), dim3(kAttnThreads), smem, stream, pdl, a);
+}
+
+size_t attn_ws_floats(int H, int KV, int D, int nsplit) {
+  return (size_t)KV * nsplit * (H / KV) * (D + 2);
+}
+
+}  // namespace mlb

@@ -1,0 +1,93 @@
+// runtime.cuh — model, context and decode step (host side).
+#pragma once
+
+#include <nccl.h>
+
+#include <map>
+#include <memory>
+#include <vector>
+
+#include "attention.cuh"
+#include "gemv.cuh"
+
+namespace mlb {
+
+// Device allocation that frees itself.
+struct DevBuf {
+  void* p = nullptr;
+  size_t bytes = 0;
+  DevBuf() = default;
+  explicit DevBuf(size_t n) { alloc(n); }
+  void alloc(size_t n);
+  void reset();
+  ~DevBuf() { reset(); }
+  DevBuf(const DevBuf&) = delete;
+  DevBuf& operator=(const DevBuf&) = delete;
+  DevBuf(DevBuf&& o) noexcept : p(o.p), bytes(o.bytes) { o.p = nullptr; o.bytes = 0; }
+  DevBuf& operator=(DevBuf&& o) noexcept {
+    if (this != &o) { reset(); p = o.p; bytes = o.bytes; o.p = nullptr; o.bytes = 0; }
+    return *this;
+  }
+  template <class T> T* as() const { return static_cast<T*>(p); }
+};
+
+struct RawTensor {  // one uploaded GGUF tensor shard on the device, before fusing
+  int qtype = 0, rows = 0, cols = 0;  // shard shape
+  size_t pitch = 0;
+  DevBuf buf;
+};
+
+struct LayerPlan {
+  DevBuf attn_norm, ffn_norm, bias;  // bias: fused local [q | k | v] or empty
+  QMatrix qkv, wo, gateup, down;
+  DevBuf qkv_buf, wo_buf, gateup_buf, down_buf;
+  int qkv_k_off = 0, qkv_v_off = 0;
+};
+
+struct ModelImpl {
+  mlb_config cfg{};
+  int device = 0;
+  int tp_rank = 0, tp_size = 1;
+  ncclComm_t comm = nullptr;
+  // this rank's shard
+  int q_heads = 0, kv_heads = 0, q_head0 = 0, kv_head0 = 0;
+  int ffn_rows = 0, ffn_row0 = 0;     // hidden rows (block aligned)
+  int vocab_rows = 0, vocab_row0 = 0, vocab_pad = 0;
+  bool neox = false;
+  bool finalized = false;
+  // weights
+  DevBuf embedding, final_norm;
+  QMatrix lm_head;
+  DevBuf lm_head_buf;
+  std::vector<LayerPlan> layers;
+  DevBuf rope;  // [max_seq][D/2] float2
+  // pending uploads (kind, layer) -> shard on device
+  std::map<std::pair<int, int>, RawTensor> pending;
+  cudaStream_t stream = nullptr;
+  size_t resident_bytes() const;
+  size_t step_weight_bytes() const;
+};
+
+struct ContextImpl {
+  ModelImpl* m = nullptr;
+  int attention_mode = MLB_ATTN_CPU_COMPAT;
+  cudaStream_t stream = nullptr;
+  DevBuf keys, values;        // [L][S][KV_local][D]
+  DevBuf xa, xb, y, q, attn, hidden, logits_local, logits;
+  DevBuf gemv_ws, gemv_cnt, attn_ws, attn_cnt, status;
+  DevBuf scalars;             // int: token, pos, step, next token ; then tokens[max_seq]
+  int* h_scalars = nullptr;   // pinned: token, pos
+  float* h_logits = nullptr;  // pinned
+  int* h_tokens = nullptr;    // pinned
+  int attn_splits = 1;
+  GemvWorkspace ws;
+  cudaGraph_t graph = nullptr;
+  cudaGraphExec_t exec = nullptr;
+  int kernels_per_step = 0;
+  void build_graph();
+  void record_step(cudaStream_t s, bool pdl);
+  void check_status();
+  ~ContextImpl();
+};
+
+}  // namespace mlb
