@@ -41,7 +41,11 @@ def parse_args():
     p.add_argument("--steps", type=int, default=64)
     p.add_argument("--warmup", type=int, default=8)
     p.add_argument("--impl", choices=["b200", "reference"], default="b200")
-    p.add_argument("--workload", choices=sorted(C.WORKLOADS), default="llama2-7b-q4_0")
+    p.add_argument("--workload", choices=sorted(C.WORKLOADS) + ["gemv-sweep"],
+                   default="llama2-7b-q4_0")
+    p.add_argument("--sweep-n", type=str, default="4096,11008,14336")
+    p.add_argument("--sweep-m", type=str, default="1,4,16,64")
+    p.add_argument("--sweep-q", type=str, default="q4_0,q4_1,q8_0")
     p.add_argument("--ctx", type=int, default=512, help="KV positions filled before timing")
     p.add_argument("--no-cpu-baseline", action="store_true")
     return p.parse_args()
@@ -195,6 +199,28 @@ def run_reference(args, cfg, qtype, bias, world, rank):
 
 # ---------------------------------------------------------------- GPU arm
 
+def time_launches(torch, launch, n):
+    """Average device time of one launch: n launches captured in a CUDA graph
+    (no host launch latency between them), replayed and timed with events."""
+    launch(0)  # first call outside capture: one-time kernel attributes
+    torch.cuda.synchronize()
+    s = torch.cuda.Stream()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(s):
+        with torch.cuda.graph(g, stream=s):
+            for i in range(n):
+                launch(i)
+    g.replay()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    cur = torch.cuda.current_stream()
+    a.record(cur)
+    g.replay()
+    b.record(cur)
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) / n
+
+
 def gemv_roofline(torch, mlb, cfg, qtype, world, peak):
     """Live per-launch timing of the dominant kernel: the fused gate/up GEMV of
     this rank's shard, rotating over copies that together exceed L2."""
@@ -205,19 +231,7 @@ def gemv_roofline(torch, mlb, cfg, qtype, world, peak):
     mats = [mlb.QMatrix.synthesize(qtype, n, k, SEED, 900 + i, raw=False) for i in range(copies)]
     x = torch.randn(1, k, device="cuda")
     y = torch.empty(1, n, device="cuda")
-    stream = torch.cuda.current_stream()
-    for m in mats:
-        m.gemv(x, y)
-    torch.cuda.synchronize()
-    evs = []
-    for i in range(8 * copies):
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a.record(stream)
-        mats[i % copies].gemv(x, y)
-        b.record(stream)
-        evs.append((a, b))
-    torch.cuda.synchronize()
-    ms = statistics.mean(a.elapsed_time(b) for a, b in evs)
+    ms = time_launches(torch, lambda i: mats[i % copies].gemv(x, y), 8 * copies)
     achieved = nbytes / (ms * 1e-3) / 1e9
     return {"bound": "hbm", "achieved": achieved, "peak": peak[0], "unit": "GB/s",
             "frac": achieved / peak[0], "traffic": GEMV_TRAFFIC_BYTES,
@@ -280,10 +294,12 @@ def run_gpu(args, cfg, qtype, bias, rank, world, local):
     with Clocks([local]) as clk:
         barrier()
         ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.profiler.start()
         ev0.record(stream)
         toks = ctx.decode_greedy(tok, pos, args.steps)
         ev1.record(stream)
         torch.cuda.synchronize()
+        torch.cuda.profiler.stop()
         barrier()
     ms = max_over_ranks(ev0.elapsed_time(ev1))
     ctx_end = pos + args.steps
@@ -369,8 +385,82 @@ def run_gpu(args, cfg, qtype, bias, rank, world, local):
         dist.destroy_process_group()
 
 
+def run_gemv_sweep(args):
+    """Standalone quantised GEMV/GEMM sweep: K = 4096, N x M over the formats,
+    raw random GGUF blocks (fp16 scale |N(0,1)|*0.01, uniform codes), x ~ N(0,1).
+    Each launch reads a different copy of the weights (copies > 2x L2)."""
+    import torch
+
+    import mini_llama_b200 as mlb
+
+    peak = measured_peaks()
+    qnames = {v: k for k, v in C.QTYPE_NAMES.items()}
+    k = 4096
+    rows = []
+    with Clocks([0]) as clk:
+        for qn in args.sweep_q.split(","):
+            qtype = qnames[qn]
+            for n in [int(v) for v in args.sweep_n.split(",")]:
+                wbytes = n * (k // 32) * C.BLOCK_BYTES[qtype]
+                copies = max(2, int(np.ceil(260e6 / wbytes)))
+                mats = [mlb.QMatrix.synthesize(qtype, n, k, SEED, 7000 + i, raw=True)
+                        for i in range(copies)]
+                for m in [int(v) for v in args.sweep_m.split(",")]:
+                    x = torch.randn(m, k, device="cuda")
+                    y = torch.empty(m, n, device="cuda")
+                    for i in range(args.warmup):
+                        mats[i % copies].gemv(x, y)
+                    torch.cuda.synchronize()
+                    torch.cuda.profiler.start()
+                    us = 1e3 * time_launches(torch, lambda i: mats[i % copies].gemv(x, y),
+                                             args.steps)
+                    torch.cuda.profiler.stop()
+                    nbytes = wbytes + m * k * 4 + m * n * 4
+                    rows.append({"q": qn, "n": n, "k": k, "m": m, "us": us,
+                                 "gbs": nbytes / (us * 1e-6) / 1e9,
+                                 "frac": nbytes / (us * 1e-6) / 1e9 / peak[0]})
+                del mats
+    head = next((r for r in rows if r["q"] == "q4_0" and r["m"] == 1 and r["n"] == 11008), rows[0])
+    cpu = None
+    if not args.no_cpu_baseline:
+        import oracle
+
+        if oracle.ref_available():
+            r = oracle.ref()
+            r.set_threads(cpu_threads())
+            kind, lib, threads = "reference", r, r.threads()
+        else:
+            kind, lib, threads = "port", oracle.port(), 1
+        qtype = qnames[head["q"]]
+        w = C.synth_tensor(SEED, C.W_WQ, 0, qtype, head["n"], k, threads=cpu_threads())
+        x = np.random.default_rng(0).normal(0, 1, k).astype(np.float32)
+        t0 = time.perf_counter()
+        reps = 0
+        while time.perf_counter() - t0 < 10.0:
+            lib.linear(qtype, x, w, head["n"])
+            reps += 1
+        secs = (time.perf_counter() - t0) / reps
+        cpu = {"value": (w.nbytes + k * 4 + head["n"] * 4) / secs / 1e9, "unit": "GB/s",
+               "cores": threads, "kind": kind,
+               "sample": f"{reps} LinearQ40 calls, {head['n']}x{k} M=1 (~10 s)"}
+    print(json.dumps({
+        "metric": "quant GEMV achieved HBM GB/s", "value": head["gbs"], "unit": "GB/s",
+        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": head["us"] / 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": head["q"] + "/fp32", "data": "synthetic raw GGUF blocks",
+        "config": {"workload": "gemv-sweep", "headline": f"{head['q']} {head['n']}x{k} M=1",
+                   "l2": "rotating weight copies > 2x L2"},
+        "roofline": {"bound": "hbm", "achieved": head["gbs"], "peak": peak[0], "unit": "GB/s",
+                     "frac": head["frac"], "traffic": None},
+        "sweep": rows, "cpu_baseline": cpu, "clocks": clk.summary(),
+        "gpu_launches": args.steps * len(rows)}))
+
+
 def main():
     args = parse_args()
+    if args.workload == "gemv-sweep":
+        run_gemv_sweep(args)
+        return
     rank, world, local = dist_env()
     if world != args.gpus and world > 1:
         raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE {world}")

@@ -60,10 +60,12 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnKAr
   const int region = max(4 * kAttnTile * pitch, hstep_ * G * D);  // K/V tiles, later group sums
   float* qs = sm + region;                     // [G][D]
   float* ps = qs + G * D;                      // [G][tile] probabilities
-  float* st = ps + G * kAttnTile;              // [G] m, [G] l, [G] alpha
+  float* part = ps + G * kAttnTile;            // [4 warps][G][tile] partial scores
+  float* st = part + 4 * G * kAttnTile;        // [G] m, [G] l, [G] alpha
   float* mrun = st, *lrun = st + G, *alpha = st + 2 * G;
   __shared__ int last_flag;
 
+  pdl_launch_dependents();  // dependents still wait for this grid to complete
   pdl_wait();
   const int pos = a.pos_dev ? *a.pos_dev : a.pos_host;
   const int n = pos + 1;
@@ -124,19 +126,31 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnKAr
       cp_async_wait<0>();
     }
     __syncthreads();
-    // scores and per-head tile statistics
-    const float* krow = kt + (buf * kAttnTile + lane) * pitch;
-    for (int h = warp; h < G; h += 4) {
-      float dot = 0.0f;
-      const float* qh = qs + h * D;
-      for (int d = 0; d < D; d += 4) {
-        float4 kv = *reinterpret_cast<const float4*>(krow + d);
-        float4 qv = *reinterpret_cast<const float4*>(qh + d);
-        dot = fmaf(qv.x, kv.x, dot);
-        dot = fmaf(qv.y, kv.y, dot);
-        dot = fmaf(qv.z, kv.z, dot);
-        dot = fmaf(qv.w, kv.w, dot);
+    // scores: warp w takes a quarter of head_dim for every position (lane) and
+    // every head of the group; the four partial dots are summed in warp order
+    {
+      const int nvec = D >> 2;
+      const int v0 = warp * nvec / 4, v1 = (warp + 1) * nvec / 4;
+      const float* krow = kt + (buf * kAttnTile + lane) * pitch;
+      for (int h = 0; h < G; ++h) {
+        const float* qh = qs + h * D;
+        float dot = 0.0f;
+        for (int vi = v0; vi < v1; ++vi) {
+          const float4 kv = *reinterpret_cast<const float4*>(krow + vi * 4);
+          const float4 qv = *reinterpret_cast<const float4*>(qh + vi * 4);
+          dot = fmaf(qv.x, kv.x, dot);
+          dot = fmaf(qv.y, kv.y, dot);
+          dot = fmaf(qv.z, kv.z, dot);
+          dot = fmaf(qv.w, kv.w, dot);
+        }
+        part[(warp * G + h) * kAttnTile + lane] = dot;
       }
+    }
+    __syncthreads();
+    // per-head tile statistics and probabilities (warp per head)
+    for (int h = warp; h < G; h += 4) {
+      const float dot = ((part[(0 * G + h) * kAttnTile + lane] + part[(1 * G + h) * kAttnTile + lane]) +
+                         part[(2 * G + h) * kAttnTile + lane]) + part[(3 * G + h) * kAttnTile + lane];
       const int t = t0 + lane;
       float s = t < t_end ? __fmul_rn(dot, a.scale) : -INFINITY;
       float tmax = warp_max(s);
@@ -181,7 +195,6 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnKAr
     }
     __syncthreads();
   }
-  pdl_launch_dependents();
 
   // sum the position groups (fixed order) through shared memory, then write
   // this slice's (m, l, O)
@@ -210,22 +223,45 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnKAr
   __syncthreads();
   if (!last_flag) return;
   __threadfence();
-  // combine the slices of this KV head in slice order
-  for (int i = threadIdx.x; i < G * D; i += kAttnThreads) {
-    int h = i / D, d = i - h * D;
+  // combine the slices of this KV head in slice order: per (head, slice) weight
+  // e^(m_s - m) / l into shared memory, then every output element is one pass
+  // of independent loads
+  float* wsl = kt;  // [G][nsplit], reuses the K tiles (no cp.async in flight)
+  for (int h = warp; h < G; h += 4) {
     float m = -INFINITY;
-    for (int s = 0; s < a.nsplit; ++s)
+    for (int s = lane; s < a.nsplit; s += 32)
       m = fmaxf(m, __ldcg(a.ws + (((size_t)kvh * a.nsplit + s) * G + h) * rec));
-    float l = 0.0f, acc = 0.0f;
-    for (int s = 0; s < a.nsplit; ++s) {
+    m = warp_max(m);
+    float l = 0.0f;
+    for (int s = lane; s < a.nsplit; s += 32) {
       const float* r = a.ws + (((size_t)kvh * a.nsplit + s) * G + h) * rec;
-      float ms = __ldcg(r);
-      if (ms == -INFINITY) continue;
-      float e = expf(ms - m);
+      const float ms = __ldcg(r);
+      const float e = ms == -INFINITY ? 0.0f : expf(ms - m);
+      wsl[h * a.nsplit + s] = e;
       l = fmaf(__ldcg(r + 1), e, l);
-      acc = fmaf(__ldcg(r + 2 + d), e, acc);
     }
-    a.out[(size_t)(kvh * G + h) * D + d] = __fdiv_rn(acc, l);
+    l = warp_sum(l);
+    const float inv = 1.0f / l;
+    __syncwarp();
+    for (int s = lane; s < a.nsplit; s += 32) wsl[h * a.nsplit + s] *= inv;
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < G * D; i += kAttnThreads) {
+    const int h = i / D, d = i - h * D;
+    const float* base = a.ws + ((size_t)kvh * a.nsplit * G + h) * rec + 2 + d;
+    const size_t step = (size_t)G * rec;
+    float acc = 0.0f;
+    int s = 0;
+    for (; s + 4 <= a.nsplit; s += 4) {
+      const float o0 = __ldcg(base + (s + 0) * step), o1 = __ldcg(base + (s + 1) * step);
+      const float o2 = __ldcg(base + (s + 2) * step), o3 = __ldcg(base + (s + 3) * step);
+      acc = fmaf(o0, wsl[h * a.nsplit + s], acc);
+      acc = fmaf(o1, wsl[h * a.nsplit + s + 1], acc);
+      acc = fmaf(o2, wsl[h * a.nsplit + s + 2], acc);
+      acc = fmaf(o3, wsl[h * a.nsplit + s + 3], acc);
+    }
+    for (; s < a.nsplit; ++s) acc = fmaf(__ldcg(base + s * step), wsl[h * a.nsplit + s], acc);
+    a.out[(size_t)(kvh * G + h) * D + d] = acc;
   }
   if (threadIdx.x == 0) a.counters[kvh] = 0;
 }
@@ -295,7 +331,7 @@ size_t attn_smem_bytes(int G, int D) {
   const int pitch = D + 4;
   const int hstep = kAttnThreads / (D / 4);
   const int region = std::max(4 * kAttnTile * pitch, hstep * G * D);
-  return (size_t)(region + G * D + G * kAttnTile + 3 * G) * sizeof(float);
+  return (size_t)(region + G * D + 5 * G * kAttnTile + 3 * G) * sizeof(float);
 }
 
 int attn_splits(int KV, int sms, int max_seq) {
@@ -345,6 +381,12 @@ void attn_launch(const AttnLaunch& l, cudaStream_t stream, bool pdl) {
                                     cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gsm));
     launch_pdl(attn_decode_generic_kernel, dim3(l.H), dim3(kAttnThreads), gsm, stream, pdl, a);
     return;
+  }
+  {
+    // the combine keeps G x nsplit slice weights in the K/V tile region
+    const int G = l.H / l.KV, pitch = l.D + 4, hstep = kAttnThreads / (l.D / 4);
+    const int region = std::max(4 * kAttnTile * pitch, hstep * G * l.D);
+    a.nsplit = std::max(1, std::min(l.nsplit, region / G));
   }
   const size_t smem = attn_smem_bytes(l.H / l.KV, l.D);
   static size_t smem_set[64] = {};

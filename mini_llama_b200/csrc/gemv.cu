@@ -49,9 +49,14 @@ void qmatrix_geometry(QMatrix& m, int qtype, int n, int k, int max_batch) {
   if (qtype != MLB_Q8_0 && qtype != MLB_Q4_0 && qtype != MLB_Q4_1)
     invalid("qmatrix: unsupported quant type " + std::to_string(qtype));
   m.nchunks = (k + kChunkK - 1) / kChunkK;
-  int mb = max_batch < 1 ? 1 : (max_batch > kMaxBatch ? kMaxBatch : max_batch);
-  int gc = 16 / (mb >= 3 ? 4 : mb);
-  m.gc = std::min(gc, m.nchunks);
+  // Chunk group: all of K in one group up to 64 chunks (K <= 16384) for one
+  // batch row (the staged activations then take at most 72 KB of shared
+  // memory); wider batches stage proportionally fewer chunks, and Q8_0 (whose
+  // weight ring needs twice the room) half as many again.
+  const int mb = max_batch < 1 ? 1 : (max_batch > kMaxBatch ? kMaxBatch : max_batch);
+  const int mbucket = mb >= 3 ? 4 : mb;
+  const int whole = mbucket == 1 ? 64 : (qtype == MLB_Q8_0 ? 32 : 64) / mbucket;
+  m.gc = m.nchunks <= whole ? m.nchunks : whole / 2;
   m.ngroups = (m.nchunks + m.gc - 1) / m.gc;
   m.nsb = (long long)m.ntiles * m.nchunks;
   m.bytes = (size_t)m.nsb * sb_bytes(qtype);
@@ -238,6 +243,7 @@ __device__ void epilogue_row(const EpiParams& p, int tile, int row, int r, const
 struct GemvKArgs {
   const uint8_t* w;
   int sbb;
+  int stages;  // ring depth per warp (2..4)
   int ntiles, nchunks, gc, ngroups;
   long long nsb;
   int k;
@@ -256,7 +262,7 @@ struct SbPos {
   int grp, t, cc, geff;
 };
 
-__device__ __forceinline__ SbPos sb_decode(long long u, int ntiles, int nchunks, int gc) {
+__host__ __device__ inline SbPos sb_decode(long long u, int ntiles, int nchunks, int gc) {
   SbPos s;
   long long per = (long long)ntiles * gc;
   s.grp = (int)(u / per);
@@ -267,24 +273,24 @@ __device__ __forceinline__ SbPos sb_decode(long long u, int ntiles, int nchunks,
   return s;
 }
 
-__device__ __forceinline__ long long warp_start(long long w, long long nsb, long long W) {
-  return nsb * w / W;
+// CTA c of G owns super-blocks [cta_start(c), cta_start(c + 1)).
+__host__ __device__ inline long long cta_start(long long c, long long nsb, long long G) {
+  return nsb * c / G;
 }
 
-// Calls f(start_chunk) for every segment tile t is split into by the static
-// partition (chunk-group runs cut at warp-range boundaries), in chunk order.
-// Works for any warp count, including warps with empty ranges.
+// Calls f(start_chunk) for every segment tile t is split into: its runs in each
+// chunk group, cut at CTA-range boundaries; in chunk order.
 template <class F>
 __device__ __forceinline__ int for_each_segment(int t, int ntiles, int nchunks, int gc,
-                                                int ngroups, long long nsb, long long W, F f) {
+                                                int ngroups, long long nsb, long long G, F f) {
   int n = 0;
   for (int gr = 0; gr < ngroups; ++gr) {
     const int geff = min(gc, nchunks - gr * gc);
     const long long u0 = (long long)gr * ntiles * gc + (long long)t * geff, end = u0 + geff;
     long long p = u0;
     while (p < end) {
-      const long long w = ((p + 1) * W + nsb - 1) / nsb - 1;  // warp whose range holds p
-      const long long e = warp_start(w + 1, nsb, W);
+      const long long c = ((p + 1) * G + nsb - 1) / nsb - 1;  // CTA whose range holds p
+      const long long e = cta_start(c + 1, nsb, G);
       f(gr * gc + (int)(p - u0));
       ++n;
       p = e < end ? e : end;
@@ -294,228 +300,237 @@ __device__ __forceinline__ int for_each_segment(int t, int ntiles, int nchunks, 
 }
 
 constexpr int kFragLaneStride = 36;  // u32 per lane per chunk (32 + 4 pad: no bank conflicts)
+constexpr int kMaxStages = 4;
+constexpr int kSegList = 32;         // segment starts gathered per pass of a fix-up
 
 template <int M>
 __host__ __device__ constexpr int frag_chunk_u32() {
   return 8 * M * kFragLaneStride;
 }
-
-template <int QT, int M>
-__host__ __device__ constexpr int red_floats() {
-  return kGemvWarps * 16 * M;
+// (group, tile) runs one CTA range may touch; the launcher sizes the grid so
+// that no CTA exceeds it.
+template <int M>
+__host__ __device__ constexpr int max_cta_runs() {
+  return M == 1 ? 8 : 4;
 }
 
+struct GemvSmem {
+  size_t ring, bars, frag, bsum, slots, red, misc, total;
+};
+
 template <int QT, int M>
-size_t gemv_smem_bytes(int gc, int sbb) {
-  size_t ring = (size_t)kGemvWarps * kGemvStages * sbb;
-  size_t bars = (size_t)kGemvWarps * kGemvStages * 8;
-  size_t frag = (size_t)2 * gc * frag_chunk_u32<M>() * 4;
-  size_t bsum = QT == MLB_Q4_1 ? (size_t)2 * gc * 8 * M * 4 : 0;
-  size_t red = (size_t)red_floats<QT, M>() * 4;
-  return ring + bars + frag + bsum + red + 64;
+__host__ __device__ GemvSmem gemv_smem_layout(int gc, int nslots, int sbb, int stages) {
+  GemvSmem s;
+  s.ring = (size_t)kGemvWarps * stages * sbb;
+  s.bars = (size_t)kGemvWarps * kMaxStages * 8;
+  s.frag = (size_t)nslots * gc * frag_chunk_u32<M>() * 4;
+  s.bsum = QT == MLB_Q4_1 ? (size_t)nslots * gc * 8 * M * 4 : 0;
+  s.slots = (size_t)max_cta_runs<M>() * kGemvWarps * 16 * M * 4;
+  s.red = (size_t)kGemvWarps * (16 * M + kSegList) * 4;
+  s.misc = 256 + (size_t)(max_cta_runs<M>() + 1) * 8 + (size_t)max_cta_runs<M>() * 12;
+  s.total = s.ring + s.bars + s.frag + s.bsum + s.slots + s.red + s.misc;
+  return s;
 }
 
 template <int QT, int M, bool NORM>
 __global__ void __launch_bounds__(kGemvWarps * 32, 1) gemv_sb_kernel(const GemvKArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
+  constexpr int R = max_cta_runs<M>();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int sbb = a.sbb;
+  const int sbb = a.sbb, S = a.stages;
+  const int nslots = a.ngroups > 1 ? 2 : 1;
+  const GemvSmem L = gemv_smem_layout<QT, M>(a.gc, nslots, sbb, S);
   uint8_t* ring = smem;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(ring + (size_t)kGemvWarps * kGemvStages * sbb);
-  uint32_t* frag = reinterpret_cast<uint32_t*>(bars + kGemvWarps * kGemvStages);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L.ring);
+  uint32_t* frag = reinterpret_cast<uint32_t*>(smem + L.ring + L.bars);
+  float* bsum = reinterpret_cast<float*>(smem + L.ring + L.bars + L.frag);
+  float* slots = reinterpret_cast<float*>(smem + L.ring + L.bars + L.frag + L.bsum);
+  float* red = slots + L.slots / 4;
+  uint8_t* misc = reinterpret_cast<uint8_t*>(red + L.red / 4);
+  float* inv_rms = reinterpret_cast<float*>(misc);            // [M]
+  float* part = inv_rms + 4;                                   // [kGemvWarps]
+  int* nruns_s = reinterpret_cast<int*>(part + kGemvWarps);    // [1]
+  long long* run_u0 = reinterpret_cast<long long*>(misc + 256);  // [R + 1]
+  int* run_t = reinterpret_cast<int*>(run_u0 + R + 1);         // [R]
+  int* run_grp = run_t + R;
+  int* run_cc0 = run_grp + R;
   const int slot_u32 = a.gc * frag_chunk_u32<M>();
-  float* bsum = reinterpret_cast<float*>(frag + 2 * slot_u32);
   const int bsum_slot = a.gc * 8 * M;
-  float* red = bsum + (QT == MLB_Q4_1 ? 2 * bsum_slot : 0);
-  float* misc = red + red_floats<QT, M>();  // inv_rms[M], partial sums
 
-  const long long W = (long long)gridDim.x * kGemvWarps;
-  const long long wg = (long long)blockIdx.x * kGemvWarps + warp;
-  const long long ub = warp_start(wg, a.nsb, W), ue = warp_start(wg + 1, a.nsb, W);
-  const long long cb = warp_start((long long)blockIdx.x * kGemvWarps, a.nsb, W);
-  const long long ce = warp_start((long long)(blockIdx.x + 1) * kGemvWarps, a.nsb, W);
-  uint64_t* mybars = bars + warp * kGemvStages;
-  uint8_t* myring = ring + (size_t)warp * kGemvStages * sbb;
+  const long long G = gridDim.x;
+  const long long cb = cta_start(blockIdx.x, a.nsb, G), ce = cta_start(blockIdx.x + 1, a.nsb, G);
+  uint64_t* mybars = bars + warp * kMaxStages;
+  uint8_t* myring = ring + (size_t)warp * S * sbb;
 
-  // 1. Barriers, then start streaming weights (independent of the previous kernel).
+  // 1. Barriers, then start streaming weights (independent of the previous
+  //    kernel): warp w takes super-blocks cb + w, cb + w + 16, ...
   if (lane == 0) {
-    for (int s = 0; s < kGemvStages; ++s) mbar_init(&mybars[s], 1);
+    for (int s = 0; s < S; ++s) mbar_init(&mybars[s], 1);
     fence_mbar_init();
     fence_proxy_async_smem();
   }
   __syncwarp();
   if (lane == 0) {
-    for (int s = 0; s < kGemvStages && ub + s < ue; ++s) {
+    for (int s = 0; s < S; ++s) {
+      const long long u = cb + warp + (long long)s * kGemvWarps;
+      if (u >= ce) break;
       mbar_arrive_expect_tx(&mybars[s], sbb);
-      bulk_g2s(myring + (size_t)s * sbb, a.w + (size_t)(ub + s) * sbb, sbb, &mybars[s]);
+      bulk_g2s(myring + (size_t)s * sbb, a.w + (size_t)u * sbb, sbb, &mybars[s]);
     }
   }
-
+  // The run table of this CTA range (no dependence on the previous kernel).
+  if (threadIdx.x == 0) {
+    long long u = cb;
+    int r = 0;
+    while (u < ce && r < R) {
+      const SbPos sp = sb_decode(u, a.ntiles, a.nchunks, a.gc);
+      const long long len = min((long long)(sp.geff - sp.cc), ce - u);
+      run_u0[r] = u;
+      run_t[r] = sp.t;
+      run_grp[r] = sp.grp;
+      run_cc0[r] = sp.cc;
+      u += len;
+      ++r;
+    }
+    run_u0[r] = u;
+    *nruns_s = (u < ce) ? -1 : r;  // -1: more runs than the launcher allowed
+  }
+  // The next kernel may be scheduled as soon as an SM has room; it waits for
+  // this grid to complete before reading anything this grid writes.
+  pdl_launch_dependents();
   // 2. Inputs of the previous kernel are visible after this.
   pdl_wait();
 
   const int rows = a.rows;
   if (NORM) {
     // inv_rms[r] = 1 / sqrt(sum(x^2)/K + eps), src/ops.cc:55-61 (tree order).
-    float* part = misc + M;
     for (int r = 0; r < rows; ++r) {
       float ss = 0.0f;
       const float* xr = a.x + (size_t)r * a.ldx;
-      for (int i = threadIdx.x; i < a.k; i += blockDim.x) ss = fmaf(xr[i], xr[i], ss);
+      if ((a.k & 3) == 0 && (((uintptr_t)xr) & 15) == 0) {
+        const float4* x4 = reinterpret_cast<const float4*>(xr);
+        for (int i = threadIdx.x; i < (a.k >> 2); i += blockDim.x) {
+          const float4 v = x4[i];
+          ss = fmaf(v.x, v.x, ss);
+          ss = fmaf(v.y, v.y, ss);
+          ss = fmaf(v.z, v.z, ss);
+          ss = fmaf(v.w, v.w, ss);
+        }
+      } else {
+        for (int i = threadIdx.x; i < a.k; i += blockDim.x) ss = fmaf(xr[i], xr[i], ss);
+      }
       ss = warp_sum(ss);
       if (lane == 0) part[warp] = ss;
       __syncthreads();
       if (threadIdx.x == 0) {
         float t = 0.0f;
-        for (int w = 0; w < kGemvWarps; ++w) t += part[w];
+        for (int w = 0; w < kGemvWarps; ++w) t += part[w];  // fixed order
         t = __fdiv_rn(t, (float)a.k);
-        misc[r] = __fdiv_rn(1.0f, sqrtf(__fadd_rn(t, a.eps)));
+        inv_rms[r] = __fdiv_rn(1.0f, sqrtf(__fadd_rn(t, a.eps)));
       }
       __syncthreads();
     }
+  } else {
+    __syncthreads();  // run table visible
   }
-
-  // 3. Stage x (normalised if fused) for the <= 2 chunk groups this CTA touches,
-  //    in mma B-fragment order, split into fp16 hi + lo.
-  int g0 = 0, g1 = -1;
-  if (ce > cb) {
-    g0 = sb_decode(cb, a.ntiles, a.nchunks, a.gc).grp;
-    g1 = sb_decode(ce - 1, a.ntiles, a.nchunks, a.gc).grp;
-  }
-  if (g1 - g0 > 1) {  // host guarantees <= 2 groups per CTA
+  const int nruns = *nruns_s;
+  if (nruns < 0) {
     if (threadIdx.x == 0 && a.status) {
       atomicExch(&a.status->code, MLB_ERR_INVALID);
       atomicExch(&a.status->where, 1);
     }
     return;
   }
+  const int g0 = nruns > 0 ? run_grp[0] : 0;
+  const int g1 = nruns > 0 ? run_grp[nruns - 1] : -1;
+
+  // 3. Stage x (normalised if fused) for the <= 2 chunk groups this CTA touches,
+  //    in mma B-fragment order, split into fp16 hi + lo; zero the run slots.
+  for (int i = threadIdx.x; i < R * kGemvWarps * 16 * M; i += blockDim.x) slots[i] = 0.0f;
   for (int j = 0; j <= g1 - g0; ++j) {
     const int grp = g0 + j;
     const int geff = min(a.gc, a.nchunks - grp * a.gc);
     const int kbase = grp * a.gc * kChunkK;
     uint32_t* fs = frag + j * slot_u32;
-    const int pairs = geff * 128 * M;
-    for (int idx = threadIdx.x; idx < pairs; idx += blockDim.x) {
-      int r = idx / (geff * 128);
-      int rem = idx - r * geff * 128;
-      int cc = rem >> 7, pe = rem & 127;
-      int kk = pe * 2;
-      int s = kk >> 4, wv = kk & 15;
-      int reg = wv >= 8, cl = (wv & 7) >> 1;
-      int k = kbase + cc * kChunkK + kk;
-      float x0 = 0.0f, x1 = 0.0f;
+    float* bs = bsum + j * bsum_slot;
+    // one thread per 4 consecutive inputs (2 B-fragment pairs); 8 consecutive
+    // threads cover one 32-input block, so Q4_1 block sums reduce by shuffles
+    const int quads = geff * 64 * M;
+    for (int idx = threadIdx.x; idx < quads; idx += blockDim.x) {
+      const int r = idx / (geff * 64);
+      const int rem = idx - r * geff * 64;
+      const int cc = rem >> 6, q4 = rem & 63;
+      const int k = kbase + cc * kChunkK + q4 * 4;
+      float v[4] = {0.0f, 0.0f, 0.0f, 0.0f};
       if (r < rows) {
         const float* xr = a.x + (size_t)r * a.ldx;
-        if (k < a.k) x0 = xr[k];
-        if (k + 1 < a.k) x1 = xr[k + 1];
+        if (k + 3 < a.k && ((((uintptr_t)(xr + k)) & 15) == 0)) {
+          const float4 t = *reinterpret_cast<const float4*>(xr + k);
+          v[0] = t.x; v[1] = t.y; v[2] = t.z; v[3] = t.w;
+        } else {
+          for (int e = 0; e < 4; ++e)
+            if (k + e < a.k) v[e] = xr[k + e];
+        }
         if (NORM) {
-          float sc = misc[r];
-          if (k < a.k) x0 = __fmul_rn(__fmul_rn(x0, sc), a.norm_w[k]);
-          if (k + 1 < a.k) x1 = __fmul_rn(__fmul_rn(x1, sc), a.norm_w[k + 1]);
+          const float sc = inv_rms[r];
+          for (int e = 0; e < 4; ++e)
+            if (k + e < a.k) v[e] = __fmul_rn(__fmul_rn(v[e], sc), a.norm_w[k + e]);
         }
       }
-      __half h0 = __float2half_rn(x0), h1 = __float2half_rn(x1);
-      __half l0 = __float2half_rn(x0 - __half2float(h0));
-      __half l1 = __float2half_rn(x1 - __half2float(h1));
       uint32_t* base = fs + cc * frag_chunk_u32<M>();
-      int lane_hi = 4 * (2 * r) + cl, lane_lo = lane_hi + 4;
-      base[lane_hi * kFragLaneStride + s * 2 + reg] = h2_as_u32(__halves2half2(h0, h1));
-      base[lane_lo * kFragLaneStride + s * 2 + reg] = h2_as_u32(__halves2half2(l0, l1));
-    }
-    if (QT == MLB_Q4_1) {
-      float* bs = bsum + j * bsum_slot;
-      for (int idx = threadIdx.x; idx < geff * 8 * M; idx += blockDim.x) {
-        int r = idx % M, b = (idx / M) & 7, cc = idx / (8 * M);
-        float s = 0.0f;
-        int k0 = kbase + cc * kChunkK + b * 32;
-        if (r < rows) {
-          const float* xr = a.x + (size_t)r * a.ldx;
-          for (int i = 0; i < 32 && k0 + i < a.k; ++i) {
-            float xv = xr[k0 + i];
-            if (NORM) xv = __fmul_rn(__fmul_rn(xv, misc[r]), a.norm_w[k0 + i]);
-            s += xv;
-          }
-        }
-        bs[(cc * 8 + b) * M + r] = s;
+#pragma unroll
+      for (int p2 = 0; p2 < 2; ++p2) {
+        const int kk = q4 * 4 + p2 * 2;  // even input index inside the chunk
+        const int st = kk >> 4, wv = kk & 15;
+        const int reg = wv >= 8, cl = (wv & 7) >> 1;
+        const __half h0 = __float2half_rn(v[2 * p2]), h1 = __float2half_rn(v[2 * p2 + 1]);
+        const __half l0 = __float2half_rn(v[2 * p2] - __half2float(h0));
+        const __half l1 = __float2half_rn(v[2 * p2 + 1] - __half2float(h1));
+        const int lane_hi = 4 * (2 * r) + cl, lane_lo = lane_hi + 4;
+        base[lane_hi * kFragLaneStride + st * 2 + reg] = h2_as_u32(__halves2half2(h0, h1));
+        base[lane_lo * kFragLaneStride + st * 2 + reg] = h2_as_u32(__halves2half2(l0, l1));
+      }
+      if (QT == MLB_Q4_1) {
+        float s4 = (v[0] + v[1]) + (v[2] + v[3]);
+        s4 += __shfl_xor_sync(0xffffffffu, s4, 1);
+        s4 += __shfl_xor_sync(0xffffffffu, s4, 2);
+        s4 += __shfl_xor_sync(0xffffffffu, s4, 4);
+        if ((q4 & 7) == 0) bs[(cc * 8 + (q4 >> 3)) * M + r] = s4;
       }
     }
   }
   __syncthreads();
-  // Let the next kernel launch and begin its own weight prefetch.
-  pdl_launch_dependents();
 
-  // 4. Stream this warp's super-blocks.
+  // 4. Stream this warp's super-blocks, accumulating per run.
   const int g = lane >> 2, cl = lane & 3;
   const bool bl = lane < 8 * M;  // lanes carrying B-fragment columns
-  float* myred = red + warp * 16 * M;
+  const int qbytes = QT == MLB_Q8_0 ? 4096 : 2048;
   float acc0 = 0.0f, acc1 = 0.0f;
-  int cur_t = -1, cur_grp = -1, seg_c0 = 0;
-  int b_chunk = -1;
+  int b_chunk = -1, r = 0, last_r = -1;
   uint32_t B[16][2];
 #pragma unroll
   for (int s = 0; s < 16; ++s) B[s][0] = B[s][1] = 0u;
-
-  auto flush = [&](int t, int grp, int c0) {
-    // Per-lane accumulators -> myred[row][r]
-    __syncwarp();
-    if (cl < M) {
-      myred[g * M + cl] = acc0;
-      myred[(g + 8) * M + cl] = acc1;
-    }
-    __syncwarp();
-    // Number of segments tile t is split into (static partition).
-    const int nseg = for_each_segment(t, a.ntiles, a.nchunks, a.gc, a.ngroups, a.nsb, W,
-                                      [](int) {});
-    bool finish = true;
-    if (nseg > 1) {
-      float* slot = a.ws + ((size_t)t * a.nchunks + c0) * 16 * M;
-      for (int i = lane; i < 16 * M; i += 32) slot[i] = myred[i];
-      __threadfence();
-      __syncwarp();
-      int last = 0;
-      if (lane == 0) last = (atomicAdd(&a.counters[t], 1) == nseg - 1);
-      last = __shfl_sync(0xffffffffu, last, 0);
-      finish = last != 0;
-      if (finish) {
-        __threadfence();
-        // Sum every segment of the tile in chunk order (deterministic).
-        for (int i = lane; i < 16 * M; i += 32) {
-          float s = 0.0f;
-          for_each_segment(t, a.ntiles, a.nchunks, a.gc, a.ngroups, a.nsb, W, [&](int c) {
-            s += __ldcg(a.ws + ((size_t)t * a.nchunks + c) * 16 * M + i);
-          });
-          myred[i] = s;
-        }
-        if (lane == 0) a.counters[t] = 0;
-        __syncwarp();
+  int slot = 0;
+  uint32_t parity = 0;
+  for (long long u = cb + warp; u < ce; u += kGemvWarps) {
+    while (u >= run_u0[r + 1]) ++r;
+    if (r != last_r) {
+      if (last_r >= 0 && cl < M) {
+        float* sl = slots + ((size_t)last_r * kGemvWarps + warp) * 16 * M;
+        sl[g * M + cl] = acc0;
+        sl[(g + 8) * M + cl] = acc1;
       }
+      acc0 = acc1 = 0.0f;
+      last_r = r;
     }
-    if (finish) {
-      for (int i = lane; i < 16 * M; i += 32) {
-        int row = i / M, r = i - row * M;
-        if (r < rows) epilogue_row<M>(a.epi, t, row, r, myred);
-      }
-    }
-    __syncwarp();
-    acc0 = 0.0f;
-    acc1 = 0.0f;
-  };
-
-  long long it = 0;
-  for (long long u = ub; u < ue; ++u, ++it) {
-    const SbPos sp = sb_decode(u, a.ntiles, a.nchunks, a.gc);
-    if (sp.t != cur_t || sp.grp != cur_grp) {
-      if (cur_t >= 0) flush(cur_t, cur_grp, seg_c0);
-      cur_t = sp.t;
-      cur_grp = sp.grp;
-      seg_c0 = sp.grp * a.gc + sp.cc;
-    }
-    const int chunk = sp.grp * a.gc + sp.cc;
+    const int grp = run_grp[r];
+    const int cc = run_cc0[r] + (int)(u - run_u0[r]);
+    const int chunk = grp * a.gc + cc;
     if (chunk != b_chunk) {
       b_chunk = chunk;
       if (bl) {
         const uint32_t* fsrc =
-            frag + (sp.grp - g0) * slot_u32 + sp.cc * frag_chunk_u32<M>() + lane * kFragLaneStride;
+            frag + (grp - g0) * slot_u32 + cc * frag_chunk_u32<M>() + lane * kFragLaneStride;
 #pragma unroll
         for (int s = 0; s < 8; ++s) {
           uint4 v = *reinterpret_cast<const uint4*>(fsrc + s * 4);
@@ -526,12 +541,10 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 1) gemv_sb_kernel(const GemvK
         }
       }
     }
-    const int slot = (int)(it % kGemvStages);
-    const uint32_t parity = (uint32_t)((it / kGemvStages) & 1);
     if (!mbar_wait_bounded(&mybars[slot], parity, a.status, 2)) return;
     const uint8_t* sb = myring + (size_t)slot * sbb;
 
-    const int qbytes = QT == MLB_Q8_0 ? 4096 : 2048;
+    // everything this lane needs from the super-block, as 16-byte loads
     const uint4 sc0 = *reinterpret_cast<const uint4*>(sb + qbytes + g * 32);
     const uint4 sc1 = *reinterpret_cast<const uint4*>(sb + qbytes + g * 32 + 16);
     const uint32_t scw[8] = {sc0.x, sc0.y, sc0.z, sc0.w, sc1.x, sc1.y, sc1.z, sc1.w};
@@ -542,12 +555,17 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 1) gemv_sb_kernel(const GemvK
       mnw[0] = m0.x; mnw[1] = m0.y; mnw[2] = m0.z; mnw[3] = m0.w;
       mnw[4] = m1.x; mnw[5] = m1.y; mnw[6] = m1.z; mnw[7] = m1.w;
     }
+    constexpr int kQLoads = QT == MLB_Q8_0 ? 8 : 4;  // uint4 per lane per super-block
+    uint4 qv[kQLoads];
+#pragma unroll
+    for (int i = 0; i < kQLoads; ++i)
+      qv[i] = *reinterpret_cast<const uint4*>(sb + (size_t)(i * 32 + lane) * 16);
 
 #pragma unroll
     for (int b = 0; b < 8; ++b) {
       uint32_t A1[4], A2[4];
       if (QT == MLB_Q8_0) {
-        const uint4 q = *reinterpret_cast<const uint4*>(sb + (size_t)(b * 32 + lane) * 16);
+        const uint4 q = qv[b];
         const __half2 bias = __float2half2_rn(1152.0f);
         const uint32_t wx[4] = {q.x ^ 0x80808080u, q.y ^ 0x80808080u, q.z ^ 0x80808080u,
                                 q.w ^ 0x80808080u};
@@ -561,9 +579,8 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 1) gemv_sb_kernel(const GemvK
         A2[1] = h2_as_u32(__hsub2(u32_as_h2(__byte_perm(wx[3], 0x64646464u, 0x4140)), bias));
         A2[3] = h2_as_u32(__hsub2(u32_as_h2(__byte_perm(wx[3], 0x64646464u, 0x4342)), bias));
       } else {
-        const uint2 q =
-            *reinterpret_cast<const uint2*>(sb + (size_t)((b >> 1) * 32 + lane) * 16 + (b & 1) * 8);
-        const uint32_t w0 = q.x, w1 = q.y;  // rows g and g+8
+        const uint4 q = qv[b >> 1];
+        const uint32_t w0 = (b & 1) ? q.z : q.x, w1 = (b & 1) ? q.w : q.y;  // rows g, g+8
         const uint32_t w0s = w0 >> 8, w1s = w1 >> 8;
         const uint32_t M1 = 0x000F000Fu, M2 = 0x00F000F0u, E = 0x64006400u;
         // low nibbles: 1024 + q ; high nibbles: 1024 + 16 q
@@ -588,20 +605,116 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 1) gemv_sb_kernel(const GemvK
       if (QT == MLB_Q4_1) {
         const float2 mn = __half22float2(u32_as_h2(mnw[b]));
         const int rr = cl < M ? cl : 0;
-        const float sx = bsum[(sp.grp - g0) * bsum_slot + (sp.cc * 8 + b) * M + rr];
+        const float sx = bsum[(grp - g0) * bsum_slot + (cc * 8 + b) * M + rr];
         acc0 = fmaf(mn.x, sx, acc0);
         acc1 = fmaf(mn.y, sx, acc1);
       }
     }
+    // All lanes have consumed the slot (their loads fed the MMAs above), so lane 0
+    // can refill it; the mbarrier protocol orders the bulk copy after the reads.
     __syncwarp();
-    if (lane == 0 && u + kGemvStages < ue) {
-      fence_proxy_async_smem();
+    const long long un = u + (long long)S * kGemvWarps;
+    if (lane == 0 && un < ce) {
       mbar_arrive_expect_tx(&mybars[slot], sbb);
-      bulk_g2s(myring + (size_t)slot * sbb, a.w + (size_t)(u + kGemvStages) * sbb, sbb,
-               &mybars[slot]);
+      bulk_g2s(myring + (size_t)slot * sbb, a.w + (size_t)un * sbb, sbb, &mybars[slot]);
+    }
+    if (++slot == S) {
+      slot = 0;
+      parity ^= 1u;
     }
   }
-  if (cur_t >= 0) flush(cur_t, cur_grp, seg_c0);
+  if (last_r >= 0 && cl < M) {
+    float* sl = slots + ((size_t)last_r * kGemvWarps + warp) * 16 * M;
+    sl[g * M + cl] = acc0;
+    sl[(g + 8) * M + cl] = acc1;
+  }
+  __syncthreads();
+
+  // 5. Finish the runs: sum the warps' slots in warp order; a run that is a
+  //    whole tile goes straight to the epilogue, a partial one joins the
+  //    tile's other segments through the workspace (last arriver sums them in
+  //    chunk order).
+  float* myred = red + warp * (16 * M + kSegList);
+  int* seglist = reinterpret_cast<int*>(myred + 16 * M);
+  for (int rr = warp; rr < nruns; rr += kGemvWarps) {
+    const int t = run_t[rr], grp = run_grp[rr];
+    const int geff = min(a.gc, a.nchunks - grp * a.gc);
+    const long long len = run_u0[rr + 1] - run_u0[rr];
+    for (int i = lane; i < 16 * M; i += 32) {
+      float s = 0.0f;
+      for (int w = 0; w < kGemvWarps; ++w) s += slots[((size_t)rr * kGemvWarps + w) * 16 * M + i];
+      myred[i] = s;
+    }
+    __syncwarp();
+    bool finish = a.ngroups == 1 && run_cc0[rr] == 0 && len == geff;
+    if (!finish) {
+      float* slotw = a.ws + ((size_t)t * a.nchunks + grp * a.gc + run_cc0[rr]) * 16 * M;
+      for (int i = lane; i < 16 * M; i += 32) slotw[i] = myred[i];
+      __threadfence();
+      __syncwarp();
+      int nseg = 0;
+      if (lane == 0)
+        nseg = for_each_segment(t, a.ntiles, a.nchunks, a.gc, a.ngroups, a.nsb, G, [](int) {});
+      int last = 0;
+      if (lane == 0) last = (atomicAdd(&a.counters[t], 1) == nseg - 1);
+      last = __shfl_sync(0xffffffffu, last, 0);
+      finish = last != 0;
+      if (finish) {
+        __threadfence();
+        float s[(16 * M + 31) / 32];
+#pragma unroll
+        for (int q = 0; q < (16 * M + 31) / 32; ++q) s[q] = 0.0f;
+        // gather the segment starts kSegList at a time, then sum with
+        // independent loads, in chunk order
+        int done = 0;
+        while (true) {
+          int cnt = 0;
+          if (lane == 0) {
+            int idx = 0;
+            for_each_segment(t, a.ntiles, a.nchunks, a.gc, a.ngroups, a.nsb, G, [&](int c) {
+              if (idx >= done && idx < done + kSegList) seglist[idx - done] = c;
+              ++idx;
+            });
+            cnt = min(kSegList, idx - done);
+          }
+          cnt = __shfl_sync(0xffffffffu, cnt, 0);
+          __syncwarp();
+          if (cnt <= 0) break;
+#pragma unroll
+          for (int q = 0; q < (16 * M + 31) / 32; ++q) {
+            const int i = lane + 32 * q;
+            if (i < 16 * M)
+              for (int j = 0; j < cnt; ++j)
+                s[q] += __ldcg(a.ws + ((size_t)t * a.nchunks + seglist[j]) * 16 * M + i);
+          }
+          done += cnt;
+          __syncwarp();
+          if (cnt < kSegList) break;
+        }
+#pragma unroll
+        for (int q = 0; q < (16 * M + 31) / 32; ++q) {
+          const int i = lane + 32 * q;
+          if (i < 16 * M) myred[i] = s[q];
+        }
+        if (lane == 0) a.counters[t] = 0;
+        __syncwarp();
+      }
+    }
+    if (finish) {
+      for (int i = lane; i < 16 * M; i += 32) {
+        int row = i / M, rb = i - row * M;
+        if (rb < rows) epilogue_row<M>(a.epi, t, row, rb, myred);
+      }
+      if (a.epi.argmax_key) {
+        unsigned long long key = 0ull;
+        if (lane < 16 && t * 16 + lane < a.epi.n_out)
+          key = argmax_key_of(myred[lane * M], a.epi.argmax_base + t * 16 + lane);
+        key = warp_max_u64(key);
+        if (lane == 0 && key) atomicMax(a.epi.argmax_key, key);
+      }
+    }
+    __syncwarp();
+  }
 }
 
 // ------------------------------------------------------------ F32 GEMV kernel
@@ -664,6 +777,13 @@ __global__ void __launch_bounds__(256) gemv_f32_kernel(const float* w, int ntile
       int row = i / M, r = i - row * M;
       if (r < rows) epilogue_row<M>(epi, t, row, r, red[warp]);
     }
+    if (epi.argmax_key) {
+      unsigned long long key = 0ull;
+      if (lane < 16 && t * 16 + lane < epi.n_out)
+        key = argmax_key_of(red[warp][lane * M], epi.argmax_base + t * 16 + lane);
+      key = warp_max_u64(key);
+      if (lane == 0 && key) atomicMax(epi.argmax_key, key);
+    }
     __syncwarp();
   }
 }
@@ -672,6 +792,45 @@ __global__ void __launch_bounds__(256) gemv_f32_kernel(const float* w, int ntile
 
 static int pick_batch(int rows) { return rows <= 1 ? 1 : (rows == 2 ? 2 : 4); }
 
+// Largest number of (group, tile) runs, and of chunk groups, any CTA range
+// touches when the super-blocks are split over G CTAs.
+static void cta_span(const QMatrix& m, long long G, int* max_runs, int* max_groups) {
+  *max_runs = 0;
+  *max_groups = 0;
+  for (long long c = 0; c < G; ++c) {
+    long long u = cta_start(c, m.nsb, G);
+    const long long ce = cta_start(c + 1, m.nsb, G);
+    int runs = 0, g0 = -1, g1 = -1;
+    while (u < ce) {
+      const SbPos sp = sb_decode(u, m.ntiles, m.nchunks, m.gc);
+      if (g0 < 0) g0 = sp.grp;
+      g1 = sp.grp;
+      u += std::min((long long)(sp.geff - sp.cc), ce - u);
+      ++runs;
+    }
+    *max_runs = std::max(*max_runs, runs);
+    *max_groups = std::max(*max_groups, g0 < 0 ? 0 : g1 - g0 + 1);
+  }
+}
+
+// Grid for a matrix: one CTA per SM unless a CTA range would touch more runs
+// or chunk groups than its shared memory holds; then more (smaller) CTAs.
+template <int M>
+static long long choose_grid(const QMatrix& m, int sms) {
+  const int idx = M == 1 ? 0 : (M == 2 ? 1 : 2);
+  if (m.grid_cache[idx] > 0) return m.grid_cache[idx];
+  long long G = std::min<long long>(std::max<long long>(sms, m.ngroups > 1 ? m.ngroups + 1 : 1),
+                                    m.nsb);
+  while (true) {
+    int runs = 0, groups = 0;
+    cta_span(m, G, &runs, &groups);
+    if ((runs <= max_cta_runs<M>() && groups <= 2) || G >= m.nsb) break;
+    G = std::min<long long>(m.nsb, G + G / 4 + 1);
+  }
+  m.grid_cache[idx] = (int)G;
+  return G;
+}
+
 template <int QT, int M, bool NORM>
 static void launch_sb(const QMatrix& m, const float* x, int rows, int ldx, const NormSpec& norm,
                       const EpiParams& epi, const GemvWorkspace& ws, cudaStream_t stream,
@@ -679,28 +838,26 @@ static void launch_sb(const QMatrix& m, const float* x, int rows, int ldx, const
   int dev = 0;
   MLB_CUDA(cudaGetDevice(&dev));
   const int sbb = sb_bytes(QT);
-  const size_t smem = gemv_smem_bytes<QT, M>(m.gc, sbb);
+  const int nslots = m.ngroups > 1 ? 2 : 1;
+  constexpr size_t kSmemMax = 227 * 1024;
+  const size_t fixed = gemv_smem_layout<QT, M>(m.gc, nslots, sbb, 0).total;
+  const int stages = (int)std::min<size_t>(
+      kMaxStages, fixed < kSmemMax ? (kSmemMax - fixed) / ((size_t)kGemvWarps * sbb) : 0);
+  if (stages < 2) invalid("gemv: staged activations leave no room for the weight ring");
+  const size_t smem = gemv_smem_layout<QT, M>(m.gc, nslots, sbb, stages).total;
   static size_t smem_set[64] = {};
   if (dev < 64 && smem_set[dev] < smem) {
     MLB_CUDA(cudaFuncSetAttribute(gemv_sb_kernel<QT, M, NORM>,
                                   cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     smem_set[dev] = smem;
   }
-  int sms = sm_count(dev);
-  long long grid = grid_ctas > 0 ? grid_ctas : sms;
-  // Every CTA must span <= 2 chunk groups (its range must not exceed a group):
-  // at least ngroups + 1 CTAs. At most one CTA per 8 super-blocks, so warps are
-  // not idle; that bound alone already keeps a CTA range within 8-9 SBs, which
-  // never exceeds a group of >= 16 SBs (or there is a single group).
-  long long per_group = (long long)m.ntiles * m.gc;
-  long long min_grid = (m.nsb + per_group - 1) / per_group + 1;
-  long long max_grid = std::max(1LL, m.nsb / kGemvWarps);
-  grid = std::min(std::max(grid, min_grid), max_grid);
+  const long long grid = grid_ctas > 0 ? grid_ctas : choose_grid<M>(m, sm_count(dev));
   if ((size_t)m.ntiles * m.nchunks * 16 * M > ws.partial_floats || (size_t)m.ntiles > ws.counter_count)
     invalid("gemv: workspace too small");
   GemvKArgs a;
   a.w = m.data;
   a.sbb = sbb;
+  a.stages = stages;
   a.ntiles = m.ntiles;
   a.nchunks = m.nchunks;
   a.gc = m.gc;

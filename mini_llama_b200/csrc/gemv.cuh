@@ -22,8 +22,7 @@ namespace mlb {
 
 constexpr int kTileRows = 16;
 constexpr int kChunkK = 256;
-constexpr int kGemvWarps = 8;
-constexpr int kGemvStages = 4;
+constexpr int kGemvWarps = 16;  // warps per CTA, one CTA per SM
 constexpr int kMaxBatch = 4;  // batch rows one pass of the MMA GEMV carries
 
 inline int sb_bytes(int qtype) {
@@ -61,7 +60,35 @@ struct EpiParams {
   float* keys;                // cache slot base of this layer: + pos * kv_rows
   float* values;
   float* q_out;
+  // Greedy argmax fused into a store epilogue (batch row 0): every finished
+  // tile folds its rows into *argmax_key with atomicMax on
+  // (order-preserving float bits << 32 | ~index); argmax_base offsets the index
+  // (vocabulary shard start under tensor parallelism).
+  unsigned long long* argmax_key;
+  int argmax_base;
 };
+
+#if defined(__CUDACC__)
+// Key whose unsigned order is (value, then lower index) order; NaN maps to 0
+// and never wins, as in ArgMax (src/ops.cc:226-231, `x > best` is false for NaN).
+__device__ __forceinline__ unsigned long long argmax_key_of(float v, int index) {
+  if (v != v) return 0ull;
+  unsigned int u = __float_as_uint(v);
+  u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+  return ((unsigned long long)u << 32) | (unsigned long long)(0xFFFFFFFFu - (unsigned int)index);
+}
+__device__ __forceinline__ int argmax_index_of(unsigned long long key) {
+  return key == 0ull ? 0 : (int)(0xFFFFFFFFu - (unsigned int)(key & 0xFFFFFFFFull));
+}
+__device__ __forceinline__ unsigned long long warp_max_u64(unsigned long long v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    unsigned long long w = __shfl_xor_sync(0xffffffffu, v, o);
+    v = w > v ? w : v;
+  }
+  return v;
+}
+#endif
 
 struct QMatrix {
   int qtype = 0;
@@ -73,6 +100,7 @@ struct QMatrix {
   size_t gguf_bytes = 0;     // algorithmic GGUF bytes
   uint8_t* data = nullptr;   // device
   bool owns = true;
+  mutable int grid_cache[3] = {0, 0, 0};  // launch grid per batch width (1, 2, 4)
 };
 
 // Geometry for a [n, k] weight of qtype with group size chosen for batch M.

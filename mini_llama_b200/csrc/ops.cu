@@ -90,9 +90,9 @@ __global__ void softmax_kernel(const float* x, int n, float* y) {
 // Embedding row; the token comes from the host or from device memory.
 __global__ void embedding_kernel(const float* table, int vocab, int dim, const int* token_dev,
                                  int token_host, float* y) {
+  pdl_launch_dependents();
   pdl_wait();
   int tok = token_dev ? *token_dev : token_host;
-  pdl_launch_dependents();
   if (tok < 0 || tok >= vocab) return;  // validated on the host before launch
   const float* row = table + (size_t)tok * dim;
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < dim; i += gridDim.x * blockDim.x)
@@ -166,12 +166,6 @@ __global__ void argmax_kernel(const float* x, int n, int* out_dev, int* out_dev2
   }
 }
 
-__global__ void incr_kernel(int* v) {
-  pdl_wait();
-  pdl_launch_dependents();
-  *v += 1;
-}
-
 // ------------------------------------------------------------- launchers
 
 static unsigned blocks_for(long long n, int t = 256) { return (unsigned)((n + t - 1) / t); }
@@ -215,7 +209,6 @@ void op_kv_write(float* keys, float* values, size_t slot, int n, const float* k,
 void op_argmax(const float* x, int n, int* out_dev, int* out_dev2, cudaStream_t s, bool pdl) {
   launch_pdl(argmax_kernel, dim3(1), dim3(1024), 0, s, pdl, x, n, out_dev, out_dev2);
 }
-void op_incr(int* v, cudaStream_t s, bool pdl) { launch_pdl(incr_kernel, dim3(1), dim3(1), 0, s, pdl, v); }
 
 // (cos, sin) of pos * theta^(-2j/D) for j < D/2, evaluated on the host with the
 // reference's float expressions (src/ops.cc:148-151 and 168-170).

@@ -17,7 +17,6 @@ void op_rope(float* q, float* k, int nh, int nkv, int D, int neox, const float2*
 void op_kv_write(float* keys, float* values, size_t slot, int n, const float* k, const float* v,
                  cudaStream_t s);
 void op_argmax(const float* x, int n, int* out_dev, int* out_dev2, cudaStream_t s, bool pdl);
-void op_incr(int* v, cudaStream_t s, bool pdl);
 void op_fill(float* p, long long n, float v, cudaStream_t s);
 void rope_table_host(float theta, int D, int pos0, int npos, float2* out);
 // Seeded GGUF blocks for destination rows whose source rows are src_rows[i]

@@ -450,6 +450,8 @@ ContextImpl::~ContextImpl() {
   if (m) cudaSetDevice(m->device);
   if (exec) cudaGraphExecDestroy(exec);
   if (graph) cudaGraphDestroy(graph);
+  if (exec_greedy) cudaGraphExecDestroy(exec_greedy);
+  if (graph_greedy) cudaGraphDestroy(graph_greedy);
   if (h_scalars) cudaFreeHost(h_scalars);
   if (h_logits) cudaFreeHost(h_logits);
   if (h_tokens) cudaFreeHost(h_tokens);
@@ -506,6 +508,8 @@ ContextImpl* context_create(ModelImpl& m, int mode) {
   // scalars: [0] token, [1] pos, [2] step, [3] spare, then tokens[max_seq]
   c->scalars.alloc((size_t)(4 + cf.max_seq_len) * 4);
   MLB_CUDA(cudaMemset(c->scalars.p, 0, c->scalars.bytes));
+  c->argmax_key.alloc(sizeof(unsigned long long));
+  MLB_CUDA(cudaMemset(c->argmax_key.p, 0, sizeof(unsigned long long)));
   MLB_CUDA(cudaMallocHost(&c->h_scalars, 4 * sizeof(int)));
   MLB_CUDA(cudaMallocHost(&c->h_logits, (size_t)cf.vocab_size * 4));
   MLB_CUDA(cudaMallocHost(&c->h_tokens, (size_t)cf.max_seq_len * 4));
@@ -513,10 +517,20 @@ ContextImpl* context_create(ModelImpl& m, int mode) {
   return c.release();
 }
 
-__global__ void argmax_to_slot_kernel(const float* x, int n, int* token, int* tokens,
-                                      const int* step);
+// Ends a step: the greedy token of the fused argmax becomes the next input
+// token and tokens[step]; position and step advance; the key is cleared.
+__global__ void step_finalize_kernel(unsigned long long* key, int* token, int* tokens, int* step,
+                                     int* pos) {
+  pdl_wait();
+  const int t = argmax_index_of(*key);
+  *token = t;
+  tokens[*step] = t;
+  *step += 1;
+  *pos += 1;
+  *key = 0ull;
+}
 
-void ContextImpl::record_step(cudaStream_t s, bool pdl) {
+void ContextImpl::record_step(cudaStream_t s, bool pdl, bool full_logits) {
   const mlb_config& cf = m->cfg;
   const int D = cf.head_dim;
   int* d_token = scalars.as<int>();
@@ -622,72 +636,38 @@ void ContextImpl::record_step(cudaStream_t s, bool pdl) {
   el.y = m->tp_size == 1 ? logits.as<float>() : logits_local.as<float>();
   el.ldy = m->vocab_rows;
   el.n_out = m->vocab_rows;
+  el.argmax_key = argmax_key.as<unsigned long long>();
+  el.argmax_base = m->vocab_row0;
   NormSpec fin{m->final_norm.as<float>(), cf.rms_norm_eps};
   gemv_launch(m->lm_head, xa.as<float>(), 1, cf.dim, fin, el, ws, s, pdl);
   kernels_per_step += gemv_kernel_count(m->lm_head, 1);
-  if (m->tp_size > 1)
-    MLB_NCCL(ncclAllGather(logits_local.p, logits.p, m->vocab_rows, ncclFloat, m->comm, s));
-  argmax_to_slot_kernel<<<1, 1024, 0, s>>>(logits.as<float>(), cf.vocab_size, d_token, d_tokens,
-                                           d_step);
-  MLB_CUDA(cudaGetLastError());
+  if (m->tp_size > 1) {
+    // greedy token across the vocabulary shards: max of the packed keys
+    MLB_NCCL(ncclAllReduce(argmax_key.p, argmax_key.p, 1, ncclUint64, ncclMax, m->comm, s));
+    if (full_logits)
+      MLB_NCCL(ncclAllGather(logits_local.p, logits.p, m->vocab_rows, ncclFloat, m->comm, s));
+  }
+  launch_pdl(step_finalize_kernel, dim3(1), dim3(1), 0, s, pdl && m->tp_size == 1,
+             argmax_key.as<unsigned long long>(), d_token, d_tokens, d_step, d_pos);
   ++kernels_per_step;
-  op_incr(d_pos, s, false);
-  op_incr(d_step, s, false);
-  kernels_per_step += 2;
-}
-
-__global__ void argmax_to_slot_kernel(const float* x, int n, int* token, int* tokens,
-                                      const int* step) {
-  __shared__ float bv[32];
-  __shared__ int bi[32];
-  float best = -INFINITY;
-  int idx = 0x7fffffff;
-  for (int i = threadIdx.x; i < n; i += blockDim.x) {
-    float v = x[i];
-    if (v > best || (v == best && i < idx)) {
-      best = v;
-      idx = i;
-    }
-  }
-  for (int o = 16; o > 0; o >>= 1) {
-    float ov = __shfl_xor_sync(0xffffffffu, best, o);
-    int oi = __shfl_xor_sync(0xffffffffu, idx, o);
-    if (ov > best || (ov == best && oi < idx)) {
-      best = ov;
-      idx = oi;
-    }
-  }
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  if (lane == 0) {
-    bv[warp] = best;
-    bi[warp] = idx;
-  }
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    for (int w = 1; w < (int)(blockDim.x >> 5); ++w)
-      if (bv[w] > best || (bv[w] == best && bi[w] < idx)) {
-        best = bv[w];
-        idx = bi[w];
-      }
-    if (idx == 0x7fffffff) idx = 0;
-    *token = idx;
-    tokens[*step] = idx;
-  }
 }
 
 void ContextImpl::build_graph() {
   set_device(m->device);
-  MLB_CUDA(cudaStreamBeginCapture(stream, cudaStreamCaptureModeThreadLocal));
-  try {
-    record_step(stream, true);
-  } catch (...) {
-    cudaGraph_t g = nullptr;
-    cudaStreamEndCapture(stream, &g);
-    if (g) cudaGraphDestroy(g);
-    throw;
+  for (int full = 1; full >= 0; --full) {
+    MLB_CUDA(cudaStreamBeginCapture(stream, cudaStreamCaptureModeThreadLocal));
+    try {
+      record_step(stream, true, full != 0);
+    } catch (...) {
+      cudaGraph_t g = nullptr;
+      cudaStreamEndCapture(stream, &g);
+      if (g) cudaGraphDestroy(g);
+      throw;
+    }
+    cudaGraph_t& g = full ? graph : graph_greedy;
+    MLB_CUDA(cudaStreamEndCapture(stream, &g));
+    MLB_CUDA(cudaGraphInstantiate(full ? &exec : &exec_greedy, g, 0));
   }
-  MLB_CUDA(cudaStreamEndCapture(stream, &graph));
-  MLB_CUDA(cudaGraphInstantiate(&exec, graph, 0));
 }
 
 void ContextImpl::check_status() {
@@ -734,7 +714,7 @@ void context_decode_greedy(ContextImpl& c, int token, int pos, int n, int* token
   c.h_scalars[1] = pos;
   c.h_scalars[2] = 0;
   MLB_CUDA(cudaMemcpyAsync(c.scalars.p, c.h_scalars, 3 * sizeof(int), cudaMemcpyHostToDevice, c.stream));
-  for (int i = 0; i < n; ++i) MLB_CUDA(cudaGraphLaunch(c.exec, c.stream));
+  for (int i = 0; i < n; ++i) MLB_CUDA(cudaGraphLaunch(c.exec_greedy, c.stream));
   MLB_CUDA(cudaMemcpyAsync(c.h_tokens, c.scalars.as<int>() + 4, (size_t)n * 4,
                            cudaMemcpyDeviceToHost, c.stream));
   MLB_CUDA(cudaStreamSynchronize(c.stream));

@@ -76,16 +76,18 @@ struct ContextImpl {
   DevBuf xa, xb, y, q, attn, hidden, logits_local, logits;
   DevBuf gemv_ws, gemv_cnt, attn_ws, attn_cnt, status;
   DevBuf scalars;             // int: token, pos, step, next token ; then tokens[max_seq]
+  DevBuf argmax_key;          // u64 packed (logit, index) of the step's greedy argmax
   int* h_scalars = nullptr;   // pinned: token, pos
   float* h_logits = nullptr;  // pinned
   int* h_tokens = nullptr;    // pinned
   int attn_splits = 1;
   GemvWorkspace ws;
-  cudaGraph_t graph = nullptr;
-  cudaGraphExec_t exec = nullptr;
+  cudaGraph_t graph = nullptr, graph_greedy = nullptr;
+  cudaGraphExec_t exec = nullptr;         // step that also leaves full logits on the device
+  cudaGraphExec_t exec_greedy = nullptr;  // step that only produces the next token
   int kernels_per_step = 0;
   void build_graph();
-  void record_step(cudaStream_t s, bool pdl);
+  void record_step(cudaStream_t s, bool pdl, bool full_logits);
   void check_status();
   ~ContextImpl();
 };
