@@ -152,6 +152,27 @@ int mlb_attention_decode(const float* q_dev, const float* keys_dev,
                          int head_dim, int mode, float* out_dev, int device_id,
                          void* stream);
 
+/* The same attention as mlb_attention_decode, for callers that must not
+ * allocate device memory during the call: hosts whose device memory is owned by
+ * their own allocator under a fixed budget, and latency-sensitive decode loops
+ * that cannot afford cudaMalloc/cudaFree (cudaFree synchronises the device).
+ * It has no counterpart in the reference (whose attention allocates its score
+ * buffer per call, src/cuda_attention.cu:268-273). Its split-K scratch is a
+ * fixed array inside the library: 4 MiB of partials (at most 2^20 floats for
+ * one split: n_kv_heads * (n_heads / n_kv_heads) * (head_dim + 2)) plus
+ * counters for at most 1024 KV heads; larger shapes are rejected with
+ * MLB_ERR_INVALID. Every GPU that loads the library holds this array until the
+ * process exits. The first call on a device looks up the array's device
+ * address, so make that first call before any stream capture. All calls share
+ * the array: calls that overlap on the GPU (other streams, other threads) race
+ * and give wrong results; run them one after another. Asynchronous on `stream`
+ * (no host synchronisation). */
+int mlb_attention_decode_noalloc(const float* q_dev, const float* keys_dev,
+                                 const float* values_dev, int n_layers,
+                                 int max_seq_len, int layer, int pos, int n_heads,
+                                 int n_kv_heads, int head_dim, int mode,
+                                 float* out_dev, int device_id, void* stream);
+
 /* --------------------------------------------------------- prepared weights
  * A weight repacked once into the B200 GEMV layout (what the decode path
  * streams). No reference counterpart as an API: it is the device-resident

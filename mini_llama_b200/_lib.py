@@ -49,6 +49,8 @@ SIGNATURES = [
                               _c_int, _vp]),
     ("mlb_attention_decode", _c_int, [_vp, _vp, _vp, _c_int, _c_int, _c_int, _c_int, _c_int,
                                       _c_int, _c_int, _c_int, _vp, _c_int, _vp]),
+    ("mlb_attention_decode_noalloc", _c_int, [_vp, _vp, _vp, _c_int, _c_int, _c_int, _c_int,
+                                              _c_int, _c_int, _c_int, _c_int, _vp, _c_int, _vp]),
     ("mlb_qmatrix_create", _c_int, [_c_int, _vp, _c_int, _c_int, _c_int, _c_int,
                                     ctypes.POINTER(_vp)]),
     ("mlb_qmatrix_synthesize", _c_int, [_c_int, _c_int, _c_int, _c_u64, _c_u64, _c_int, _c_int,
