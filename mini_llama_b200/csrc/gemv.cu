@@ -311,7 +311,7 @@ __host__ __device__ constexpr int frag_chunk_u32() {
 // that no CTA exceeds it.
 template <int M>
 __host__ __device__ constexpr int max_cta_runs() {
-  return M == 1 ? 8 : 4;
+  return M == 1 ? 16 : 4;
 }
 
 struct GemvSmem {
@@ -814,7 +814,8 @@ static void cta_span(const QMatrix& m, long long G, int* max_runs, int* max_grou
 }
 
 // Grid for a matrix: one CTA per SM unless a CTA range would touch more runs
-// or chunk groups than its shared memory holds; then more (smaller) CTAs.
+// or chunk groups than its shared memory holds; then whole extra waves of
+// (smaller) CTAs, since only one CTA fits on an SM.
 template <int M>
 static long long choose_grid(const QMatrix& m, int sms) {
   const int idx = M == 1 ? 0 : (M == 2 ? 1 : 2);
@@ -825,7 +826,7 @@ static long long choose_grid(const QMatrix& m, int sms) {
     int runs = 0, groups = 0;
     cta_span(m, G, &runs, &groups);
     if ((runs <= max_cta_runs<M>() && groups <= 2) || G >= m.nsb) break;
-    G = std::min<long long>(m.nsb, G + G / 4 + 1);
+    G = std::min<long long>(m.nsb, (G / sms + 1) * sms);
   }
   m.grid_cache[idx] = (int)G;
   return G;
