@@ -259,6 +259,17 @@ int mlb_decode_greedy(mlb_context* c, int token, int pos, int n_steps,
 void* mlb_context_stream(mlb_context* c);
 /* Number of kernels one decode step launches on this rank. */
 int mlb_context_kernels_per_step(const mlb_context* c);
+/* Selects how a single-GPU decode step runs: 1 = the persistent step kernel
+ * (one cooperative launch computes the whole step; the default wherever the
+ * model allows it), 0 = one kernel per op in a CUDA graph. Asking for 1 on a
+ * model the step kernel does not take (tensor parallel, F32 or mixed quant
+ * types, head_dim > 128 or not a multiple of 4, very large GQA groups)
+ * returns MLB_ERR_INVALID and mlb_last_error() gives the reason. No reference
+ * counterpart: the reference always launches one kernel per op
+ * (src/forward.cc:700-794). */
+int mlb_context_set_step_kernel(mlb_context* c, int enable);
+/* 1 when this context's steps run as the persistent step kernel, else 0. */
+int mlb_context_step_kernel(const mlb_context* c);
 
 /* 128-byte NCCL unique id for building a tensor-parallel communicator. */
 int mlb_nccl_unique_id(void* out128);

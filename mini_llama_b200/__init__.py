@@ -389,8 +389,8 @@ class CudaModel:
         check(lib().mlb_model_bytes(self.h, ctypes.byref(r), ctypes.byref(s)))
         return r.value, s.value
 
-    def context(self, attention_mode=ATTN_CPU_COMPAT):
-        return Context(self, attention_mode)
+    def context(self, attention_mode=ATTN_CPU_COMPAT, step_kernel=None):
+        return Context(self, attention_mode, step_kernel)
 
     def close(self):
         if getattr(self, "h", None):
@@ -407,13 +407,22 @@ class CudaModel:
 class Context:
     """MiniLlamaContext with its CUDA KV cache (include/mini_llama/context.h)."""
 
-    def __init__(self, model: CudaModel, attention_mode=ATTN_CPU_COMPAT):
+    def __init__(self, model: CudaModel, attention_mode=ATTN_CPU_COMPAT, step_kernel=None):
         self.model = model
         h = ctypes.c_void_p()
         check(lib().mlb_context_create(model.h, attention_mode, ctypes.byref(h)))
         self.h = h
         self.pos = 0
         self.token_history = []
+        if step_kernel is not None:
+            self.set_step_kernel(step_kernel)
+
+    def set_step_kernel(self, enable: bool):
+        """True: one persistent kernel per decode step; False: one kernel per op."""
+        check(lib().mlb_context_set_step_kernel(self.h, 1 if enable else 0))
+
+    def step_kernel(self) -> bool:
+        return bool(lib().mlb_context_step_kernel(self.h))
 
     def forward_token(self, token: int, pos: int) -> np.ndarray:
         """ForwardToken's device branch (src/forward.cc:776-794): host logits."""

@@ -74,6 +74,8 @@ SIGNATURES = [
     ("mlb_decode_greedy", _c_int, [_vp, _c_int, _c_int, _c_int, _vp]),
     ("mlb_context_stream", _vp, [_vp]),
     ("mlb_context_kernels_per_step", _c_int, [_vp]),
+    ("mlb_context_set_step_kernel", _c_int, [_vp, _c_int]),
+    ("mlb_context_step_kernel", _c_int, [_vp]),
     ("mlb_nccl_unique_id", _c_int, [_vp]),
 ]
 

@@ -512,6 +512,15 @@ int mlb_context_kernels_per_step(const mlb_context* c) {
   return c ? c->impl->kernels_per_step : 0;
 }
 
+int mlb_context_set_step_kernel(mlb_context* c, int enable) {
+  return guarded([&] {
+    if (!c) invalid("mlb_context_set_step_kernel: null context");
+    c->impl->set_use_step(enable != 0);
+  });
+}
+
+int mlb_context_step_kernel(const mlb_context* c) { return c && c->impl->use_step ? 1 : 0; }
+
 int mlb_nccl_unique_id(void* out128) {
   return guarded([&] {
     if (!out128) invalid("mlb_nccl_unique_id: null output");

@@ -22,6 +22,7 @@
 // programmatic dependent launch a GEMV streams its weights while the previous
 // kernel finishes.
 #include "gemv.cuh"
+#include "gemv_dev.cuh"
 
 #include <algorithm>
 #include <cmath>
@@ -163,81 +164,6 @@ void qmatrix_repack(const QMatrix& m, const uint8_t* src, size_t src_pitch, cons
   MLB_CUDA(cudaGetLastError());
 }
 
-// --------------------------------------------------------------- epilogues
-
-template <int M>
-__device__ void epilogue_row(const EpiParams& p, int tile, int row, int r, const float* vals) {
-  float v = vals[row * M + r];
-  int grow = tile * 16 + row;
-  switch (p.kind) {
-    case kEpiStore:
-      if (grow < p.n_out) p.y[(size_t)r * p.ldy + grow] = v;
-      break;
-    case kEpiResidual:
-      if (grow < p.n_out)
-        p.y[(size_t)r * p.ldy + grow] = __fadd_rn(p.resid[(size_t)r * p.ldr + grow], v);
-      break;
-    case kEpiSwiglu: {
-      if (row >= 8) break;
-      int h = tile * 8 + row;
-      if (h >= p.n_out) break;
-      float g = v, u = vals[(row + 8) * M + r];
-      float sg = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-g)));
-      p.y[(size_t)r * p.ldy + h] = __fmul_rn(__fmul_rn(g, sg), u);
-      break;
-    }
-    case kEpiQkv: {
-      int local, size, sec;
-      if (grow < p.k_off) {
-        sec = 0; local = grow; size = p.q_rows;
-      } else if (grow < p.v_off) {
-        sec = 1; local = grow - p.k_off; size = p.kv_rows;
-      } else {
-        sec = 2; local = grow - p.v_off; size = p.kv_rows;
-      }
-      if (local >= size) break;
-      const int D = p.head_dim;
-      auto logical = [&](int l) {
-        if (!p.neox || sec == 2) return l;
-        int hd = l / D, q = l - hd * D;
-        return hd * D + ((q & 1) ? (q >> 1) + D / 2 : (q >> 1));
-      };
-      const int bias_base = sec == 0 ? 0 : (sec == 1 ? p.q_rows : p.q_rows + p.kv_rows);
-      int L = logical(local);
-      if (p.bias) v = __fadd_rn(v, p.bias[bias_base + L]);
-      int pos = *p.pos;
-      if (sec == 2) {
-        p.values[(size_t)pos * p.kv_rows + L] = v;
-        break;
-      }
-      int partner = local ^ 1;
-      float w = vals[(row ^ 1) * M + r];
-      if (p.bias) w = __fadd_rn(w, p.bias[bias_base + logical(partner)]);
-      int in_head = L % D;
-      int j;
-      bool first;
-      if (p.neox) {
-        first = in_head < D / 2;
-        j = first ? in_head : in_head - D / 2;
-      } else {
-        first = (in_head & 1) == 0;
-        j = in_head >> 1;
-      }
-      float2 cs = p.rope[(size_t)pos * (D / 2) + j];
-      float out;
-      if (first)  // a*c - b*s with a = this, b = partner (src/ops.cc:155, 174)
-        out = __fsub_rn(__fmul_rn(v, cs.x), __fmul_rn(w, cs.y));
-      else        // a*s + b*c with a = partner, b = this (src/ops.cc:156, 175)
-        out = __fadd_rn(__fmul_rn(w, cs.y), __fmul_rn(v, cs.x));
-      if (sec == 0)
-        p.q_out[(size_t)r * p.q_rows + L] = out;
-      else
-        p.keys[(size_t)pos * p.kv_rows + L] = out;
-      break;
-    }
-  }
-}
-
 // ---------------------------------------------------- super-block GEMV kernel
 
 struct GemvKArgs {
@@ -258,64 +184,8 @@ struct GemvKArgs {
   EpiParams epi;
 };
 
-struct SbPos {
-  int grp, t, cc, geff;
-};
-
-__host__ __device__ inline SbPos sb_decode(long long u, int ntiles, int nchunks, int gc) {
-  SbPos s;
-  long long per = (long long)ntiles * gc;
-  s.grp = (int)(u / per);
-  long long rem = u - (long long)s.grp * per;
-  s.geff = min(gc, nchunks - s.grp * gc);
-  s.t = (int)(rem / s.geff);
-  s.cc = (int)(rem - (long long)s.t * s.geff);
-  return s;
-}
-
-// CTA c of G owns super-blocks [cta_start(c), cta_start(c + 1)).
-__host__ __device__ inline long long cta_start(long long c, long long nsb, long long G) {
-  return nsb * c / G;
-}
-
-// Calls f(start_chunk) for every segment tile t is split into: its runs in each
-// chunk group, cut at CTA-range boundaries; in chunk order.
-template <class F>
-__device__ __forceinline__ int for_each_segment(int t, int ntiles, int nchunks, int gc,
-                                                int ngroups, long long nsb, long long G, F f) {
-  int n = 0;
-  for (int gr = 0; gr < ngroups; ++gr) {
-    const int geff = min(gc, nchunks - gr * gc);
-    const long long u0 = (long long)gr * ntiles * gc + (long long)t * geff, end = u0 + geff;
-    long long p = u0;
-    while (p < end) {
-      const long long c = ((p + 1) * G + nsb - 1) / nsb - 1;  // CTA whose range holds p
-      const long long e = cta_start(c + 1, nsb, G);
-      f(gr * gc + (int)(p - u0));
-      ++n;
-      p = e < end ? e : end;
-    }
-  }
-  return n;
-}
-
-constexpr int kFragLaneStride = 36;  // u32 per lane per chunk (32 + 4 pad: no bank conflicts)
-constexpr int kMaxStages = 4;
-constexpr int kSegList = 32;         // segment starts gathered per pass of a fix-up
-
-template <int M>
-__host__ __device__ constexpr int frag_chunk_u32() {
-  return 8 * M * kFragLaneStride;
-}
-// (group, tile) runs one CTA range may touch; the launcher sizes the grid so
-// that no CTA exceeds it.
-template <int M>
-__host__ __device__ constexpr int max_cta_runs() {
-  return M == 1 ? 16 : 4;
-}
-
 struct GemvSmem {
-  size_t ring, bars, frag, bsum, slots, red, misc, total;
+  size_t ring, bars, frag, side, parts, red, misc, total;
 };
 
 template <int QT, int M>
@@ -324,18 +194,36 @@ __host__ __device__ GemvSmem gemv_smem_layout(int gc, int nslots, int sbb, int s
   s.ring = (size_t)kGemvWarps * stages * sbb;
   s.bars = (size_t)kGemvWarps * kMaxStages * 8;
   s.frag = (size_t)nslots * gc * frag_chunk_u32<M>() * 4;
-  s.bsum = QT == MLB_Q4_1 ? (size_t)nslots * gc * 8 * M * 4 : 0;
-  s.slots = (size_t)max_cta_runs<M>() * kGemvWarps * 16 * M * 4;
+  s.side = (size_t)nslots * gc * side_per_chunk<QT, M>() * 4;
+  s.parts = (size_t)win_sbs<M>() * 16 * M * 4;
   s.red = (size_t)kGemvWarps * (16 * M + kSegList) * 4;
-  s.misc = 256 + (size_t)(max_cta_runs<M>() + 1) * 8 + (size_t)max_cta_runs<M>() * 12;
-  s.total = s.ring + s.bars + s.frag + s.bsum + s.slots + s.red + s.misc;
+  s.misc = 256 + (size_t)(kWinRuns + 1) * 4 + (size_t)kWinRuns * 12;
+  s.total = s.ring + s.bars + s.frag + s.side + s.parts + s.red + s.misc;
   return s;
 }
+
+// Lane 0's side of a warp's weight ring for one matrix: the warp's remaining
+// super-blocks cb + warp, cb + warp + 16, ... as a pointer walk.
+struct LinearRefill {
+  const uint8_t* next;
+  long long step;  // 16 super-blocks, in bytes
+  int left, sbb;
+  int inflight;    // copies issued and not yet consumed
+  uint8_t* ring;
+  uint64_t* bars;
+  __device__ __forceinline__ void operator()(int slot) {
+    if (left <= 0) return;
+    mbar_arrive_expect_tx(bars + slot, sbb);
+    bulk_g2s(ring + (size_t)slot * sbb, next, sbb, bars + slot);
+    next += step;
+    --left;
+    ++inflight;
+  }
+};
 
 template <int QT, int M, bool NORM>
 __global__ void __launch_bounds__(kGemvWarps * 32, 1) gemv_sb_kernel(const GemvKArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
-  constexpr int R = max_cta_runs<M>();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int sbb = a.sbb, S = a.stages;
   const int nslots = a.ngroups > 1 ? 2 : 1;
@@ -343,377 +231,85 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 1) gemv_sb_kernel(const GemvK
   uint8_t* ring = smem;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L.ring);
   uint32_t* frag = reinterpret_cast<uint32_t*>(smem + L.ring + L.bars);
-  float* bsum = reinterpret_cast<float*>(smem + L.ring + L.bars + L.frag);
-  float* slots = reinterpret_cast<float*>(smem + L.ring + L.bars + L.frag + L.bsum);
-  float* red = slots + L.slots / 4;
+  float* side = reinterpret_cast<float*>(smem + L.ring + L.bars + L.frag);
+  float* parts = reinterpret_cast<float*>(smem + L.ring + L.bars + L.frag + L.side);
+  float* red = parts + L.parts / 4;
   uint8_t* misc = reinterpret_cast<uint8_t*>(red + L.red / 4);
   float* inv_rms = reinterpret_cast<float*>(misc);            // [M]
   float* part = inv_rms + 4;                                   // [kGemvWarps]
   int* nruns_s = reinterpret_cast<int*>(part + kGemvWarps);    // [1]
-  long long* run_u0 = reinterpret_cast<long long*>(misc + 256);  // [R + 1]
-  int* run_t = reinterpret_cast<int*>(run_u0 + R + 1);         // [R]
-  int* run_grp = run_t + R;
-  int* run_cc0 = run_grp + R;
-  const int slot_u32 = a.gc * frag_chunk_u32<M>();
-  const int bsum_slot = a.gc * 8 * M;
+  int* ok_s = nruns_s + 1;                                     // [1]
+  RunTable rt;
+  rt.u0 = reinterpret_cast<int*>(misc + 256);                  // [kWinRuns + 1]
+  rt.t = reinterpret_cast<int*>(rt.u0 + kWinRuns + 1);         // [kWinRuns]
+  rt.grp = rt.t + kWinRuns;
+  rt.cc0 = rt.grp + kWinRuns;
 
-  const long long G = gridDim.x;
-  const long long cb = cta_start(blockIdx.x, a.nsb, G), ce = cta_start(blockIdx.x + 1, a.nsb, G);
+  const int G = gridDim.x;
+  const int cb = cta_start(blockIdx.x, G, a.ntiles, a.nchunks, a.gc, a.ngroups);
+  const int ce = cta_start(blockIdx.x + 1, G, a.ntiles, a.nchunks, a.gc, a.ngroups);
   uint64_t* mybars = bars + warp * kMaxStages;
   uint8_t* myring = ring + (size_t)warp * S * sbb;
 
   // 1. Barriers, then start streaming weights (independent of the previous
   //    kernel): warp w takes super-blocks cb + w, cb + w + 16, ...
+  LinearRefill refill;
+  refill.next = a.w + (size_t)(cb + warp) * sbb;
+  refill.step = (long long)kGemvWarps * sbb;
+  refill.left = cb + warp < ce ? (ce - cb - warp + kGemvWarps - 1) / kGemvWarps : 0;
+  refill.sbb = sbb;
+  refill.inflight = 0;
+  refill.ring = myring;
+  refill.bars = mybars;
   if (lane == 0) {
     for (int s = 0; s < S; ++s) mbar_init(&mybars[s], 1);
     fence_mbar_init();
     fence_proxy_async_smem();
+    for (int s = 0; s < S; ++s) refill(s);
   }
   __syncwarp();
-  if (lane == 0) {
-    for (int s = 0; s < S; ++s) {
-      const long long u = cb + warp + (long long)s * kGemvWarps;
-      if (u >= ce) break;
-      mbar_arrive_expect_tx(&mybars[s], sbb);
-      bulk_g2s(myring + (size_t)s * sbb, a.w + (size_t)u * sbb, sbb, &mybars[s]);
-    }
-  }
-  // The run table of this CTA range (no dependence on the previous kernel).
-  if (threadIdx.x == 0) {
-    long long u = cb;
-    int r = 0;
-    while (u < ce && r < R) {
-      const SbPos sp = sb_decode(u, a.ntiles, a.nchunks, a.gc);
-      const long long len = min((long long)(sp.geff - sp.cc), ce - u);
-      run_u0[r] = u;
-      run_t[r] = sp.t;
-      run_grp[r] = sp.grp;
-      run_cc0[r] = sp.cc;
-      u += len;
-      ++r;
-    }
-    run_u0[r] = u;
-    *nruns_s = (u < ce) ? -1 : r;  // -1: more runs than the launcher allowed
-  }
   // The next kernel may be scheduled as soon as an SM has room; it waits for
   // this grid to complete before reading anything this grid writes.
   pdl_launch_dependents();
   // 2. Inputs of the previous kernel are visible after this.
   pdl_wait();
+  if (cb >= ce) return;  // block-uniform; no copies were issued
+  const int g0 = sb_decode(cb, a.ntiles, a.nchunks, a.gc).grp;
+  const int g1 = sb_decode(ce - 1, a.ntiles, a.nchunks, a.gc).grp;
 
-  const int rows = a.rows;
-  if (NORM) {
-    // inv_rms[r] = 1 / sqrt(sum(x^2)/K + eps), src/ops.cc:55-61 (tree order).
-    for (int r = 0; r < rows; ++r) {
-      float ss = 0.0f;
-      const float* xr = a.x + (size_t)r * a.ldx;
-      if ((a.k & 3) == 0 && (((uintptr_t)xr) & 15) == 0) {
-        const float4* x4 = reinterpret_cast<const float4*>(xr);
-        for (int i = threadIdx.x; i < (a.k >> 2); i += blockDim.x) {
-          const float4 v = x4[i];
-          ss = fmaf(v.x, v.x, ss);
-          ss = fmaf(v.y, v.y, ss);
-          ss = fmaf(v.z, v.z, ss);
-          ss = fmaf(v.w, v.w, ss);
-        }
-      } else {
-        for (int i = threadIdx.x; i < a.k; i += blockDim.x) ss = fmaf(xr[i], xr[i], ss);
-      }
-      ss = warp_sum(ss);
-      if (lane == 0) part[warp] = ss;
-      __syncthreads();
-      if (threadIdx.x == 0) {
-        float t = 0.0f;
-        for (int w = 0; w < kGemvWarps; ++w) t += part[w];  // fixed order
-        t = __fdiv_rn(t, (float)a.k);
-        inv_rms[r] = __fdiv_rn(1.0f, sqrtf(__fadd_rn(t, a.eps)));
-      }
-      __syncthreads();
-    }
+  // 3. Stage x (normalised if fused) for the <= 2 chunk groups this CTA touches.
+  if (M == 1) {
+    stage_x_m1<QT>(a.x, a.k, NORM ? a.norm_w : nullptr, a.eps, a.gc, a.nchunks, g0, g1, frag,
+                   side, part, inv_rms);
   } else {
-    __syncthreads();  // run table visible
+    if (NORM) norm_inv_rms(a.x, a.ldx, a.rows, a.k, a.eps, part, inv_rms);
+    stage_x<QT, M>(a.x, a.ldx, a.rows, a.k, NORM ? a.norm_w : nullptr, inv_rms, a.gc, a.nchunks,
+                   g0, g1, frag, side);
   }
-  const int nruns = *nruns_s;
-  if (nruns < 0) {
-    if (threadIdx.x == 0 && a.status) {
-      atomicExch(&a.status->code, MLB_ERR_INVALID);
-      atomicExch(&a.status->where, 1);
-    }
-    return;
-  }
-  const int g0 = nruns > 0 ? run_grp[0] : 0;
-  const int g1 = nruns > 0 ? run_grp[nruns - 1] : -1;
 
-  // 3. Stage x (normalised if fused) for the <= 2 chunk groups this CTA touches,
-  //    in mma B-fragment order, split into fp16 hi + lo; zero the run slots.
-  for (int i = threadIdx.x; i < R * kGemvWarps * 16 * M; i += blockDim.x) slots[i] = 0.0f;
-  for (int j = 0; j <= g1 - g0; ++j) {
-    const int grp = g0 + j;
-    const int geff = min(a.gc, a.nchunks - grp * a.gc);
-    const int kbase = grp * a.gc * kChunkK;
-    uint32_t* fs = frag + j * slot_u32;
-    float* bs = bsum + j * bsum_slot;
-    // one thread per 4 consecutive inputs (2 B-fragment pairs); 8 consecutive
-    // threads cover one 32-input block, so Q4_1 block sums reduce by shuffles
-    const int quads = geff * 64 * M;
-    for (int idx = threadIdx.x; idx < quads; idx += blockDim.x) {
-      const int r = idx / (geff * 64);
-      const int rem = idx - r * geff * 64;
-      const int cc = rem >> 6, q4 = rem & 63;
-      const int k = kbase + cc * kChunkK + q4 * 4;
-      float v[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-      if (r < rows) {
-        const float* xr = a.x + (size_t)r * a.ldx;
-        if (k + 3 < a.k && ((((uintptr_t)(xr + k)) & 15) == 0)) {
-          const float4 t = *reinterpret_cast<const float4*>(xr + k);
-          v[0] = t.x; v[1] = t.y; v[2] = t.z; v[3] = t.w;
-        } else {
-          for (int e = 0; e < 4; ++e)
-            if (k + e < a.k) v[e] = xr[k + e];
-        }
-        if (NORM) {
-          const float sc = inv_rms[r];
-          for (int e = 0; e < 4; ++e)
-            if (k + e < a.k) v[e] = __fmul_rn(__fmul_rn(v[e], sc), a.norm_w[k + e]);
-        }
-      }
-      uint32_t* base = fs + cc * frag_chunk_u32<M>();
-#pragma unroll
-      for (int p2 = 0; p2 < 2; ++p2) {
-        const int kk = q4 * 4 + p2 * 2;  // even input index inside the chunk
-        const int st = kk >> 4, wv = kk & 15;
-        const int reg = wv >= 8, cl = (wv & 7) >> 1;
-        const __half h0 = __float2half_rn(v[2 * p2]), h1 = __float2half_rn(v[2 * p2 + 1]);
-        const __half l0 = __float2half_rn(v[2 * p2] - __half2float(h0));
-        const __half l1 = __float2half_rn(v[2 * p2 + 1] - __half2float(h1));
-        const int lane_hi = 4 * (2 * r) + cl, lane_lo = lane_hi + 4;
-        base[lane_hi * kFragLaneStride + st * 2 + reg] = h2_as_u32(__halves2half2(h0, h1));
-        base[lane_lo * kFragLaneStride + st * 2 + reg] = h2_as_u32(__halves2half2(l0, l1));
-      }
-      if (QT == MLB_Q4_1) {
-        float s4 = (v[0] + v[1]) + (v[2] + v[3]);
-        s4 += __shfl_xor_sync(0xffffffffu, s4, 1);
-        s4 += __shfl_xor_sync(0xffffffffu, s4, 2);
-        s4 += __shfl_xor_sync(0xffffffffu, s4, 4);
-        if ((q4 & 7) == 0) bs[(cc * 8 + (q4 >> 3)) * M + r] = s4;
-      }
-    }
-  }
-  __syncthreads();
-
-  // 4. Stream this warp's super-blocks, accumulating per run.
-  const int g = lane >> 2, cl = lane & 3;
-  const bool bl = lane < 8 * M;  // lanes carrying B-fragment columns
-  const int qbytes = QT == MLB_Q8_0 ? 4096 : 2048;
-  float acc0 = 0.0f, acc1 = 0.0f;
-  int b_chunk = -1, r = 0, last_r = -1;
-  uint32_t B[16][2];
-#pragma unroll
-  for (int s = 0; s < 16; ++s) B[s][0] = B[s][1] = 0u;
+  // 4. Windows of the range: stream, then finish their runs.
+  const FinishGeom fg{a.ntiles, a.nchunks, a.gc, a.ngroups, a.rows};
   int slot = 0;
   uint32_t parity = 0;
-  for (long long u = cb + warp; u < ce; u += kGemvWarps) {
-    while (u >= run_u0[r + 1]) ++r;
-    if (r != last_r) {
-      if (last_r >= 0 && cl < M) {
-        float* sl = slots + ((size_t)last_r * kGemvWarps + warp) * 16 * M;
-        sl[g * M + cl] = acc0;
-        sl[(g + 8) * M + cl] = acc1;
-      }
-      acc0 = acc1 = 0.0f;
-      last_r = r;
+  if (threadIdx.x == 0) *ok_s = 1;
+  for (int wb = cb; wb < ce;) {
+    if (threadIdx.x == 0)
+      *nruns_s = build_window(wb, ce, a.ntiles, a.nchunks, a.gc, kWinRuns, win_sbs<M>(), rt);
+    __syncthreads();  // run table (and the staged x) visible; parts free
+    const int nruns = *nruns_s;
+    const int we = rt.u0[nruns];
+    if (!consume_window<QT, M>(cb, wb, we, a.ntiles, a.nchunks, a.gc, g0, frag, side, parts,
+                               myring, mybars, sbb, S, slot, parity, refill.inflight, a.status,
+                               2, refill))
+      *ok_s = 0;  // every writer stores 0
+    __syncthreads();
+    if (!*ok_s) {  // a bounded wait gave up (status recorded): leave together
+      if (lane == 0) ring_drain(mybars, S, slot, parity, refill.inflight);
+      return;
     }
-    const int grp = run_grp[r];
-    const int cc = run_cc0[r] + (int)(u - run_u0[r]);
-    const int chunk = grp * a.gc + cc;
-    if (chunk != b_chunk) {
-      b_chunk = chunk;
-      if (bl) {
-        const uint32_t* fsrc =
-            frag + (grp - g0) * slot_u32 + cc * frag_chunk_u32<M>() + lane * kFragLaneStride;
-#pragma unroll
-        for (int s = 0; s < 8; ++s) {
-          uint4 v = *reinterpret_cast<const uint4*>(fsrc + s * 4);
-          B[2 * s][0] = v.x;
-          B[2 * s][1] = v.y;
-          B[2 * s + 1][0] = v.z;
-          B[2 * s + 1][1] = v.w;
-        }
-      }
-    }
-    if (!mbar_wait_bounded(&mybars[slot], parity, a.status, 2)) return;
-    const uint8_t* sb = myring + (size_t)slot * sbb;
-
-    // everything this lane needs from the super-block, as 16-byte loads
-    const uint4 sc0 = *reinterpret_cast<const uint4*>(sb + qbytes + g * 32);
-    const uint4 sc1 = *reinterpret_cast<const uint4*>(sb + qbytes + g * 32 + 16);
-    const uint32_t scw[8] = {sc0.x, sc0.y, sc0.z, sc0.w, sc1.x, sc1.y, sc1.z, sc1.w};
-    uint32_t mnw[8];
-    if (QT == MLB_Q4_1) {
-      const uint4 m0 = *reinterpret_cast<const uint4*>(sb + 2304 + g * 32);
-      const uint4 m1 = *reinterpret_cast<const uint4*>(sb + 2304 + g * 32 + 16);
-      mnw[0] = m0.x; mnw[1] = m0.y; mnw[2] = m0.z; mnw[3] = m0.w;
-      mnw[4] = m1.x; mnw[5] = m1.y; mnw[6] = m1.z; mnw[7] = m1.w;
-    }
-    constexpr int kQLoads = QT == MLB_Q8_0 ? 8 : 4;  // uint4 per lane per super-block
-    uint4 qv[kQLoads];
-#pragma unroll
-    for (int i = 0; i < kQLoads; ++i)
-      qv[i] = *reinterpret_cast<const uint4*>(sb + (size_t)(i * 32 + lane) * 16);
-
-#pragma unroll
-    for (int b = 0; b < 8; ++b) {
-      uint32_t A1[4], A2[4];
-      if (QT == MLB_Q8_0) {
-        const uint4 q = qv[b];
-        const __half2 bias = __float2half2_rn(1152.0f);
-        const uint32_t wx[4] = {q.x ^ 0x80808080u, q.y ^ 0x80808080u, q.z ^ 0x80808080u,
-                                q.w ^ 0x80808080u};
-        // wx[0]: row g (k 2c,2c+1,2c+8,2c+9), wx[1]: row g (+16), wx[2..3]: row g+8
-        A1[0] = h2_as_u32(__hsub2(u32_as_h2(__byte_perm(wx[0], 0x64646464u, 0x4140)), bias));
-        A1[2] = h2_as_u32(__hsub2(u32_as_h2(__byte_perm(wx[0], 0x64646464u, 0x4342)), bias));
-        A1[1] = h2_as_u32(__hsub2(u32_as_h2(__byte_perm(wx[2], 0x64646464u, 0x4140)), bias));
-        A1[3] = h2_as_u32(__hsub2(u32_as_h2(__byte_perm(wx[2], 0x64646464u, 0x4342)), bias));
-        A2[0] = h2_as_u32(__hsub2(u32_as_h2(__byte_perm(wx[1], 0x64646464u, 0x4140)), bias));
-        A2[2] = h2_as_u32(__hsub2(u32_as_h2(__byte_perm(wx[1], 0x64646464u, 0x4342)), bias));
-        A2[1] = h2_as_u32(__hsub2(u32_as_h2(__byte_perm(wx[3], 0x64646464u, 0x4140)), bias));
-        A2[3] = h2_as_u32(__hsub2(u32_as_h2(__byte_perm(wx[3], 0x64646464u, 0x4342)), bias));
-      } else {
-        const uint4 q = qv[b >> 1];
-        const uint32_t w0 = (b & 1) ? q.z : q.x, w1 = (b & 1) ? q.w : q.y;  // rows g, g+8
-        const uint32_t w0s = w0 >> 8, w1s = w1 >> 8;
-        const uint32_t M1 = 0x000F000Fu, M2 = 0x00F000F0u, E = 0x64006400u;
-        // low nibbles: 1024 + q ; high nibbles: 1024 + 16 q
-        const __half2 lo_off = __float2half2_rn(QT == MLB_Q4_0 ? 1032.0f : 1024.0f);
-        const __half2 hi_mul = __float2half2_rn(1.0f / 16.0f);
-        const __half2 hi_off = __float2half2_rn(QT == MLB_Q4_0 ? -72.0f : -64.0f);
-        A1[0] = h2_as_u32(__hsub2(u32_as_h2(lop3_and_or(w0, M1, E)), lo_off));
-        A1[1] = h2_as_u32(__hsub2(u32_as_h2(lop3_and_or(w1, M1, E)), lo_off));
-        A1[2] = h2_as_u32(__hsub2(u32_as_h2(lop3_and_or(w0s, M1, E)), lo_off));
-        A1[3] = h2_as_u32(__hsub2(u32_as_h2(lop3_and_or(w1s, M1, E)), lo_off));
-        A2[0] = h2_as_u32(__hfma2(u32_as_h2(lop3_and_or(w0, M2, E)), hi_mul, hi_off));
-        A2[1] = h2_as_u32(__hfma2(u32_as_h2(lop3_and_or(w1, M2, E)), hi_mul, hi_off));
-        A2[2] = h2_as_u32(__hfma2(u32_as_h2(lop3_and_or(w0s, M2, E)), hi_mul, hi_off));
-        A2[3] = h2_as_u32(__hfma2(u32_as_h2(lop3_and_or(w1s, M2, E)), hi_mul, hi_off));
-      }
-      float d[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-      mma_16816(d, A1, B[2 * b][0], B[2 * b][1]);
-      mma_16816(d, A2, B[2 * b + 1][0], B[2 * b + 1][1]);
-      const float2 sc = __half22float2(u32_as_h2(scw[b]));
-      acc0 = fmaf(sc.x, d[0] + d[1], acc0);
-      acc1 = fmaf(sc.y, d[2] + d[3], acc1);
-      if (QT == MLB_Q4_1) {
-        const float2 mn = __half22float2(u32_as_h2(mnw[b]));
-        const int rr = cl < M ? cl : 0;
-        const float sx = bsum[(grp - g0) * bsum_slot + (cc * 8 + b) * M + rr];
-        acc0 = fmaf(mn.x, sx, acc0);
-        acc1 = fmaf(mn.y, sx, acc1);
-      }
-    }
-    // All lanes have consumed the slot (their loads fed the MMAs above), so lane 0
-    // can refill it; the mbarrier protocol orders the bulk copy after the reads.
-    __syncwarp();
-    const long long un = u + (long long)S * kGemvWarps;
-    if (lane == 0 && un < ce) {
-      mbar_arrive_expect_tx(&mybars[slot], sbb);
-      bulk_g2s(myring + (size_t)slot * sbb, a.w + (size_t)un * sbb, sbb, &mybars[slot]);
-    }
-    if (++slot == S) {
-      slot = 0;
-      parity ^= 1u;
-    }
-  }
-  if (last_r >= 0 && cl < M) {
-    float* sl = slots + ((size_t)last_r * kGemvWarps + warp) * 16 * M;
-    sl[g * M + cl] = acc0;
-    sl[(g + 8) * M + cl] = acc1;
-  }
-  __syncthreads();
-
-  // 5. Finish the runs: sum the warps' slots in warp order; a run that is a
-  //    whole tile goes straight to the epilogue, a partial one joins the
-  //    tile's other segments through the workspace (last arriver sums them in
-  //    chunk order).
-  float* myred = red + warp * (16 * M + kSegList);
-  int* seglist = reinterpret_cast<int*>(myred + 16 * M);
-  for (int rr = warp; rr < nruns; rr += kGemvWarps) {
-    const int t = run_t[rr], grp = run_grp[rr];
-    const int geff = min(a.gc, a.nchunks - grp * a.gc);
-    const long long len = run_u0[rr + 1] - run_u0[rr];
-    for (int i = lane; i < 16 * M; i += 32) {
-      float s = 0.0f;
-      for (int w = 0; w < kGemvWarps; ++w) s += slots[((size_t)rr * kGemvWarps + w) * 16 * M + i];
-      myred[i] = s;
-    }
-    __syncwarp();
-    bool finish = a.ngroups == 1 && run_cc0[rr] == 0 && len == geff;
-    if (!finish) {
-      float* slotw = a.ws + ((size_t)t * a.nchunks + grp * a.gc + run_cc0[rr]) * 16 * M;
-      for (int i = lane; i < 16 * M; i += 32) slotw[i] = myred[i];
-      __threadfence();
-      __syncwarp();
-      int nseg = 0;
-      if (lane == 0)
-        nseg = for_each_segment(t, a.ntiles, a.nchunks, a.gc, a.ngroups, a.nsb, G, [](int) {});
-      int last = 0;
-      if (lane == 0) last = (atomicAdd(&a.counters[t], 1) == nseg - 1);
-      last = __shfl_sync(0xffffffffu, last, 0);
-      finish = last != 0;
-      if (finish) {
-        __threadfence();
-        float s[(16 * M + 31) / 32];
-#pragma unroll
-        for (int q = 0; q < (16 * M + 31) / 32; ++q) s[q] = 0.0f;
-        // gather the segment starts kSegList at a time, then sum with
-        // independent loads, in chunk order
-        int done = 0;
-        while (true) {
-          int cnt = 0;
-          if (lane == 0) {
-            int idx = 0;
-            for_each_segment(t, a.ntiles, a.nchunks, a.gc, a.ngroups, a.nsb, G, [&](int c) {
-              if (idx >= done && idx < done + kSegList) seglist[idx - done] = c;
-              ++idx;
-            });
-            cnt = min(kSegList, idx - done);
-          }
-          cnt = __shfl_sync(0xffffffffu, cnt, 0);
-          __syncwarp();
-          if (cnt <= 0) break;
-#pragma unroll
-          for (int q = 0; q < (16 * M + 31) / 32; ++q) {
-            const int i = lane + 32 * q;
-            if (i < 16 * M)
-              for (int j = 0; j < cnt; ++j)
-                s[q] += __ldcg(a.ws + ((size_t)t * a.nchunks + seglist[j]) * 16 * M + i);
-          }
-          done += cnt;
-          __syncwarp();
-          if (cnt < kSegList) break;
-        }
-#pragma unroll
-        for (int q = 0; q < (16 * M + 31) / 32; ++q) {
-          const int i = lane + 32 * q;
-          if (i < 16 * M) myred[i] = s[q];
-        }
-        if (lane == 0) a.counters[t] = 0;
-        __syncwarp();
-      }
-    }
-    if (finish) {
-      for (int i = lane; i < 16 * M; i += 32) {
-        int row = i / M, rb = i - row * M;
-        if (rb < rows) epilogue_row<M>(a.epi, t, row, rb, myred);
-      }
-      if (a.epi.argmax_key) {
-        unsigned long long key = 0ull;
-        if (lane < 16 && t * 16 + lane < a.epi.n_out)
-          key = argmax_key_of(myred[lane * M], a.epi.argmax_base + t * 16 + lane);
-        key = warp_max_u64(key);
-        if (lane == 0 && key) atomicMax(a.epi.argmax_key, key);
-      }
-    }
-    __syncwarp();
+    finish_runs<M>(parts, red, rt, nruns, wb, fg, a.ws, a.counters, a.epi);
+    __syncthreads();
+    wb = we;
   }
 }
 
@@ -792,42 +388,30 @@ __global__ void __launch_bounds__(256) gemv_f32_kernel(const float* w, int ntile
 
 static int pick_batch(int rows) { return rows <= 1 ? 1 : (rows == 2 ? 2 : 4); }
 
-// Largest number of (group, tile) runs, and of chunk groups, any CTA range
-// touches when the super-blocks are split over G CTAs.
-static void cta_span(const QMatrix& m, long long G, int* max_runs, int* max_groups) {
-  *max_runs = 0;
-  *max_groups = 0;
-  for (long long c = 0; c < G; ++c) {
-    long long u = cta_start(c, m.nsb, G);
-    const long long ce = cta_start(c + 1, m.nsb, G);
-    int runs = 0, g0 = -1, g1 = -1;
-    while (u < ce) {
-      const SbPos sp = sb_decode(u, m.ntiles, m.nchunks, m.gc);
-      if (g0 < 0) g0 = sp.grp;
-      g1 = sp.grp;
-      u += std::min((long long)(sp.geff - sp.cc), ce - u);
-      ++runs;
-    }
-    *max_runs = std::max(*max_runs, runs);
-    *max_groups = std::max(*max_groups, g0 < 0 ? 0 : g1 - g0 + 1);
+// Largest number of chunk groups any CTA range touches when the group-tiles
+// are split over G CTAs.
+static int cta_groups(const QMatrix& m, int G) {
+  int worst = 0;
+  for (int c = 0; c < G; ++c) {
+    const int u = cta_start(c, G, m.ntiles, m.nchunks, m.gc, m.ngroups);
+    const int ce = cta_start(c + 1, G, m.ntiles, m.nchunks, m.gc, m.ngroups);
+    if (u >= ce) continue;
+    const int g0 = sb_decode(u, m.ntiles, m.nchunks, m.gc).grp;
+    const int g1 = sb_decode(ce - 1, m.ntiles, m.nchunks, m.gc).grp;
+    worst = std::max(worst, g1 - g0 + 1);
   }
+  return worst;
 }
 
-// Grid for a matrix: one CTA per SM unless a CTA range would touch more runs
-// or chunk groups than its shared memory holds; then whole extra waves of
-// (smaller) CTAs, since only one CTA fits on an SM.
+// Grid for a matrix: one CTA per SM (at most one per group-tile), more when a
+// CTA range would touch more chunk groups than its staged activations hold.
 template <int M>
 static long long choose_grid(const QMatrix& m, int sms) {
   const int idx = M == 1 ? 0 : (M == 2 ? 1 : 2);
   if (m.grid_cache[idx] > 0) return m.grid_cache[idx];
-  long long G = std::min<long long>(std::max<long long>(sms, m.ngroups > 1 ? m.ngroups + 1 : 1),
-                                    m.nsb);
-  while (true) {
-    int runs = 0, groups = 0;
-    cta_span(m, G, &runs, &groups);
-    if ((runs <= max_cta_runs<M>() && groups <= 2) || G >= m.nsb) break;
-    G = std::min<long long>(m.nsb, (G / sms + 1) * sms);
-  }
+  const long long ngt = (long long)m.ngroups * m.ntiles;
+  long long G = std::min<long long>(sms, ngt);
+  while (G < ngt && cta_groups(m, (int)G) > 2) G = std::min<long long>(ngt, G + sms);
   m.grid_cache[idx] = (int)G;
   return G;
 }

@@ -24,6 +24,7 @@ constexpr int kTileRows = 16;
 constexpr int kChunkK = 256;
 constexpr int kGemvWarps = 16;  // warps per CTA, one CTA per SM
 constexpr int kMaxBatch = 4;  // batch rows one pass of the MMA GEMV carries
+constexpr int kMaxStages = 4;  // deepest per-warp weight ring
 
 inline int sb_bytes(int qtype) {
   return qtype == MLB_Q8_0 ? 4352 : (qtype == MLB_Q4_1 ? 2560 : 2304);

@@ -446,12 +446,18 @@ size_t ModelImpl::step_weight_bytes() const {
 
 // ---------------------------------------------------------------- context
 
+void ContextImpl::release_graphs() {
+  if (exec_greedy && exec_greedy != exec) cudaGraphExecDestroy(exec_greedy);
+  if (exec) cudaGraphExecDestroy(exec);
+  if (graph_greedy && graph_greedy != graph) cudaGraphDestroy(graph_greedy);
+  if (graph) cudaGraphDestroy(graph);
+  exec = exec_greedy = nullptr;
+  graph = graph_greedy = nullptr;
+}
+
 ContextImpl::~ContextImpl() {
   if (m) cudaSetDevice(m->device);
-  if (exec) cudaGraphExecDestroy(exec);
-  if (graph) cudaGraphDestroy(graph);
-  if (exec_greedy) cudaGraphExecDestroy(exec_greedy);
-  if (graph_greedy) cudaGraphDestroy(graph_greedy);
+  release_graphs();
   if (h_scalars) cudaFreeHost(h_scalars);
   if (h_logits) cudaFreeHost(h_logits);
   if (h_tokens) cudaFreeHost(h_tokens);
@@ -513,8 +519,180 @@ ContextImpl* context_create(ModelImpl& m, int mode) {
   MLB_CUDA(cudaMallocHost(&c->h_scalars, 4 * sizeof(int)));
   MLB_CUDA(cudaMallocHost(&c->h_logits, (size_t)cf.vocab_size * 4));
   MLB_CUDA(cudaMallocHost(&c->h_tokens, (size_t)cf.max_seq_len * 4));
+  c->plan_step();
+  c->use_step = c->step.ok;
   c->build_graph();
   return c.release();
+}
+
+// The phase list of one decode step for the persistent kernel, or the reason
+// it cannot run this model (then the per-op graph is used).
+void ContextImpl::plan_step() {
+  step = StepPlan{};
+  const mlb_config& cf = m->cfg;
+  const int D = cf.head_dim;
+  auto no = [&](const std::string& why) {
+    step.ok = false;
+    step.why = why;
+  };
+  if (m->tp_size != 1) return no("tensor-parallel steps use the per-op path");
+  std::string why;
+  if (!step_attn_ok(m->q_heads, m->kv_heads, D, &why)) return no(why);
+  const int grid = sm_count(m->device);
+  if (grid > 256) return no("more than 256 SMs");
+  const int qt = m->lm_head.qtype;
+  std::vector<const QMatrix*> mats;
+  for (const auto& L : m->layers) {
+    mats.push_back(&L.qkv);
+    mats.push_back(&L.wo);
+    mats.push_back(&L.gateup);
+    mats.push_back(&L.down);
+  }
+  mats.push_back(&m->lm_head);
+  int scratch = step_attn_scratch(m->q_heads / m->kv_heads, D);
+  for (const QMatrix* q : mats) {
+    if (q->qtype != qt) return no("projections of more than one quant type");
+    if (!step_gemv_ok(*q, grid, &why)) return no(why);
+    scratch = std::max(scratch, step_gemv_scratch(*q));
+  }
+  const int stride = sb_bytes(qt);
+  constexpr size_t kSmemMax = 227 * 1024;
+  int stages = 0;
+  for (int s = kMaxStages; s >= 2 && !stages; --s)
+    if (step_smem_bytes(scratch, stride, s) <= kSmemMax) stages = s;
+  if (!stages) return no("weight ring and scratch exceed shared memory");
+  const size_t smem = step_smem_bytes(scratch, stride, stages);
+  if (step_max_blocks_per_sm(qt, m->q_heads / m->kv_heads, smem) < 1)
+    return no("the step kernel does not fit on an SM");
+
+  // phases
+  const size_t layer_kv = (size_t)cf.max_seq_len * m->kv_heads * D;
+  std::vector<StepPhase> ph;
+  auto gemv = [&](const QMatrix& q, const float* x, const float* norm_w, const EpiParams& e) {
+    StepPhase p{};
+    p.kind = kPhaseGemv;
+    p.g.w = q.data;
+    p.g.sbb = sb_bytes(q.qtype);
+    p.g.ntiles = q.ntiles;
+    p.g.nchunks = q.nchunks;
+    p.g.gc = q.gc;
+    p.g.ngroups = q.ngroups;
+    p.g.nsb = q.nsb;
+    p.g.k = q.k;
+    p.g.x = x;
+    p.g.norm_w = norm_w;
+    p.g.eps = cf.rms_norm_eps;
+    p.g.epi = e;
+    ph.push_back(p);
+  };
+  int* d_pos = scalars.as<int>() + 1;
+  for (int l = 0; l < cf.n_layers; ++l) {
+    const LayerPlan& L = m->layers[l];
+    const float* x_in = l == 0 ? nullptr : xa.as<float>();  // null: embedding row
+    EpiParams e{};
+    e.kind = kEpiQkv;
+    e.q_rows = m->q_heads * D;
+    e.kv_rows = m->kv_heads * D;
+    e.k_off = L.qkv_k_off;
+    e.v_off = L.qkv_v_off;
+    e.head_dim = D;
+    e.neox = m->neox;
+    e.bias = L.bias.p ? L.bias.as<float>() : nullptr;
+    e.rope = m->rope.as<float2>();
+    e.pos = d_pos;
+    e.keys = keys.as<float>() + (size_t)l * layer_kv;
+    e.values = values.as<float>() + (size_t)l * layer_kv;
+    e.q_out = q.as<float>();
+    gemv(L.qkv, x_in, L.attn_norm.as<float>(), e);
+
+    StepPhase a{};
+    a.kind = kPhaseAttn;
+    a.at.q = q.as<float>();
+    a.at.keys = keys.as<float>() + (size_t)l * layer_kv;
+    a.at.values = values.as<float>() + (size_t)l * layer_kv;
+    a.at.out = attn.as<float>();
+    a.at.H = m->q_heads;
+    a.at.KV = m->kv_heads;
+    a.at.D = D;
+    a.at.scale = attn_scale(D);
+    a.at.include_current_v = attention_mode == MLB_ATTN_STANDARD;
+    ph.push_back(a);
+
+    EpiParams eo{};
+    eo.kind = kEpiResidual;
+    eo.y = xb.as<float>();
+    eo.resid = x_in;  // null: embedding row
+    eo.ldy = eo.ldr = cf.dim;
+    eo.n_out = cf.dim;
+    gemv(L.wo, attn.as<float>(), nullptr, eo);
+
+    EpiParams eg{};
+    eg.kind = kEpiSwiglu;
+    eg.y = hidden.as<float>();
+    eg.ldy = m->ffn_rows;
+    eg.n_out = m->ffn_rows;
+    gemv(L.gateup, xb.as<float>(), L.ffn_norm.as<float>(), eg);
+
+    EpiParams ed{};
+    ed.kind = kEpiResidual;
+    ed.y = xa.as<float>();
+    ed.resid = xb.as<float>();
+    ed.ldy = ed.ldr = cf.dim;
+    ed.n_out = cf.dim;
+    gemv(L.down, hidden.as<float>(), nullptr, ed);
+  }
+  EpiParams el{};
+  el.kind = kEpiStore;
+  el.y = logits.as<float>();
+  el.ldy = m->vocab_rows;
+  el.n_out = m->vocab_rows;
+  el.argmax_key = argmax_key.as<unsigned long long>();
+  el.argmax_base = 0;
+  gemv(m->lm_head, cf.n_layers == 0 ? nullptr : xa.as<float>(), m->final_norm.as<float>(), el);
+
+  step_phases.alloc(ph.size() * sizeof(StepPhase));
+  MLB_CUDA(cudaMemcpy(step_phases.p, ph.data(), ph.size() * sizeof(StepPhase),
+                      cudaMemcpyHostToDevice));
+  step_sync.alloc(2 * sizeof(unsigned int));
+  MLB_CUDA(cudaMemset(step_sync.p, 0, step_sync.bytes));
+  const int gq = m->q_heads / m->kv_heads;
+  step_attn_ws.alloc((size_t)2 * grid * gq * (D + 4) * 4);
+  step_attn_cnt.alloc((size_t)m->kv_heads * 4);
+  MLB_CUDA(cudaMemset(step_attn_cnt.p, 0, step_attn_cnt.bytes));
+  step.ok = true;
+  step.qtype = qt;
+  step.gq = gq;
+  step.grid = grid;
+  step.stages = stages;
+  step.sb_stride = stride;
+  step.scratch_bytes = scratch;
+  step.smem = smem;
+  step.nphases = (int)ph.size();
+  step.phases = step_phases.p;
+}
+
+void ContextImpl::launch_step(cudaStream_t s) {
+  StepArgs a{};
+  a.phases = static_cast<const StepPhase*>(step.phases);
+  a.nphases = step.nphases;
+  a.sb_stride = step.sb_stride;
+  a.stages = step.stages;
+  a.scratch_bytes = step.scratch_bytes;
+  a.embedding = m->embedding.as<float>();
+  a.dim = m->cfg.dim;
+  int* d_token = scalars.as<int>();
+  a.token = d_token;
+  a.pos = d_token + 1;
+  a.step = d_token + 2;
+  a.tokens = d_token + 4;
+  a.argmax_key = argmax_key.as<unsigned long long>();
+  a.ws = gemv_ws.as<float>();
+  a.counters = gemv_cnt.as<int>();
+  a.attn_ws = step_attn_ws.as<float>();
+  a.attn_counters = step_attn_cnt.as<int>();
+  a.sync = step_sync.as<unsigned int>();
+  a.status = status.as<DeviceStatus>();
+  step_launch(step, a, s);
 }
 
 // Ends a step: the greedy token of the fused argmax becomes the next input
@@ -539,6 +717,13 @@ void ContextImpl::record_step(cudaStream_t s, bool pdl, bool full_logits) {
   int* d_tokens = d_token + 4;
   const size_t layer_kv = (size_t)cf.max_seq_len * m->kv_heads * D;
   const float scale = attn_scale(D);
+  if (use_step) {
+    (void)pdl;
+    (void)full_logits;  // single GPU: the logits are always written
+    launch_step(s);
+    kernels_per_step = 1;
+    return;
+  }
   kernels_per_step = 0;
   op_embedding(m->embedding.as<float>(), cf.vocab_size, cf.dim, d_token, 0, xa.as<float>(), s, pdl);
   ++kernels_per_step;
@@ -654,6 +839,33 @@ void ContextImpl::record_step(cudaStream_t s, bool pdl, bool full_logits) {
 
 void ContextImpl::build_graph() {
   set_device(m->device);
+  release_graphs();
+  direct_launch = false;
+  if (use_step) {
+    // one kernel per step: a graph only saves its launch call; launch directly
+    // when the cooperative launch cannot be captured
+    cudaGraph_t g = nullptr;
+    MLB_CUDA(cudaStreamBeginCapture(stream, cudaStreamCaptureModeThreadLocal));
+    bool captured = true;
+    try {
+      record_step(stream, false, true);
+    } catch (...) {
+      captured = false;
+    }
+    cudaError_t e = cudaStreamEndCapture(stream, &g);
+    if (!captured || e != cudaSuccess || !g ||
+        cudaGraphInstantiate(&exec, g, 0) != cudaSuccess) {
+      cudaGetLastError();
+      if (g) cudaGraphDestroy(g);
+      exec = nullptr;
+      direct_launch = true;
+      kernels_per_step = 1;
+      return;
+    }
+    graph = g;
+    exec_greedy = exec;  // same step either way on one GPU
+    return;
+  }
   for (int full = 1; full >= 0; --full) {
     MLB_CUDA(cudaStreamBeginCapture(stream, cudaStreamCaptureModeThreadLocal));
     try {
@@ -670,10 +882,31 @@ void ContextImpl::build_graph() {
   }
 }
 
+void ContextImpl::replay(bool greedy) {
+  if (direct_launch)
+    launch_step(stream);
+  else
+    MLB_CUDA(cudaGraphLaunch(greedy ? exec_greedy : exec, stream));
+}
+
+void ContextImpl::set_use_step(bool on) {
+  if (on && !step.ok) invalid("decode step kernel unavailable: " + step.why);
+  set_device(m->device);
+  MLB_CUDA(cudaStreamSynchronize(stream));
+  use_step = on;
+  build_graph();
+}
+
 void ContextImpl::check_status() {
   DeviceStatus st{};
   MLB_CUDA(cudaMemcpy(&st, status.p, sizeof(st), cudaMemcpyDeviceToHost));
   if (st.code != 0) {
+    // a failed step may leave arrival counters and the argmax key mid-way
+    MLB_CUDA(cudaMemset(gemv_cnt.p, 0, gemv_cnt.bytes));
+    MLB_CUDA(cudaMemset(attn_cnt.p, 0, attn_cnt.bytes));
+    MLB_CUDA(cudaMemset(argmax_key.p, 0, argmax_key.bytes));
+    if (step_sync.p) MLB_CUDA(cudaMemset(step_sync.p, 0, step_sync.bytes));
+    if (step_attn_cnt.p) MLB_CUDA(cudaMemset(step_attn_cnt.p, 0, step_attn_cnt.bytes));
     MLB_CUDA(cudaMemset(status.p, 0, sizeof(st)));
     fail(st.code, "decode step: a device-side check failed (site " + std::to_string(st.where) + ")");
   }
@@ -692,7 +925,7 @@ void context_step_async(ContextImpl& c, int token, int pos) {
   c.h_scalars[1] = pos;
   c.h_scalars[2] = 0;
   MLB_CUDA(cudaMemcpyAsync(c.scalars.p, c.h_scalars, 3 * sizeof(int), cudaMemcpyHostToDevice, c.stream));
-  MLB_CUDA(cudaGraphLaunch(c.exec, c.stream));
+  c.replay(false);
 }
 
 void context_forward_token(ContextImpl& c, int token, int pos, float* logits_host) {
@@ -714,7 +947,7 @@ void context_decode_greedy(ContextImpl& c, int token, int pos, int n, int* token
   c.h_scalars[1] = pos;
   c.h_scalars[2] = 0;
   MLB_CUDA(cudaMemcpyAsync(c.scalars.p, c.h_scalars, 3 * sizeof(int), cudaMemcpyHostToDevice, c.stream));
-  for (int i = 0; i < n; ++i) MLB_CUDA(cudaGraphLaunch(c.exec_greedy, c.stream));
+  for (int i = 0; i < n; ++i) c.replay(true);
   MLB_CUDA(cudaMemcpyAsync(c.h_tokens, c.scalars.as<int>() + 4, (size_t)n * 4,
                            cudaMemcpyDeviceToHost, c.stream));
   MLB_CUDA(cudaStreamSynchronize(c.stream));

@@ -9,6 +9,7 @@
 
 #include "attention.cuh"
 #include "gemv.cuh"
+#include "step.cuh"
 
 namespace mlb {
 
@@ -86,8 +87,19 @@ struct ContextImpl {
   cudaGraphExec_t exec = nullptr;         // step that also leaves full logits on the device
   cudaGraphExec_t exec_greedy = nullptr;  // step that only produces the next token
   int kernels_per_step = 0;
+  // Persistent decode-step kernel (single GPU): plan, phase table, grid sync
+  // words and attention workspace. use_step selects it over the per-op graph.
+  StepPlan step;
+  DevBuf step_phases, step_sync, step_attn_ws, step_attn_cnt;
+  bool use_step = false;
+  bool direct_launch = false;  // step kernel launched without a graph
+  void plan_step();
   void build_graph();
   void record_step(cudaStream_t s, bool pdl, bool full_logits);
+  void launch_step(cudaStream_t s);
+  void release_graphs();
+  void replay(bool greedy);  // one step from the graph (or a direct launch)
+  void set_use_step(bool on);
   void check_status();
   ~ContextImpl();
 };

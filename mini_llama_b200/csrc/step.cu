@@ -1,0 +1,730 @@
+// step.cu — the persistent decode-step kernel.
+//
+// Reference: the device branch of ForwardToken / ForwardLayerDevice
+// (src/forward.cc:700-794), which issues, per layer, RMSNorm, three
+// projections, RoPE, a KV-cache write, attention, wo, a residual add,
+// RMSNorm, gate/up, SiLU*mul, down and a residual add as separate kernels with
+// device synchronisation in between.
+//
+// Here one cooperative launch of one CTA per SM (16 warps each) runs the
+// whole step as a list of phases: per layer the fused QKV projection (RMSNorm
+// prologue; bias, RoPE, q store, K/V cache write epilogue), attention, wo
+// (residual epilogue), fused gate/up (RMSNorm prologue, SiLU*mul epilogue),
+// down (residual epilogue); then the lm_head (final RMSNorm, logits, greedy
+// argmax) and the token/position update. The embedding row is read in place.
+//
+// Phases are separated by grid barriers, but the weight stream is not: every
+// warp owns a ring of shared-memory slots fed by cp.async.bulk, and its
+// producer walks the warp's super-blocks of ALL projection phases in order.
+// A slot freed in phase p is refilled with the next super-block the warp will
+// need, which may belong to phase p + 1 or later, so HBM keeps streaming
+// weights while the CTA waits at a barrier, stages activations or runs
+// attention. The arithmetic is the standalone GEMV's (gemv_dev.cuh), so
+// results are identical to the per-op path.
+//
+// Attention spreads the (KV head, position) pairs of the step evenly over the
+// CTAs. A CTA's share of one head is a "piece"; its 16 warps take blocks of
+// positions round robin, each keeping an online softmax (m, l, o) per query
+// head of the GQA group; the CTA combines its warps in warp order. A piece
+// that is a whole head writes the output; otherwise it leaves (m, l, o) in a
+// workspace slot and the last piece of the head to arrive combines all pieces
+// in position order. Deterministic, like the GEMV fix-ups.
+//
+// Every wait is bounded (about 2 s of clock64 polling): on timeout the kernel
+// records MLB_ERR_TIMEOUT in the status word, waits (bounded) for its own
+// bulk copies still in flight and returns; other CTAs see the status word at
+// their next barrier and return too. A launch that finds the status word set
+// does nothing.
+#include "step.cuh"
+
+#include <algorithm>
+#include <cstring>
+
+#include "gemv_dev.cuh"
+
+namespace mlb {
+
+namespace {
+
+constexpr int kStepWarps = kGemvWarps;  // 16
+constexpr int kStepThreads = kStepWarps * 32;
+constexpr int kMaxGrid = 256;
+constexpr long long kWaitCycles = 4000000000LL;
+
+// HG: query heads per pass over the positions (1, 2 or 4; groups of other
+// sizes run ceil(gq / HG) passes with the missing heads masked).
+template <int HG>
+struct AttnShape {
+  static constexpr int PB = 4;                // positions per warp block
+  static constexpr int NV = HG * PB;          // scores per block (<= 16)
+};
+
+// Shared state of one CTA besides the ring and the scratch region.
+struct StepShared {
+  StepPhase cur[2];  // this phase's descriptor and the next one's (prefetched)
+  float inv_rms[4];
+  float part[kStepWarps];
+  int run_u0[kWinRuns + 1];
+  int run_t[kWinRuns], run_grp[kWinRuns], run_cc0[kWinRuns];
+  int nruns;
+  int flag;
+  int pieces[kMaxGrid];
+};
+
+__device__ __forceinline__ unsigned int ld_acquire_u32(const unsigned int* p) {
+  unsigned int v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void record_error(DeviceStatus* st, int code, int where) {
+  if (atomicCAS(&st->code, 0, code) == 0) atomicExch(&st->where, where);
+}
+
+// Grid barrier over all CTAs of the launch (co-resident: cooperative launch).
+// The arrival counter only grows within a step; the step's last CTA resets it.
+// Returns false (block-uniform) when the wait timed out or another CTA
+// recorded an error.
+__device__ bool grid_barrier(unsigned int* counter, DeviceStatus* st, int where, int* flag) {
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    const unsigned int n = gridDim.x;
+    const unsigned int arrived = atomicAdd(counter, 1u) + 1u;
+    const unsigned int target = (arrived + n - 1u) / n * n;
+    const long long t0 = clock64();
+    int ok = 1;
+    while ((int)(ld_acquire_u32(counter) - target) < 0) {
+      if (*(volatile int*)&st->code != 0) {
+        ok = 0;
+        break;
+      }
+      if (clock64() - t0 > kWaitCycles) {
+        record_error(st, MLB_ERR_TIMEOUT, where);
+        ok = 0;
+        break;
+      }
+    }
+    __threadfence();
+    *flag = ok;
+  }
+  __syncthreads();
+  const int ok = *flag;
+  __syncthreads();
+  return ok != 0;
+}
+
+// ------------------------------------------------------------ weight ring
+
+// Per-warp ring of `stages` slots. Lane 0 issues copies; every lane tracks the
+// consumer position (slot, parity) identically.
+struct Ring {
+  uint8_t* base;     // this warp's slots
+  uint64_t* bars;    // this warp's barriers
+  int stride, stages;
+  int slot;
+  uint32_t parity;
+  int inflight;      // copies issued and not yet consumed (lane 0's count)
+};
+
+// The producer side: the next super-block this warp will need, over all
+// projection phases in order, as a pointer walk within each phase.
+struct Producer {
+  int p;               // phase of the next super-block (nphases: none left)
+  const uint8_t* next; // its address
+  long long step;      // 16 super-blocks of phase p, in bytes
+  int left;            // super-blocks of phase p left for this warp
+  int sbb;
+};
+
+__device__ __noinline__ void producer_seek(Producer& pr, const StepPhase* ph, int nph,
+                                           int warp) {
+  const int G = gridDim.x, c = blockIdx.x;
+  while (pr.p < nph) {
+    if (__ldg(&ph[pr.p].kind) == kPhaseGemv) {
+      const StepGemv& g = ph[pr.p].g;
+      const int nt = __ldg(&g.ntiles), nc = __ldg(&g.nchunks), gc = __ldg(&g.gc);
+      const int ng = __ldg(&g.ngroups);
+      const int cb = cta_start(c, G, nt, nc, gc, ng), ce = cta_start(c + 1, G, nt, nc, gc, ng);
+      if (cb + warp < ce) {
+        pr.sbb = __ldg(&g.sbb);
+        pr.next = reinterpret_cast<const uint8_t*>(__ldg(reinterpret_cast<const unsigned long long*>(
+                      &g.w))) + (size_t)(cb + warp) * pr.sbb;
+        pr.step = (long long)kStepWarps * pr.sbb;
+        pr.left = (ce - cb - warp + kStepWarps - 1) / kStepWarps;
+        return;
+      }
+    }
+    ++pr.p;
+  }
+}
+
+// Lane 0: the producer's next super-block into ring slot `slot`, if any is left.
+__device__ __forceinline__ void producer_issue(Producer& pr, Ring& rg, int slot,
+                                               const StepPhase* ph, int nph, int warp) {
+  if (pr.p >= nph) return;
+  uint64_t* bar = rg.bars + slot;
+  mbar_arrive_expect_tx(bar, pr.sbb);
+  bulk_g2s(rg.base + (size_t)slot * rg.stride, pr.next, pr.sbb, bar);
+  ++rg.inflight;
+  pr.next += pr.step;
+  if (--pr.left == 0) {
+    ++pr.p;
+    producer_seek(pr, ph, nph, warp);
+  }
+}
+
+struct StepRefill {
+  Producer* pr;
+  Ring* rg;
+  const StepPhase* ph;
+  int nph, warp;
+  __device__ __forceinline__ void operator()(int slot) {
+    producer_issue(*pr, *rg, slot, ph, nph, warp);
+  }
+};
+
+// ----------------------------------------------------------- GEMV phase
+
+struct GemvScratch {
+  uint32_t* frag;
+  float* side;
+  float* parts;
+  float* red;
+};
+
+template <int QT>
+__device__ __forceinline__ GemvScratch gemv_scratch(uint8_t* scratch, const StepGemv& g) {
+  const int nslots = g.ngroups > 1 ? 2 : 1;
+  GemvScratch s;
+  s.frag = reinterpret_cast<uint32_t*>(scratch);
+  s.side = reinterpret_cast<float*>(s.frag + (size_t)nslots * g.gc * frag_chunk_u32<1>());
+  s.parts = s.side + (size_t)nslots * g.gc * side_per_chunk<QT, 1>();
+  s.red = s.parts + (size_t)win_sbs<1>() * 16;
+  return s;
+}
+
+// Returns false (block-uniform) when a wait failed; the caller drains and exits.
+template <int QT>
+__device__ bool gemv_phase(StepShared& sh, StepPhase& cur, uint8_t* scratch, Ring& rg,
+                           Producer& pr, const StepArgs& a) {
+  const StepGemv& g = cur.g;
+  const int warp = threadIdx.x >> 5;
+  const int G = gridDim.x;
+  const int cb = cta_start(blockIdx.x, G, g.ntiles, g.nchunks, g.gc, g.ngroups);
+  const int ce = cta_start(blockIdx.x + 1, G, g.ntiles, g.nchunks, g.gc, g.ngroups);
+  if (cb >= ce) return true;
+  const GemvScratch sc = gemv_scratch<QT>(scratch, g);
+  const float* x = g.x ? g.x : a.embedding + (size_t)(*a.token) * a.dim;
+  const int g0 = sb_decode(cb, g.ntiles, g.nchunks, g.gc).grp;
+  const int g1 = sb_decode(ce - 1, g.ntiles, g.nchunks, g.gc).grp;
+  stage_x_m1<QT>(x, g.k, g.norm_w, g.eps, g.gc, g.nchunks, g0, g1, sc.frag, sc.side, sh.part,
+                 sh.inv_rms);
+  // residual of the first layer: the embedding row (patched before the first
+  // barrier below, read only after it)
+  if (threadIdx.x == 0 && g.epi.kind == kEpiResidual && g.epi.resid == nullptr)
+    cur.g.epi.resid = a.embedding + (size_t)(*a.token) * a.dim;
+  const EpiParams& epi = cur.g.epi;
+  RunTable rt{sh.run_u0, sh.run_t, sh.run_grp, sh.run_cc0};
+  const FinishGeom fg{g.ntiles, g.nchunks, g.gc, g.ngroups, 1};
+  StepRefill refill{&pr, &rg, a.phases, a.nphases, warp};
+
+  // The CTA range in windows; warp w keeps taking super-blocks cb + w,
+  // cb + w + 16, ... across windows (and its producer across phases).
+  for (int wb = cb; wb < ce;) {
+    if (threadIdx.x == 0)
+      sh.nruns = build_window(wb, ce, g.ntiles, g.nchunks, g.gc, kWinRuns, win_sbs<1>(), rt);
+    __syncthreads();  // run table (and, first time, the staged x) visible
+    const int nruns = sh.nruns;
+    const int we = sh.run_u0[nruns];
+    if (!consume_window<QT, 1>(cb, wb, we, g.ntiles, g.nchunks, g.gc, g0, sc.frag, sc.side,
+                               sc.parts, rg.base, rg.bars, rg.stride, rg.stages, rg.slot,
+                               rg.parity, rg.inflight, a.status, 20, refill))
+      sh.flag = 0;  // set to 1 at the phase start; every writer stores 0
+    __syncthreads();
+    if (!sh.flag) return false;  // block-uniform: read after the barrier
+    finish_runs<1>(sc.parts, sc.red, rt, nruns, wb, fg, a.ws, a.counters, epi);
+    __syncthreads();
+    wb = we;
+  }
+  return true;
+}
+
+// ------------------------------------------------------ attention phase
+
+// Sums NV values across the warp. On return v[0] of lane L holds the total of
+// value index L / (32 / NV) (NV a power of two <= 32): each round keeps half of
+// the remaining values and adds the partner lane's copy of that half.
+template <int NV>
+__device__ __forceinline__ void warp_multi_sum(float (&v)[NV], int lane) {
+  static_assert(NV >= 1 && NV <= 32 && (NV & (NV - 1)) == 0, "NV must be a power of two");
+#pragma unroll
+  for (int r = 0; r < 5; ++r) {
+    const int off = 16 >> r;
+    const int cnt = NV >> r;  // values still held (>= 1 once r >= log2 NV)
+    if (cnt > 1) {
+      const int half = cnt >> 1;
+      const bool upper = (lane & off) != 0;
+#pragma unroll
+      for (int i = 0; i < half; ++i) {
+        const float send = upper ? v[i] : v[i + half];
+        const float keep = upper ? v[i + half] : v[i];
+        v[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+      }
+    } else {
+      v[0] += __shfl_xor_sync(0xffffffffu, v[0], off);
+    }
+  }
+}
+
+// A softmax record (m, l, o[D]) is kRec(D) floats with o at offset kRecO, so
+// that o starts on a 16-byte boundary (D is a multiple of 4).
+constexpr int kRecO = 4;
+__host__ __device__ constexpr int attn_rec(int D) { return D + kRecO; }
+
+struct AttnScratch {
+  float* wpart;   // [warps][gq][attn_rec(D)]: m, l, -, -, o
+  float* sc;      // [warps][NV] scores, then probabilities
+  float* alpha;   // [warps][HG]
+  float* ew;      // [gq][kMaxGrid] combine weights
+  float* lw;      // [gq] combined l
+};
+
+template <int HG>
+__device__ __forceinline__ AttnScratch attn_scratch(uint8_t* scratch, int D, int gq) {
+  AttnScratch s;
+  s.wpart = reinterpret_cast<float*>(scratch);
+  s.sc = s.wpart + (size_t)kStepWarps * gq * attn_rec(D);
+  s.alpha = s.sc + kStepWarps * AttnShape<HG>::NV;
+  s.lw = s.alpha + kStepWarps * HG;
+  s.ew = s.lw + gq;
+  return s;
+}
+
+// Combines nrec records (m, l, o[D]) per query head into out[h][D] (o / l).
+// rec(h, i) returns the record's base pointer; ld reads a float of it. Block-
+// wide; ends synchronised.
+template <class RecF>
+__device__ __forceinline__ void attn_combine(const AttnScratch& s, int D, int gq, int nrec,
+                                             RecF rec, bool from_global, float* out) {
+  if ((int)threadIdx.x < gq) {
+    const int h = threadIdx.x;
+    float m = -INFINITY;
+    for (int i = 0; i < nrec; ++i) {
+      const float* r = rec(h, i);
+      m = fmaxf(m, from_global ? __ldcg(r) : r[0]);
+    }
+    float l = 0.0f;
+    for (int i = 0; i < nrec; ++i) {
+      const float* r = rec(h, i);
+      const float mi = from_global ? __ldcg(r) : r[0];
+      const float li = from_global ? __ldcg(r + 1) : r[1];
+      const float e = mi == -INFINITY ? 0.0f : expf(mi - m);
+      s.ew[h * kMaxGrid + i] = e;
+      l = fmaf(li, e, l);
+    }
+    s.lw[h] = l;
+  }
+  __syncthreads();
+  for (int idx = threadIdx.x; idx < gq * D; idx += kStepThreads) {
+    const int h = idx / D, d = idx - h * D;
+    float acc = 0.0f;
+    for (int i = 0; i < nrec; ++i) {
+      const float* r = rec(h, i) + kRecO + d;
+      acc = fmaf(from_global ? __ldcg(r) : r[0], s.ew[h * kMaxGrid + i], acc);
+    }
+    out[(size_t)h * D + d] = __fdiv_rn(acc, s.lw[h]);
+  }
+  __syncthreads();
+}
+
+// One warp: positions [t0, t1) of a piece of KV head kvh, blocks of PB
+// positions round robin over warps; online softmax per query head. Query
+// heads go HG at a time (each pass re-reads the block's K/V rows, from L2).
+template <int HG>
+__device__ __forceinline__ void attn_warp(const StepAttn& at, const AttnScratch& s, int gq,
+                                          int kvh, int t0, int t1, int v_end, int warp,
+                                          int lane) {
+  constexpr int PB = AttnShape<HG>::PB, NV = AttnShape<HG>::NV;
+  constexpr unsigned kNvMask = (1u << NV) - 1u;  // lanes < NV
+  const int D = at.D, nvec = D >> 2, rec = attn_rec(D);
+  const bool dl = lane < nvec;
+  const size_t row = (size_t)at.KV * D;
+  const float* kbase = at.keys + (size_t)kvh * D + 4 * lane;
+  const float* vbase = at.values + (size_t)kvh * D + 4 * lane;
+  float* scw = s.sc + warp * NV;
+  float* alw = s.alpha + warp * HG;
+  float* wp = s.wpart + (size_t)warp * gq * rec;
+#pragma unroll 1
+  for (int hg = 0; hg < gq; hg += HG) {
+    float4 q[HG], o[HG];
+#pragma unroll
+    for (int h = 0; h < HG; ++h) {
+      q[h] = (dl && hg + h < gq)
+                 ? __ldcg(reinterpret_cast<const float4*>(at.q + (size_t)(kvh * gq + hg + h) * D) +
+                          lane)
+                 : make_float4(0.f, 0.f, 0.f, 0.f);
+      o[h] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    // lane i < NV keeps (m, l) of query head hg + i / PB
+    float m_run = -INFINITY, l_run = 0.0f;
+    for (int tb = t0 + warp * PB; tb < t1; tb += kStepWarps * PB) {
+      float4 kx[PB], vx[PB];
+#pragma unroll
+      for (int j = 0; j < PB; ++j) {
+        const int t = tb + j;
+        kx[j] = (dl && t < t1) ? __ldcg(reinterpret_cast<const float4*>(kbase + (size_t)t * row))
+                               : make_float4(0.f, 0.f, 0.f, 0.f);
+        vx[j] = (dl && t < t1 && t < v_end)
+                    ? __ldcg(reinterpret_cast<const float4*>(vbase + (size_t)t * row))
+                    : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+      float dv[NV];
+#pragma unroll
+      for (int h = 0; h < HG; ++h)
+#pragma unroll
+        for (int j = 0; j < PB; ++j) {
+          float d = q[h].x * kx[j].x;
+          d = fmaf(q[h].y, kx[j].y, d);
+          d = fmaf(q[h].z, kx[j].z, d);
+          d = fmaf(q[h].w, kx[j].w, d);
+          dv[h * PB + j] = d;
+        }
+      warp_multi_sum<NV>(dv, lane);
+      if ((lane & (32 / NV - 1)) == 0) scw[lane / (32 / NV)] = dv[0];
+      __syncwarp();
+      if (lane < NV) {
+        const int j = lane % PB;
+        const int t = tb + j;
+        const float sc = t < t1 ? __fmul_rn(scw[lane], at.scale) : -INFINITY;
+        float bmax = sc;
+#pragma unroll
+        for (int off = 1; off < PB; off <<= 1)
+          bmax = fmaxf(bmax, __shfl_xor_sync(kNvMask, bmax, off));
+        const float mnew = fmaxf(m_run, bmax);
+        const float p = t < t1 ? expf(sc - mnew) : 0.0f;
+        float psum = p;
+#pragma unroll
+        for (int off = 1; off < PB; off <<= 1) psum += __shfl_xor_sync(kNvMask, psum, off);
+        const float al = m_run == -INFINITY ? 0.0f : expf(m_run - mnew);
+        l_run = fmaf(l_run, al, psum);
+        m_run = mnew;
+        scw[lane] = t < v_end ? p : 0.0f;  // softmax weight counted, V row summed below v_end
+        if (j == 0) alw[lane / PB] = al;
+      }
+      __syncwarp();
+#pragma unroll
+      for (int h = 0; h < HG; ++h) {
+        const float al = alw[h];
+        float4 acc = make_float4(o[h].x * al, o[h].y * al, o[h].z * al, o[h].w * al);
+#pragma unroll
+        for (int j = 0; j < PB; ++j) {
+          const float p = scw[h * PB + j];
+          acc.x = fmaf(p, vx[j].x, acc.x);
+          acc.y = fmaf(p, vx[j].y, acc.y);
+          acc.z = fmaf(p, vx[j].z, acc.z);
+          acc.w = fmaf(p, vx[j].w, acc.w);
+        }
+        o[h] = acc;
+      }
+      __syncwarp();
+    }
+    // this warp's record per query head of the pass
+    if (lane < NV && lane % PB == 0 && hg + lane / PB < gq) {
+      wp[(hg + lane / PB) * rec] = m_run;
+      wp[(hg + lane / PB) * rec + 1] = l_run;
+    }
+    if (dl) {
+#pragma unroll
+      for (int h = 0; h < HG; ++h)
+        if (hg + h < gq)
+          *reinterpret_cast<float4*>(wp + (hg + h) * rec + kRecO + 4 * lane) = o[h];
+    }
+  }
+}
+
+template <int HG>
+__device__ bool attn_phase(StepShared& sh, const StepPhase& cur, uint8_t* scratch,
+                           const StepArgs& a) {
+  const StepAttn& at = cur.at;
+  const int D = at.D, rec = attn_rec(D);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int pos = *a.pos;
+  const int n = pos + 1;
+  const int v_end = at.include_current_v ? (int)n : pos;
+  const int G = gridDim.x, c = blockIdx.x;
+  const int total = at.KV * n;  // 32-bit: KV * max_seq * grid stays below 2^31
+  const int s0 = total * c / G, s1 = total * (c + 1) / G;
+  const int gq = at.H / at.KV;
+  const AttnScratch s = attn_scratch<HG>(scratch, D, gq);
+  for (int sp = s0; sp < s1;) {
+    const int kvh = sp / n;
+    const int t0 = sp - kvh * n;
+    const int t1 = min(n, s1 - kvh * n);
+    attn_warp<HG>(at, s, gq, kvh, t0, t1, v_end, warp, lane);
+    __syncthreads();
+    const bool whole = t0 == 0 && t1 == n;
+    float* out = at.out + (size_t)kvh * gq * D;
+    if (whole) {
+      attn_combine(s, D, gq, kStepWarps,
+                   [&](int h, int i) { return s.wpart + ((size_t)i * gq + h) * rec; }, false, out);
+    } else {
+      // this piece's record: combine the warps, unnormalised (m, l, o)
+      const int slot = 2 * (int)c + (sp != s0 ? 1 : 0);
+      float* dst = a.attn_ws + (size_t)slot * gq * rec;
+      if ((int)threadIdx.x < gq) {
+        const int h = threadIdx.x;
+        float m = -INFINITY;
+        for (int i = 0; i < kStepWarps; ++i) m = fmaxf(m, s.wpart[((size_t)i * gq + h) * rec]);
+        float l = 0.0f;
+        for (int i = 0; i < kStepWarps; ++i) {
+          const float* r = s.wpart + ((size_t)i * gq + h) * rec;
+          const float e = r[0] == -INFINITY ? 0.0f : expf(r[0] - m);
+          s.ew[h * kMaxGrid + i] = e;
+          l = fmaf(r[1], e, l);
+        }
+        dst[h * rec] = m;
+        dst[h * rec + 1] = l;
+      }
+      __syncthreads();
+      for (int idx = threadIdx.x; idx < gq * D; idx += kStepThreads) {
+        const int h = idx / D, d = idx - h * D;
+        float acc = 0.0f;
+        for (int i = 0; i < kStepWarps; ++i)
+          acc = fmaf(s.wpart[((size_t)i * gq + h) * rec + kRecO + d], s.ew[h * kMaxGrid + i],
+                     acc);
+        dst[h * rec + kRecO + d] = acc;
+      }
+      __threadfence();
+      __syncthreads();
+      if (threadIdx.x == 0) {
+        // pieces of this head: CTA ranges cut [kvh n, (kvh + 1) n)
+        int np = 0;
+        int p = kvh * n;
+        const int he = p + n;
+        while (p < he) {
+          const int cc = ((p + 1) * G + total - 1) / total - 1;  // CTA holding p
+          const int cs = total * cc / G, ce = total * (cc + 1) / G;
+          sh.pieces[np++] = 2 * (int)cc + (p != cs ? 1 : 0);
+          p = ce < he ? ce : he;
+        }
+        sh.nruns = np;
+        sh.flag = atomicAdd(&a.attn_counters[kvh], 1) == np - 1;
+      }
+      __syncthreads();
+      if (sh.flag) {
+        __threadfence();
+        const int np = sh.nruns;
+        attn_combine(
+            s, D, gq, np,
+            [&](int h, int i) { return a.attn_ws + ((size_t)sh.pieces[i] * gq + h) * rec; }, true,
+            out);
+        if (threadIdx.x == 0) a.attn_counters[kvh] = 0;
+      }
+      __syncthreads();
+    }
+    sp = kvh * n + t1;
+  }
+  return true;
+}
+
+// ---------------------------------------------------------------- kernel
+
+template <int QT, int HG>
+__global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const StepArgs a) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  uint8_t* ring_base = smem;
+  uint64_t* bars =
+      reinterpret_cast<uint64_t*>(smem + (size_t)kStepWarps * a.stages * a.sb_stride);
+  uint8_t* scratch = reinterpret_cast<uint8_t*>(bars + kStepWarps * kMaxStages);
+  StepShared& sh = *reinterpret_cast<StepShared*>(scratch + a.scratch_bytes);
+  // an earlier step failed: do nothing (one read, shared by the block)
+  if (threadIdx.x == 0) sh.flag = *(volatile int*)&a.status->code;
+  __syncthreads();
+  if (sh.flag != 0) return;
+  __syncthreads();
+
+  Ring rg;
+  rg.base = ring_base + (size_t)warp * a.stages * a.sb_stride;
+  rg.bars = bars + warp * kMaxStages;
+  rg.stride = a.sb_stride;
+  rg.stages = a.stages;
+  rg.slot = 0;
+  rg.parity = 0;
+  rg.inflight = 0;
+  Producer pr;
+  pr.p = 0;
+  if (lane == 0) {
+    for (int s = 0; s < a.stages; ++s) mbar_init(&rg.bars[s], 1);
+    fence_mbar_init();
+    fence_proxy_async_smem();
+    producer_seek(pr, a.phases, a.nphases, warp);
+    for (int s = 0; s < a.stages; ++s) producer_issue(pr, rg, s, a.phases, a.nphases, warp);
+  }
+  __syncwarp();
+
+  // Phase descriptors: the first one now, each later one prefetched with
+  // cp.async while the phase before it runs (complete and visible after that
+  // phase's grid barrier).
+  constexpr int kDesc16 = (int)(sizeof(StepPhase) / 16);
+  for (int i = threadIdx.x; i < kDesc16; i += kStepThreads)
+    reinterpret_cast<int4*>(&sh.cur[0])[i] = __ldg(reinterpret_cast<const int4*>(a.phases) + i);
+  bool ok = true;
+  for (int p = 0; p < a.nphases && ok; ++p) {
+    StepPhase& cur = sh.cur[p & 1];
+    if (threadIdx.x == 0) sh.flag = 1;
+    __syncthreads();
+    if (p + 1 < a.nphases) {
+      const int4* src = reinterpret_cast<const int4*>(a.phases + p + 1);
+      int4* dst = reinterpret_cast<int4*>(&sh.cur[(p + 1) & 1]);
+      for (int i = threadIdx.x; i < kDesc16; i += kStepThreads) cp_async16(dst + i, src + i);
+      cp_async_commit();
+    }
+    if (cur.kind == kPhaseGemv)
+      ok = gemv_phase<QT>(sh, cur, scratch, rg, pr, a);
+    else
+      ok = attn_phase<HG>(sh, cur, scratch, a);
+    cp_async_wait_all();
+    if (ok && p + 1 < a.nphases) ok = grid_barrier(&a.sync[0], a.status, 100 + p, &sh.flag);
+  }
+  if (!ok) {
+    if (lane == 0) ring_drain(rg.bars, rg.stages, rg.slot, rg.parity, rg.inflight);
+    return;
+  }
+  // End of step: the last CTA to finish publishes the greedy token and
+  // advances the position (step_finalize_kernel's job on the per-op path).
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    if (atomicAdd(&a.sync[1], 1u) == gridDim.x - 1) {
+      __threadfence();
+      const unsigned long long key = atomicOr(a.argmax_key, 0ull);
+      const int t = argmax_index_of(key);
+      *a.token = t;
+      a.tokens[*a.step] = t;
+      *a.step += 1;
+      *a.pos += 1;
+      *a.argmax_key = 0ull;
+      a.sync[0] = 0u;
+      a.sync[1] = 0u;
+      __threadfence();
+    }
+  }
+}
+
+// Pass width for a GQA group size: 1 and 2 exactly, 4 for every larger group.
+int pass_heads(int gq) { return gq <= 2 ? gq : 4; }
+
+template <int QT>
+void* pick_kernel(int hg) {
+  switch (hg) {
+    case 1: return (void*)decode_step_kernel<QT, 1>;
+    case 2: return (void*)decode_step_kernel<QT, 2>;
+    default: return (void*)decode_step_kernel<QT, 4>;
+  }
+}
+
+void* step_kernel_ptr(int qtype, int gq) {
+  const int hg = pass_heads(gq);
+  if (qtype == MLB_Q4_0) return pick_kernel<MLB_Q4_0>(hg);
+  if (qtype == MLB_Q4_1) return pick_kernel<MLB_Q4_1>(hg);
+  return pick_kernel<MLB_Q8_0>(hg);
+}
+
+size_t round_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+}  // namespace
+
+size_t step_smem_bytes(int scratch_bytes, int sb_stride, int stages) {
+  return (size_t)kStepWarps * stages * sb_stride + (size_t)kStepWarps * kMaxStages * 8 +
+         (size_t)scratch_bytes + round_up(sizeof(StepShared), 16);
+}
+
+int step_gemv_scratch(const QMatrix& m) {
+  const int nslots = m.ngroups > 1 ? 2 : 1;
+  size_t b = (size_t)nslots * m.gc * frag_chunk_u32<1>() * 4;
+  b += (size_t)nslots * m.gc * 8 * 4 * (m.qtype == MLB_Q4_1 ? 2 : 1);  // side data
+  b += (size_t)win_sbs<1>() * 16 * 4;  // super-block partials
+  b += (size_t)kStepWarps * (16 + kSegList) * 4;
+  return (int)round_up(b, 128);
+}
+
+int step_attn_scratch(int gq, int D) {
+  const int hg = pass_heads(gq), nv = hg * 4;
+  size_t b = (size_t)kStepWarps * gq * attn_rec(D) * 4 + (size_t)kStepWarps * nv * 4 +
+             (size_t)kStepWarps * hg * 4 + (size_t)gq * 4 + (size_t)gq * kMaxGrid * 4;
+  return (int)round_up(b, 128);
+}
+
+bool step_gemv_ok(const QMatrix& m, int grid, std::string* why) {
+  if (m.qtype != MLB_Q4_0 && m.qtype != MLB_Q4_1 && m.qtype != MLB_Q8_0) {
+    *why = "a projection is not Q4_0/Q4_1/Q8_0";
+    return false;
+  }
+  // at most two chunk groups per CTA range (the staged activations)
+  for (long long c = 0; c < grid; ++c) {
+    const int cb = cta_start((int)c, grid, m.ntiles, m.nchunks, m.gc, m.ngroups);
+    const int ce = cta_start((int)c + 1, grid, m.ntiles, m.nchunks, m.gc, m.ngroups);
+    if (cb >= ce) continue;
+    const int g0 = sb_decode(cb, m.ntiles, m.nchunks, m.gc).grp;
+    const int g1 = sb_decode(ce - 1, m.ntiles, m.nchunks, m.gc).grp;
+    if (g1 - g0 > 1) {
+      *why = "a CTA range spans more than two chunk groups";
+      return false;
+    }
+  }
+  return true;
+}
+
+bool step_attn_ok(int H, int KV, int D, std::string* why) {
+  const int gq = H / KV;
+  if (D % 4 != 0 || D > 128) {
+    *why = "head_dim must be a multiple of 4 and at most 128";
+    return false;
+  }
+  if (step_attn_scratch(gq, D) > 160 * 1024) {
+    *why = "the GQA group is too large for the attention scratch";
+    return false;
+  }
+  return true;
+}
+
+void step_launch(const StepPlan& plan, const StepArgs& args, cudaStream_t stream) {
+  if (!plan.ok) invalid("decode step kernel: " + plan.why);
+  if (plan.grid > kMaxGrid) invalid("decode step kernel: grid too large");
+  void* fn = step_kernel_ptr(plan.qtype, plan.gq);
+  int dev = 0;
+  MLB_CUDA(cudaGetDevice(&dev));
+  static size_t smem_set[64][3][3] = {};
+  const int qi = plan.qtype == MLB_Q4_0 ? 0 : (plan.qtype == MLB_Q4_1 ? 1 : 2);
+  const int gi = pass_heads(plan.gq) == 1 ? 0 : (pass_heads(plan.gq) == 2 ? 1 : 2);
+  if (dev < 64 && smem_set[dev][qi][gi] < plan.smem) {
+    MLB_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  (int)plan.smem));
+    smem_set[dev][qi][gi] = plan.smem;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)plan.grid);
+  cfg.blockDim = dim3(kStepThreads);
+  cfg.dynamicSmemBytes = plan.smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  void* params[] = {const_cast<StepArgs*>(&args)};
+  MLB_CUDA(cudaLaunchKernelExC(&cfg, fn, params));
+}
+
+// Checks done once per context: the step kernel's block fits one per SM.
+int step_max_blocks_per_sm(int qtype, int gq, size_t smem) {
+  void* fn = step_kernel_ptr(qtype, gq);
+  MLB_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  int n = 0;
+  MLB_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, fn, kStepThreads, smem));
+  return n;
+}
+
+}  // namespace mlb

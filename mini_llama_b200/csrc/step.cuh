@@ -1,0 +1,92 @@
+// step.cuh — the persistent decode-step kernel (host-side interface).
+//
+// One cooperative launch computes a whole decode step of a single-GPU model:
+// every quantised projection, attention, the lm_head with the greedy argmax,
+// and the token/position update. The grid is one CTA per SM; ops are phases
+// separated by grid barriers, and each warp's weight stream runs ahead across
+// phase boundaries (see step.cu).
+#pragma once
+
+#include "gemv.cuh"
+
+namespace mlb {
+
+enum StepPhaseKind : int { kPhaseGemv = 0, kPhaseAttn = 1 };
+
+struct StepGemv {
+  const uint8_t* w;     // super-block array
+  int sbb;              // bytes per super-block
+  int ntiles, nchunks, gc, ngroups;
+  long long nsb;
+  int k;
+  const float* x;       // activation row; null = the embedding row of the step's token
+  const float* norm_w;  // fused RMSNorm of x when non-null
+  float eps;
+  EpiParams epi;        // kEpiResidual with resid null: residual = the embedding row
+};
+
+struct StepAttn {
+  const float* q;       // [H][D]
+  const float* keys;    // layer base of the cache [max_seq][KV][D]
+  const float* values;
+  float* out;           // [H][D]
+  int H, KV, D;
+  float scale;
+  int include_current_v;
+};
+
+struct alignas(16) StepPhase {  // copied into shared memory 16 bytes at a time
+  int kind;
+  StepGemv g;
+  StepAttn at;
+};
+
+struct StepArgs {
+  const StepPhase* phases;  // device array
+  int nphases;
+  int sb_stride;            // bytes per ring slot (largest super-block)
+  int stages;               // ring slots per warp
+  int scratch_bytes;        // per-phase shared scratch
+  const float* embedding;
+  int dim;
+  int* token;               // device scalars of the context
+  int* pos;
+  int* step;
+  int* tokens;
+  unsigned long long* argmax_key;
+  float* ws;                // GEMV fix-up partials
+  int* counters;            // GEMV fix-up arrival counters (zero between phases)
+  float* attn_ws;           // attention piece records [2 * grid][gq][D + 4]
+  int* attn_counters;       // [KV] (zero between phases)
+  unsigned int* sync;       // [0] grid-barrier arrivals, [1] end-of-step arrivals
+  DeviceStatus* status;
+};
+
+// Launch plan of the step kernel for one context.
+struct StepPlan {
+  bool ok = false;
+  std::string why;          // reason the step kernel is not used, when !ok
+  int qtype = 0, gq = 0, grid = 0, stages = 0, sb_stride = 0, scratch_bytes = 0;
+  size_t smem = 0;
+  int nphases = 0;
+  void* phases = nullptr;   // device StepPhase array (owned by the context)
+  size_t attn_ws_floats = 0;
+};
+
+// Shared memory the step kernel needs for a scratch size and ring shape.
+size_t step_smem_bytes(int scratch_bytes, int sb_stride, int stages);
+// Scratch one GEMV phase needs (staged x, run slots, reduction space).
+int step_gemv_scratch(const QMatrix& m);
+// Scratch the attention phase needs.
+int step_attn_scratch(int gq, int D);
+// Whether a matrix can be a phase of the step kernel on `grid` CTAs (at most
+// two chunk groups per CTA range); otherwise sets why.
+bool step_gemv_ok(const QMatrix& m, int grid, std::string* why);
+bool step_attn_ok(int H, int KV, int D, std::string* why);
+
+// Launches one step (cooperative launch, capturable in a CUDA graph).
+void step_launch(const StepPlan& plan, const StepArgs& args, cudaStream_t stream);
+// Resident blocks of the step kernel per SM with `smem` bytes of shared memory.
+int step_max_blocks_per_sm(int qtype, int gq, size_t smem);
+
+}  // namespace mlb

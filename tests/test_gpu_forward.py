@@ -19,6 +19,8 @@ pytestmark = pytest.mark.gpu
 
 LOGIT_TOL = 2e-3
 README_TOKENS = [23, 58, 36] + [59] * 61  # README.md:297
+# how a decode step runs: the persistent step kernel, or one kernel per op
+PATHS = ["step", "per_op"]
 
 
 def meta():
@@ -30,6 +32,14 @@ def gpu_model(cfg, weights, **kw):
     m = mlb.CudaModel(cfg, **kw)
     m.load(weights)
     return m
+
+
+def make_ctx(model, path, mode=mlb.ATTN_CPU_COMPAT):
+    ctx = model.context(mode, step_kernel=(path == "step"))
+    assert ctx.step_kernel() == (path == "step")
+    if path == "step":
+        assert ctx.kernels_per_step() == 1
+    return ctx
 
 
 def greedy(ctx, prompt, steps, teacher=None):
@@ -66,8 +76,9 @@ def test_readme_model_greedy_tokens(cuda):
     assert np.abs(logits - g["logits"]).max() <= LOGIT_TOL
 
 
+@pytest.mark.parametrize("path", PATHS)
 @pytest.mark.parametrize("name", ["small_q4_0_gqa", "small_q4_1_neox_bias", "small_q8_0_ragged"])
-def test_small_models_vs_reference(cuda, name):
+def test_small_models_vs_reference(cuda, name, path):
     mt = meta()[name]
     g = np.load(golden_path(f"{name}.npz"))
     qtype = {v: k for k, v in C.QTYPE_NAMES.items()}[mt["qtype"]]
@@ -77,22 +88,23 @@ def test_small_models_vs_reference(cuda, name):
     steps = len(g["tokens"]) - len(prompt)
     gold = [int(t) for t in g["tokens"]]
     # teacher-forced: every step sees the reference's token
-    logits, toks = greedy(model.context(), prompt, steps, teacher=gold)
+    logits, toks = greedy(make_ctx(model, path), prompt, steps, teacher=gold)
     err = np.abs(logits - g["logits"]).max(axis=1)
     assert err.max() <= LOGIT_TOL, err
     # free-running greedy: token ids bit-exact
-    _, toks2 = greedy(model.context(), prompt, steps)
+    _, toks2 = greedy(make_ctx(model, path), prompt, steps)
     assert toks2 == gold
 
 
-def test_tiny_config_greedy_parity(cuda):
+@pytest.mark.parametrize("path", PATHS)
+def test_tiny_config_greedy_parity(cuda, path):
     """Tiny LLaMA (dim 288, 6 layers, vocab 32000, Q8_0): 16 prompt ids then 128
     greedy steps, token ids bit-exact against the reference CPU path."""
     mt = meta()["tiny_q8_0"]
     g = np.load(golden_path("tiny_q8_0.npz"))
     model = mlb.CudaModel(C.TINY).synthesize(C.Q8_0, mt["seed"])
     prompt = [int(t) for t in g["prompt"]]
-    logits, toks = greedy(model.context(), prompt, 128)
+    logits, toks = greedy(make_ctx(model, path), prompt, 128)
     gold = [int(t) for t in g["tokens"]]
     if toks != gold:
         i = next(i for i, (a, b) in enumerate(zip(toks, gold)) if a != b)
@@ -101,7 +113,7 @@ def test_tiny_config_greedy_parity(cuda):
     for i, s in enumerate(g["logit_steps"]):
         assert np.abs(logits[s] - g["logits"][i]).max() <= LOGIT_TOL
     # the on-device greedy loop (one graph launch per step) gives the same ids
-    ctx = model.context()
+    ctx = make_ctx(model, path)
     for pos, t in enumerate(prompt[:-1]):
         ctx.forward_token(t, pos)
     dev = ctx.decode_greedy(prompt[-1], len(prompt) - 1, 129)
@@ -143,7 +155,8 @@ def test_standard_attention_mode_differs_only_in_v_sum(cuda, port):
     assert not np.array_equal(la, lb)  # pos 0: the CPU path sums no V row at all
 
 
-def test_long_context_step(cuda, port):
+@pytest.mark.parametrize("path", PATHS)
+def test_long_context_step(cuda, port, path):
     """A step deep into the context (many attention splits) against the oracle."""
     cfg = dict(meta()["small_q4_0_gqa"]["config"], max_seq_len=1024)
     ws = list(C.host_weights(cfg, C.Q4_0, 4))
@@ -151,7 +164,7 @@ def test_long_context_step(cuda, port):
     pm = port.model(cfg)
     for kind, layer, qtype, rows, cols, arr in ws:
         pm.set_weight(kind, layer, qtype, rows, cols, arr)
-    ctx = gm.context()
+    ctx = make_ctx(gm, path)
     rng = np.random.default_rng(0)
     toks = rng.integers(0, cfg["vocab_size"], 700)
     for pos, t in enumerate(toks):
@@ -159,3 +172,51 @@ def test_long_context_step(cuda, port):
         lp = pm.forward_token(int(t), pos)
         if pos % 97 == 0 or pos == len(toks) - 1:
             assert np.abs(lg - lp).max() <= LOGIT_TOL, pos
+
+
+@pytest.mark.parametrize("mode", [mlb.ATTN_CPU_COMPAT, mlb.ATTN_STANDARD])
+@pytest.mark.parametrize("name", ["small_q4_0_gqa", "small_q4_1_neox_bias", "small_q8_0_ragged"])
+def test_step_kernel_matches_per_op_path(cuda, name, mode):
+    """Both step paths, both attention modes: same greedy ids, logits within the
+    bar (the projections are the same instructions; attention is summed in a
+    different order)."""
+    mt = meta()[name]
+    qtype = {v: k for k, v in C.QTYPE_NAMES.items()}[mt["qtype"]]
+    model = mlb.CudaModel(mt["config"]).synthesize(qtype, 11, with_bias=mt["bias"])
+    a, b = make_ctx(model, "step", mode), make_ctx(model, "per_op", mode)
+    tok_a = tok_b = 17
+    for pos in range(mt["config"]["max_seq_len"]):
+        la, lb = a.forward_token(tok_a, pos), b.forward_token(tok_b, pos)
+        assert np.abs(la - lb).max() <= LOGIT_TOL, pos
+        tok_a, tok_b = int(np.argmax(la)), int(np.argmax(lb))
+        assert tok_a == tok_b, pos
+
+
+def test_step_kernel_selection(cuda):
+    """Quantised single-GPU models default to the step kernel; F32 weights run
+    per op, and asking for the step kernel there names the reason."""
+    mt = meta()["small_q4_0_gqa"]
+    model = mlb.CudaModel(mt["config"]).synthesize(C.Q4_0, 3)
+    ctx = model.context()
+    assert ctx.step_kernel() and ctx.kernels_per_step() == 1
+    ctx.set_step_kernel(False)
+    assert not ctx.step_kernel() and ctx.kernels_per_step() > 1
+    _, ws = readme_weights()
+    f32 = gpu_model(meta()["tiny_readme"]["config"], ws).context()
+    assert not f32.step_kernel()
+    with pytest.raises(mlb.MlbError, match="not Q4_0/Q4_1/Q8_0"):
+        f32.set_step_kernel(True)
+
+
+def test_step_kernel_decode_greedy_matches_forward(cuda):
+    """The on-device greedy loop of the step kernel (position, token and step
+    advanced by the kernel itself) against step-by-step host decoding."""
+    mt = meta()["small_q4_1_neox_bias"]
+    model = mlb.CudaModel(mt["config"]).synthesize(C.Q4_1, 5, with_bias=True)
+    a = make_ctx(model, "step")
+    host, tok = [], 9
+    for pos in range(40):
+        tok = int(np.argmax(a.forward_token(tok, pos)))
+        host.append(tok)
+    b = make_ctx(model, "step")
+    assert b.decode_greedy(9, 0, 40) == host
