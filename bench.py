@@ -30,9 +30,13 @@ from mini_llama_b200 import configs as C  # noqa: E402
 
 SEED = 20261201
 # dram__bytes_read.sum + dram__bytes_write.sum of one gate/up GEMV launch
-# (22016 x 4096 Q4_0) from the ncu capture summarised in
-# profiles/gemv_q4_0_gateup_22016x4096.md; None until that capture exists.
-GEMV_TRAFFIC_BYTES = None
+# (22016 x 4096 Q4_0), from the ncu capture summarised in
+# profiles/gemv_q4_0_gateup_22016x4096.md.
+GEMV_TRAFFIC_BYTES = 50.79e6
+# The same counters for one launch of the persistent decode-step kernel
+# (Llama-2-7B shape, Q4_0), from profiles/decode_step_kernel_llama2-7b-q4_0.md;
+# None until that capture exists.
+STEP_TRAFFIC_BYTES = None
 
 
 def parse_args():
@@ -48,6 +52,10 @@ def parse_args():
     p.add_argument("--sweep-q", type=str, default="q4_0,q4_1,q8_0")
     p.add_argument("--ctx", type=int, default=512, help="KV positions filled before timing")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--layers", type=int, default=0,
+                   help="override the layer count (small profiling cases only; not a bench line)")
+    p.add_argument("--per-op", action="store_true",
+                   help="run the step as one kernel per op instead of the persistent kernel")
     return p.parse_args()
 
 
@@ -261,7 +269,8 @@ def run_gpu(args, cfg, qtype, bias, rank, world, local):
     model = mlb.CudaModel(cfg, device_id=local, tp_rank=rank, tp_size=world, nccl_id=nccl_id)
     model.synthesize(qtype, SEED, with_bias=bias)
     resident, step_weights = model.bytes()
-    ctx = model.context(mlb.ATTN_CPU_COMPAT)
+    ctx = model.context(mlb.ATTN_CPU_COMPAT, step_kernel=False if args.per_op else None)
+    step_kernel = ctx.step_kernel()
     stream = torch.cuda.ExternalStream(ctx.stream())
     tok0 = C.prompt_ids(SEED, 1, cfg["vocab_size"])[0]
     if args.ctx + args.warmup + 2 * args.steps + 2 > cfg["max_seq_len"]:
@@ -324,13 +333,26 @@ def run_gpu(args, cfg, qtype, bias, rank, world, local):
     e2e_ms = max_over_ranks(e0.elapsed_time(e1))
 
     peak = measured_peaks()
-    roof = gemv_roofline(torch, mlb, cfg, qtype, world, peak)
+    gemv_roof = gemv_roofline(torch, mlb, cfg, qtype, world, peak)
     # whole-step HBM roofline: weights + fp32 KV read at the timed context
     kv_per_pos = 2 * cfg["n_layers"] * (cfg["n_kv_heads"] // world) * cfg["head_dim"] * 4
     mid_ctx = (args.ctx + args.warmup + ctx_end) / 2
     step_bytes = step_weights + kv_per_pos * mid_ctx
     step_s = ms / 1e3 / args.steps
     kpl = ctx.kernels_per_step()
+    step_roof = {"bound": "hbm", "achieved": step_bytes / step_s / 1e9, "peak": peak[0],
+                 "unit": "GB/s", "frac": step_bytes / step_s / 1e9 / peak[0],
+                 "bytes_per_launch": step_bytes, "us_per_launch": step_s * 1e6,
+                 "note": "algorithmic bytes: GGUF weight bytes of this rank + fp32 K and V "
+                         "read per token at the mean timed context; time: CUDA events on "
+                         "the context stream around the timed greedy steps",
+                 "peak_source": peak[1] + " (MEASURED_PEAKS.json hbm_gbs, burst)"}
+    if step_kernel:
+        # one launch per step: the persistent kernel is the dominant (only) kernel
+        roof = dict(step_roof, kernel=f"decode_step_kernel<{C.QTYPE_NAMES[qtype]}>",
+                    traffic=STEP_TRAFFIC_BYTES)
+    else:
+        roof = gemv_roof
 
     cpu = None
     if world == 1 and rank == 0 and not args.no_cpu_baseline:
@@ -357,20 +379,20 @@ def run_gpu(args, cfg, qtype, bias, rank, world, local):
             "dtype": C.QTYPE_NAMES[qtype] + "/fp32",
             "data": "synthetic (seeded N(0,0.02) weights quantised like the reference; "
                     "random prompt id)",
-            "config": {"workload": args.workload, "batch": 1, "ctx": args.ctx,
+            "config": {"workload": args.workload + (f" ({args.layers} layers)" if args.layers else ""),
+                       "batch": 1, "ctx": args.ctx,
                        "ctx_end": ctx_end,
                        "parallelism": f"tp{world}" if world > 1 else "single gpu",
                        "l2": "no flush: each step streams %.2f GB of weights (> 126 MB L2)"
                              % (step_weights / 1e9),
-                       "attention": "cpu-compat (reference CPU path V sum)"},
+                       "attention": "cpu-compat (reference CPU path V sum)",
+                       "step": "persistent kernel" if step_kernel else "one kernel per op"},
             "e2e": {"value": args.steps / (e2e_ms / 1e3), "unit": "tok/s",
                     "h2d_bytes_per_step": 12, "d2h_bytes_per_step": cfg["vocab_size"] * 4,
                     "api": "mlb_forward_token (host logits)"},
             "roofline": roof,
-            "step_roofline": {"bound": "hbm", "bytes_per_step": step_bytes,
-                              "achieved": step_bytes / step_s / 1e9, "peak": peak[0],
-                              "unit": "GB/s", "frac": step_bytes / step_s / 1e9 / peak[0],
-                              "note": "GGUF weight bytes of this rank + fp32 KV read per token"},
+            "step_roofline": step_roof,
+            "gemv_roofline": gemv_roof,
             "cpu_baseline": cpu,
             "clocks": clocks,
             "gpu_launches": kpl * args.steps,
@@ -465,6 +487,8 @@ def main():
     if world != args.gpus and world > 1:
         raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE {world}")
     cfg, qtype, bias = C.WORKLOADS[args.workload]
+    if args.layers:
+        cfg = dict(cfg, n_layers=args.layers)
     if args.impl == "reference":
         run_reference(args, cfg, qtype, bias, world, rank)
         return

@@ -427,8 +427,8 @@ static void launch_sb(const QMatrix& m, const float* x, int rows, int ldx, const
   constexpr size_t kSmemMax = 227 * 1024;
   const size_t fixed = gemv_smem_layout<QT, M>(m.gc, nslots, sbb, 0).total;
   const int stages = (int)std::min<size_t>(
-      kMaxStages, fixed < kSmemMax ? (kSmemMax - fixed) / ((size_t)kGemvWarps * sbb) : 0);
-  if (stages < 2) invalid("gemv: staged activations leave no room for the weight ring");
+      kRingStages, fixed < kSmemMax ? (kSmemMax - fixed) / ((size_t)kGemvWarps * sbb) : 0);
+  if (stages < 1) invalid("gemv: staged activations leave no room for the weight ring");
   const size_t smem = gemv_smem_layout<QT, M>(m.gc, nslots, sbb, stages).total;
   static size_t smem_set[64] = {};
   if (dev < 64 && smem_set[dev] < smem) {

@@ -558,7 +558,7 @@ void ContextImpl::plan_step() {
   const int stride = sb_bytes(qt);
   constexpr size_t kSmemMax = 227 * 1024;
   int stages = 0;
-  for (int s = kMaxStages; s >= 2 && !stages; --s)
+  for (int s = kRingStages; s >= 1 && !stages; --s)
     if (step_smem_bytes(scratch, stride, s) <= kSmemMax) stages = s;
   if (!stages) return no("weight ring and scratch exceed shared memory");
   const size_t smem = step_smem_bytes(scratch, stride, stages);
@@ -656,7 +656,7 @@ void ContextImpl::plan_step() {
   step_sync.alloc(2 * sizeof(unsigned int));
   MLB_CUDA(cudaMemset(step_sync.p, 0, step_sync.bytes));
   const int gq = m->q_heads / m->kv_heads;
-  step_attn_ws.alloc((size_t)2 * grid * gq * (D + 4) * 4);
+  step_attn_ws.alloc((size_t)std::max(grid, m->kv_heads) * gq * (D + 4) * 4);  // one record per item
   step_attn_cnt.alloc((size_t)m->kv_heads * 4);
   MLB_CUDA(cudaMemset(step_attn_cnt.p, 0, step_attn_cnt.bytes));
   step.ok = true;

@@ -22,13 +22,14 @@
 // attention. The arithmetic is the standalone GEMV's (gemv_dev.cuh), so
 // results are identical to the per-op path.
 //
-// Attention spreads the (KV head, position) pairs of the step evenly over the
-// CTAs. A CTA's share of one head is a "piece"; its 16 warps take blocks of
-// positions round robin, each keeping an online softmax (m, l, o) per query
-// head of the GQA group; the CTA combines its warps in warp order. A piece
-// that is a whole head writes the output; otherwise it leaves (m, l, o) in a
-// workspace slot and the last piece of the head to arrive combines all pieces
-// in position order. Deterministic, like the GEMV fix-ups.
+// Attention cuts each KV head's positions into G / KV equal slices, one slice
+// per CTA, so every CTA carries at most one piece of work. A CTA's 16 warps
+// take blocks of positions round robin, each keeping an online softmax
+// (m, l, o) per query head of the GQA group; the CTA combines its warps in
+// warp order. A slice that is a whole head writes the output; otherwise it
+// leaves (m, l, o) in a workspace record and the last slice of the head to
+// arrive combines the slices in position order. Deterministic, like the GEMV
+// fix-ups.
 //
 // Every wait is bounded (about 2 s of clock64 polling): on timeout the kernel
 // records MLB_ERR_TIMEOUT in the status word, waits (bounded) for its own
@@ -68,7 +69,6 @@ struct StepShared {
   int run_t[kWinRuns], run_grp[kWinRuns], run_cc0[kWinRuns];
   int nruns;
   int flag;
-  int pieces[kMaxGrid];
 };
 
 __device__ __forceinline__ unsigned int ld_acquire_u32(const unsigned int* p) {
@@ -82,16 +82,18 @@ __device__ __forceinline__ void record_error(DeviceStatus* st, int code, int whe
 }
 
 // Grid barrier over all CTAs of the launch (co-resident: cooperative launch).
-// The arrival counter only grows within a step; the step's last CTA resets it.
+// Barrier k of a step waits for the arrival counter to reach k * gridDim.x:
+// each CTA arrives with a fire-and-forget release add and knows the target
+// from its own count of barriers; the step's last CTA resets the counter.
 // Returns false (block-uniform) when the wait timed out or another CTA
 // recorded an error.
-__device__ bool grid_barrier(unsigned int* counter, DeviceStatus* st, int where, int* flag) {
+__device__ bool grid_barrier(unsigned int* counter, unsigned int k, DeviceStatus* st, int where,
+                             int* flag) {
   __syncthreads();
   if (threadIdx.x == 0) {
     __threadfence();
-    const unsigned int n = gridDim.x;
-    const unsigned int arrived = atomicAdd(counter, 1u) + 1u;
-    const unsigned int target = (arrived + n - 1u) / n * n;
+    asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(counter) : "memory");
+    const unsigned int target = k * gridDim.x;
     const long long t0 = clock64();
     int ok = 1;
     while ((int)(ld_acquire_u32(counter) - target) < 0) {
@@ -452,78 +454,62 @@ __device__ bool attn_phase(StepShared& sh, const StepPhase& cur, uint8_t* scratc
   const int pos = *a.pos;
   const int n = pos + 1;
   const int v_end = at.include_current_v ? (int)n : pos;
-  const int G = gridDim.x, c = blockIdx.x;
-  const int total = at.KV * n;  // 32-bit: KV * max_seq * grid stays below 2^31
-  const int s0 = total * c / G, s1 = total * (c + 1) / G;
+  const int G = gridDim.x;
   const int gq = at.H / at.KV;
   const AttnScratch s = attn_scratch<HG>(scratch, D, gq);
-  for (int sp = s0; sp < s1;) {
-    const int kvh = sp / n;
-    const int t0 = sp - kvh * n;
-    const int t1 = min(n, s1 - kvh * n);
+  // Work items: each KV head cut into pph equal position slices, one item per
+  // CTA (CTAs past the items idle), so no CTA carries two pieces.
+  const int pph = max(1, min(G / at.KV, n));
+  const int items = at.KV * pph;
+  for (int item = blockIdx.x; item < items; item += G) {
+    const int kvh = item / pph, piece = item - kvh * pph;
+    const int t0 = n * piece / pph, t1 = n * (piece + 1) / pph;
     attn_warp<HG>(at, s, gq, kvh, t0, t1, v_end, warp, lane);
     __syncthreads();
-    const bool whole = t0 == 0 && t1 == n;
     float* out = at.out + (size_t)kvh * gq * D;
-    if (whole) {
+    if (pph == 1) {
       attn_combine(s, D, gq, kStepWarps,
                    [&](int h, int i) { return s.wpart + ((size_t)i * gq + h) * rec; }, false, out);
-    } else {
-      // this piece's record: combine the warps, unnormalised (m, l, o)
-      const int slot = 2 * (int)c + (sp != s0 ? 1 : 0);
-      float* dst = a.attn_ws + (size_t)slot * gq * rec;
-      if ((int)threadIdx.x < gq) {
-        const int h = threadIdx.x;
-        float m = -INFINITY;
-        for (int i = 0; i < kStepWarps; ++i) m = fmaxf(m, s.wpart[((size_t)i * gq + h) * rec]);
-        float l = 0.0f;
-        for (int i = 0; i < kStepWarps; ++i) {
-          const float* r = s.wpart + ((size_t)i * gq + h) * rec;
-          const float e = r[0] == -INFINITY ? 0.0f : expf(r[0] - m);
-          s.ew[h * kMaxGrid + i] = e;
-          l = fmaf(r[1], e, l);
-        }
-        dst[h * rec] = m;
-        dst[h * rec + 1] = l;
-      }
-      __syncthreads();
-      for (int idx = threadIdx.x; idx < gq * D; idx += kStepThreads) {
-        const int h = idx / D, d = idx - h * D;
-        float acc = 0.0f;
-        for (int i = 0; i < kStepWarps; ++i)
-          acc = fmaf(s.wpart[((size_t)i * gq + h) * rec + kRecO + d], s.ew[h * kMaxGrid + i],
-                     acc);
-        dst[h * rec + kRecO + d] = acc;
-      }
-      __threadfence();
-      __syncthreads();
-      if (threadIdx.x == 0) {
-        // pieces of this head: CTA ranges cut [kvh n, (kvh + 1) n)
-        int np = 0;
-        int p = kvh * n;
-        const int he = p + n;
-        while (p < he) {
-          const int cc = ((p + 1) * G + total - 1) / total - 1;  // CTA holding p
-          const int cs = total * cc / G, ce = total * (cc + 1) / G;
-          sh.pieces[np++] = 2 * (int)cc + (p != cs ? 1 : 0);
-          p = ce < he ? ce : he;
-        }
-        sh.nruns = np;
-        sh.flag = atomicAdd(&a.attn_counters[kvh], 1) == np - 1;
-      }
-      __syncthreads();
-      if (sh.flag) {
-        __threadfence();
-        const int np = sh.nruns;
-        attn_combine(
-            s, D, gq, np,
-            [&](int h, int i) { return a.attn_ws + ((size_t)sh.pieces[i] * gq + h) * rec; }, true,
-            out);
-        if (threadIdx.x == 0) a.attn_counters[kvh] = 0;
-      }
-      __syncthreads();
+      continue;
     }
-    sp = kvh * n + t1;
+    // this piece's record: the warps combined, unnormalised (m, l, o)
+    float* dst = a.attn_ws + (size_t)item * gq * rec;
+    if ((int)threadIdx.x < gq) {
+      const int h = threadIdx.x;
+      float m = -INFINITY;
+      for (int i = 0; i < kStepWarps; ++i) m = fmaxf(m, s.wpart[((size_t)i * gq + h) * rec]);
+      float l = 0.0f;
+      for (int i = 0; i < kStepWarps; ++i) {
+        const float* r = s.wpart + ((size_t)i * gq + h) * rec;
+        const float e = r[0] == -INFINITY ? 0.0f : expf(r[0] - m);
+        s.ew[h * kMaxGrid + i] = e;
+        l = fmaf(r[1], e, l);
+      }
+      dst[h * rec] = m;
+      dst[h * rec + 1] = l;
+    }
+    __syncthreads();
+    for (int idx = threadIdx.x; idx < gq * D; idx += kStepThreads) {
+      const int h = idx / D, d = idx - h * D;
+      float acc = 0.0f;
+      for (int i = 0; i < kStepWarps; ++i)
+        acc = fmaf(s.wpart[((size_t)i * gq + h) * rec + kRecO + d], s.ew[h * kMaxGrid + i], acc);
+      dst[h * rec + kRecO + d] = acc;
+    }
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) sh.flag = atomicAdd(&a.attn_counters[kvh], 1) == pph - 1;
+    __syncthreads();
+    if (sh.flag) {
+      // the last slice of the head to finish combines all slices, in order
+      __threadfence();
+      attn_combine(
+          s, D, gq, pph,
+          [&](int h, int i) { return a.attn_ws + ((size_t)(kvh * pph + i) * gq + h) * rec; },
+          true, out);
+      if (threadIdx.x == 0) a.attn_counters[kvh] = 0;
+    }
+    __syncthreads();
   }
   return true;
 }
@@ -586,7 +572,8 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
     else
       ok = attn_phase<HG>(sh, cur, scratch, a);
     cp_async_wait_all();
-    if (ok && p + 1 < a.nphases) ok = grid_barrier(&a.sync[0], a.status, 100 + p, &sh.flag);
+    if (ok && p + 1 < a.nphases)
+      ok = grid_barrier(&a.sync[0], (unsigned int)(p + 1), a.status, 100 + p, &sh.flag);
   }
   if (!ok) {
     if (lane == 0) ring_drain(rg.bars, rg.stages, rg.slot, rg.parity, rg.inflight);

@@ -56,7 +56,7 @@ struct StepArgs {
   unsigned long long* argmax_key;
   float* ws;                // GEMV fix-up partials
   int* counters;            // GEMV fix-up arrival counters (zero between phases)
-  float* attn_ws;           // attention piece records [2 * grid][gq][D + 4]
+  float* attn_ws;           // attention slice records [max(grid, KV)][gq][D + 4]
   int* attn_counters;       // [KV] (zero between phases)
   unsigned int* sync;       // [0] grid-barrier arrivals, [1] end-of-step arrivals
   DeviceStatus* status;
