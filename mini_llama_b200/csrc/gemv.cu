@@ -293,8 +293,8 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 1) gemv_sb_kernel(const GemvK
   uint32_t parity = 0;
   if (threadIdx.x == 0) *ok_s = 1;
   for (int wb = cb; wb < ce;) {
-    if (threadIdx.x == 0)
-      *nruns_s = build_window(wb, ce, a.ntiles, a.nchunks, a.gc, kWinRuns, win_sbs<M>(), rt);
+    build_window_par(wb, ce, a.ntiles, a.nchunks, a.gc, a.ngroups, kWinRuns, win_sbs<M>(), rt,
+                     nruns_s);
     __syncthreads();  // run table (and the staged x) visible; parts free
     const int nruns = *nruns_s;
     const int we = rt.u0[nruns];

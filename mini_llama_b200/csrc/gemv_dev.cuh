@@ -128,6 +128,31 @@ __device__ __forceinline__ int build_window(int wb, int ce, int ntiles, int nchu
   return r;
 }
 
+// Block-wide form of build_window. With one chunk group every run is a whole
+// tile of nchunks super-blocks, so run r of the window starts at wb + r
+// nchunks and thread r fills entry r (no serial walk); with several groups
+// thread 0 walks. *nruns is written by thread 0. Visible after the caller's
+// __syncthreads.
+__device__ __forceinline__ void build_window_par(int wb, int ce, int ntiles, int nchunks, int gc,
+                                                 int ngroups, int R, int maxsb,
+                                                 const RunTable& rt, int* nruns) {
+  if (ngroups > 1) {
+    if (threadIdx.x == 0) *nruns = build_window(wb, ce, ntiles, nchunks, gc, R, maxsb, rt);
+    return;
+  }
+  const int n = max(1, min(min((ce - wb) / nchunks, R), maxsb / nchunks));
+  const int t0 = wb / nchunks;  // wb starts a tile
+  for (int r = threadIdx.x; r <= n; r += blockDim.x) {
+    rt.u0[r] = wb + r * nchunks;
+    if (r < n) {
+      rt.t[r] = t0 + r;
+      rt.grp[r] = 0;
+      rt.cc0[r] = 0;
+    }
+  }
+  if (threadIdx.x == 0) *nruns = n;
+}
+
 // A warp's position in the super-block order, advanced 16 super-blocks at a
 // time without divisions: chunk cc of tile t in chunk group grp (geff chunks),
 // and the offsets of that chunk's staged B fragments and side data.

@@ -83,15 +83,16 @@ __device__ __forceinline__ void record_error(DeviceStatus* st, int code, int whe
 
 // Grid barrier over all CTAs of the launch (co-resident: cooperative launch).
 // Barrier k of a step waits for the arrival counter to reach k * gridDim.x:
-// each CTA arrives with a fire-and-forget release add and knows the target
-// from its own count of barriers; the step's last CTA resets the counter.
+// each CTA arrives with a fire-and-forget release add (after bar.sync, so it
+// publishes the whole CTA's writes) and knows the target from its own count
+// of barriers; the poll is an acquire load followed by bar.sync. The step's
+// last CTA resets the counter.
 // Returns false (block-uniform) when the wait timed out or another CTA
 // recorded an error.
 __device__ bool grid_barrier(unsigned int* counter, unsigned int k, DeviceStatus* st, int where,
                              int* flag) {
-  __syncthreads();
+  __syncthreads();  // the CTA's writes happen before thread 0's release below
   if (threadIdx.x == 0) {
-    __threadfence();
     asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(counter) : "memory");
     const unsigned int target = k * gridDim.x;
     const long long t0 = clock64();
@@ -107,8 +108,7 @@ __device__ bool grid_barrier(unsigned int* counter, unsigned int k, DeviceStatus
         break;
       }
     }
-    __threadfence();
-    *flag = ok;
+    *flag = ok;  // the acquire load above orders the CTA's later reads (bar.sync)
   }
   __syncthreads();
   const int ok = *flag;
@@ -234,8 +234,8 @@ __device__ bool gemv_phase(StepShared& sh, StepPhase& cur, uint8_t* scratch, Rin
   // The CTA range in windows; warp w keeps taking super-blocks cb + w,
   // cb + w + 16, ... across windows (and its producer across phases).
   for (int wb = cb; wb < ce;) {
-    if (threadIdx.x == 0)
-      sh.nruns = build_window(wb, ce, g.ntiles, g.nchunks, g.gc, kWinRuns, win_sbs<1>(), rt);
+    build_window_par(wb, ce, g.ntiles, g.nchunks, g.gc, g.ngroups, kWinRuns, win_sbs<1>(), rt,
+                     &sh.nruns);
     __syncthreads();  // run table (and, first time, the staged x) visible
     const int nruns = sh.nruns;
     const int we = sh.run_u0[nruns];
