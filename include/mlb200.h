@@ -206,6 +206,25 @@ typedef struct {
 typedef struct mlb_model mlb_model;
 typedef struct mlb_context mlb_context;
 
+/* The shard one tensor-parallel rank keeps. wq/bq rows and wo input columns:
+ * query heads [q_head0, q_head0 + q_heads) (times head_dim); wk/wv/bk/bv rows:
+ * KV heads [kv_head0, ...); w_gate/w_up rows and w_down input columns: FFN
+ * hidden rows [ffn_row0, ffn_row0 + ffn_rows), whole 32-row blocks split as
+ * evenly as the blocks allow; lm_head rows: vocabulary [vocab_row0, ...).
+ * Embedding and norms are replicated. */
+typedef struct {
+  int q_head0, q_heads;
+  int kv_head0, kv_heads;
+  int ffn_row0, ffn_rows;
+  int vocab_row0, vocab_rows;
+} mlb_tp_shard;
+
+/* Computes the shard of rank tp_rank of tp_size on the host (no device, no
+ * communicator). Returns MLB_ERR_INVALID, with the reason in mlb_last_error(),
+ * when the config cannot be split over tp_size ranks. No reference
+ * counterpart (the reference runs on one device); mlb_model_create uses it. */
+int mlb_tp_plan(const mlb_config* cfg, int tp_rank, int tp_size, mlb_tp_shard* out);
+
 /* Replaces UploadModelWeightsToCuda (include/mini_llama/model.h:103) together
  * with mlb_model_set_weight / mlb_model_finalize. With tp_size > 1 the model
  * holds this rank's tensor-parallel shard (wq/wk/wv/w_gate/w_up split by

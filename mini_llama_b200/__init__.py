@@ -31,7 +31,7 @@ __all__ = [
     "CudaRmsNormDeviceWeight", "CudaSiluDeviceInput", "CudaElementwiseMulDeviceInput",
     "CudaElementwiseAddDeviceInput", "CudaSoftmax", "CudaEmbeddingLookupDeviceWeight",
     "CudaRopeDeviceInput", "CudaArgMax", "CudaKvCache", "CudaAttentionDecodeDeviceInput",
-    "QMatrix", "CudaModel", "Context", "ForwardToken", "configs",
+    "QMatrix", "CudaModel", "Context", "ForwardToken", "configs", "tp_plan", "nccl_unique_id",
 ]
 
 
@@ -470,6 +470,16 @@ class Context:
 def ForwardToken(ctx: Context, token: int) -> np.ndarray:
     """ForwardToken(ctx, model, token) (include/mini_llama/forward.h:11) at ctx.pos."""
     return ctx.forward_token(token, ctx.pos)
+
+
+def tp_plan(cfg: dict, tp_rank: int, tp_size: int) -> dict:
+    """The tensor-parallel shard of one rank (host only; see mlb_tp_plan)."""
+    from ._lib import MlbTpShard
+
+    c = MlbConfig(**{k: cfg[k] for k, _ in MlbConfig._fields_})
+    out = MlbTpShard()
+    check(lib().mlb_tp_plan(ctypes.byref(c), int(tp_rank), int(tp_size), ctypes.byref(out)))
+    return {k: getattr(out, k) for k, _ in MlbTpShard._fields_}
 
 
 def nccl_unique_id() -> bytes:

@@ -27,6 +27,14 @@ class MlbConfig(ctypes.Structure):
         ("rope_type", ctypes.c_int)]
 
 
+class MlbTpShard(ctypes.Structure):
+    """mlb_tp_shard: the rows / input columns one tensor-parallel rank keeps."""
+
+    _fields_ = [(n, ctypes.c_int) for n in ("q_head0", "q_heads", "kv_head0", "kv_heads",
+                                             "ffn_row0", "ffn_rows", "vocab_row0",
+                                             "vocab_rows")]
+
+
 # (name, restype, argtypes) of every entry point in include/mlb200.h
 SIGNATURES = [
     ("mlb_last_error", ctypes.c_char_p, []),
@@ -58,6 +66,8 @@ SIGNATURES = [
     ("mlb_qmatrix_gemv", _c_int, [_vp, _vp, _c_int, _vp, _vp]),
     ("mlb_qmatrix_bytes", _c_size_t, [_vp]),
     ("mlb_qmatrix_destroy", _c_int, [_vp]),
+    ("mlb_tp_plan", _c_int, [ctypes.POINTER(MlbConfig), _c_int, _c_int,
+                             ctypes.POINTER(MlbTpShard)]),
     ("mlb_model_create", _c_int, [ctypes.POINTER(MlbConfig), _c_int, _c_int, _c_int, _vp,
                                   ctypes.POINTER(_vp)]),
     ("mlb_model_set_weight", _c_int, [_vp, _c_int, _c_int, _c_int, _c_int, _c_int, _vp, _c_size_t]),

@@ -43,6 +43,7 @@ int sm_count(int device_id) {
 
 // Model, context and step functions of runtime.cu.
 ModelImpl* model_create(const mlb_config* cfg, int device, int rank, int size, const void* id);
+mlb_tp_shard tp_plan(const mlb_config& c, int rank, int size);
 void model_destroy(ModelImpl* m);
 void model_set_weight(ModelImpl& m, int kind, int layer, int qtype, int rows, int cols,
                       const void* data, size_t bytes);
@@ -403,6 +404,13 @@ int mlb_qmatrix_destroy(mlb_qmatrix* m) {
 }
 
 // ------------------------------------------------------------- model/context
+
+int mlb_tp_plan(const mlb_config* cfg, int tp_rank, int tp_size, mlb_tp_shard* out) {
+  return guarded([&] {
+    if (!cfg || !out) invalid("mlb_tp_plan: null pointer");
+    *out = tp_plan(*cfg, tp_rank, tp_size);
+  });
+}
 
 int mlb_model_create(const mlb_config* cfg, int device_id, int tp_rank, int tp_size,
                      const void* nccl_id, mlb_model** out) {

@@ -160,7 +160,7 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
 }
 
 // 1-D bulk copy global -> shared, completion counted on `bar` (bytes % 16 == 0,
-// both addresses 16-byte aligned). No multicast.
+// both addresses 16-byte aligned); a plain copy into this CTA only.
 __device__ __forceinline__ void bulk_g2s(void* smem_dst, const void* gmem_src, uint32_t bytes,
                                          uint64_t* bar) {
   asm volatile(

@@ -134,6 +134,35 @@ static void shard_rows(const ModelImpl& m, int kind, int full_rows, int* row0, i
   }
 }
 
+mlb_tp_shard tp_plan(const mlb_config& c, int rank, int size) {
+  if (size < 1 || rank < 0 || rank >= size) invalid("mlb_model_create: bad tensor-parallel rank/size");
+  if (size > 1) {
+    if (c.n_heads % size || c.n_kv_heads % size)
+      invalid("tensor parallel: n_heads and n_kv_heads must be divisible by the TP size");
+    if ((c.n_heads / size * c.head_dim) % 32)
+      invalid("tensor parallel: per-rank attention width must be a multiple of 32");
+    if (c.hidden_dim % 32 || c.vocab_size % size)
+      invalid("tensor parallel: hidden_dim must be a multiple of 32 and vocab divisible by TP size");
+  }
+  mlb_tp_shard sh{};
+  sh.q_heads = c.n_heads / size;
+  sh.q_head0 = rank * sh.q_heads;
+  sh.kv_heads = c.n_kv_heads / size;
+  sh.kv_head0 = rank * sh.kv_heads;
+  if (size == 1) {
+    sh.ffn_row0 = 0;
+    sh.ffn_rows = c.hidden_dim;
+  } else {
+    const int nb = c.hidden_dim / 32;
+    const int b0 = (int)((long long)nb * rank / size), b1 = (int)((long long)nb * (rank + 1) / size);
+    sh.ffn_row0 = b0 * 32;
+    sh.ffn_rows = (b1 - b0) * 32;
+  }
+  sh.vocab_rows = c.vocab_size / size;
+  sh.vocab_row0 = rank * sh.vocab_rows;
+  return sh;
+}
+
 ModelImpl* model_create(const mlb_config* cfg, int device, int rank, int size,
                         const void* nccl_id) {
   if (!cfg) invalid("mlb_model_create: null config");
@@ -145,15 +174,7 @@ ModelImpl* model_create(const mlb_config* cfg, int device, int rank, int size,
   if (c.head_dim % 4 != 0) invalid("mlb_model_create: head_dim must be a multiple of 4");
   if (!(c.rope_theta > 0.0f) || !std::isfinite(c.rope_theta))
     invalid("Rope: theta must be finite and positive");
-  if (size < 1 || rank < 0 || rank >= size) invalid("mlb_model_create: bad tensor-parallel rank/size");
-  if (size > 1) {
-    if (c.n_heads % size || c.n_kv_heads % size)
-      invalid("tensor parallel: n_heads and n_kv_heads must be divisible by the TP size");
-    if ((c.n_heads / size * c.head_dim) % 32)
-      invalid("tensor parallel: per-rank attention width must be a multiple of 32");
-    if (c.hidden_dim % 32 || c.vocab_size % size)
-      invalid("tensor parallel: hidden_dim must be a multiple of 32 and vocab divisible by TP size");
-  }
+  const mlb_tp_shard sh = tp_plan(c, rank, size);
   attn_check_tiled(c.n_heads / size, c.n_kv_heads / size, c.head_dim);
   set_device(device);
   auto m = std::make_unique<ModelImpl>();
@@ -162,21 +183,14 @@ ModelImpl* model_create(const mlb_config* cfg, int device, int rank, int size,
   m->tp_rank = rank;
   m->tp_size = size;
   m->neox = c.rope_type == MLB_ROPE_NEOX;
-  m->q_heads = c.n_heads / size;
-  m->q_head0 = rank * m->q_heads;
-  m->kv_heads = c.n_kv_heads / size;
-  m->kv_head0 = rank * m->kv_heads;
-  if (size == 1) {
-    m->ffn_row0 = 0;
-    m->ffn_rows = c.hidden_dim;
-  } else {
-    int nb = c.hidden_dim / 32;
-    int b0 = (int)((long long)nb * rank / size), b1 = (int)((long long)nb * (rank + 1) / size);
-    m->ffn_row0 = b0 * 32;
-    m->ffn_rows = (b1 - b0) * 32;
-  }
-  m->vocab_rows = c.vocab_size / size;
-  m->vocab_row0 = rank * m->vocab_rows;
+  m->q_heads = sh.q_heads;
+  m->q_head0 = sh.q_head0;
+  m->kv_heads = sh.kv_heads;
+  m->kv_head0 = sh.kv_head0;
+  m->ffn_row0 = sh.ffn_row0;
+  m->ffn_rows = sh.ffn_rows;
+  m->vocab_rows = sh.vocab_rows;
+  m->vocab_row0 = sh.vocab_row0;
   m->vocab_pad = m->vocab_rows;
   m->layers.resize(c.n_layers);
   MLB_CUDA(cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking));

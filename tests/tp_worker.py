@@ -1,0 +1,66 @@
+"""One rank of a tensor-parallel decode run (launched by torch.distributed.run,
+one process per GPU) for tests/test_gpu_tp.py: loads a golden small model
+sharded over WORLD_SIZE ranks and decodes it; rank 0 writes the logits and
+token ids to the JSON file named on the command line."""
+import datetime
+import json
+import os
+import sys
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+sys.path.insert(0, ROOT)
+
+import torch  # noqa: E402
+import torch.distributed as dist  # noqa: E402
+
+import mini_llama_b200 as mlb  # noqa: E402
+from mini_llama_b200 import configs as C  # noqa: E402
+
+
+def main():
+    name, out = sys.argv[1], sys.argv[2]
+    rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+    local = int(os.environ.get("LOCAL_RANK", rank))
+    torch.cuda.set_device(local)
+    dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=120))
+    obj = [mlb.nccl_unique_id() if rank == 0 else None]
+    dist.broadcast_object_list(obj, src=0)
+    golden = os.path.join(ROOT, "tests", "golden")
+    with open(os.path.join(golden, "golden.json")) as f:
+        mt = json.load(f)[name]
+    g = np.load(os.path.join(golden, f"{name}.npz"))
+    qtype = {v: k for k, v in C.QTYPE_NAMES.items()}[mt["qtype"]]
+    cfg = mt["config"]
+    model = mlb.CudaModel(cfg, device_id=local, tp_rank=rank, tp_size=world, nccl_id=obj[0])
+    model.load(list(C.host_weights(cfg, qtype, mt["seed"], mt["bias"])))
+    prompt = [int(t) for t in g["prompt"]]
+    gold = [int(t) for t in g["tokens"]]
+    # teacher-forced logits (every rank runs the same steps: the step holds collectives)
+    ctx = model.context()
+    logits, tok = [], prompt[0]
+    for pos in range(len(gold)):
+        logits.append(ctx.forward_token(tok, pos))
+        tok = prompt[pos + 1] if pos + 1 < len(prompt) else gold[pos]
+    # the on-device greedy loop
+    ctx2 = model.context()
+    for pos, t in enumerate(prompt[:-1]):
+        ctx2.forward_token(t, pos)
+    dev = ctx2.decode_greedy(prompt[-1], len(prompt) - 1, len(gold) - len(prompt) + 1)
+    if rank == 0:
+        err = np.abs(np.stack(logits) - g["logits"]).max()
+        with open(out, "w") as f:
+            json.dump({"max_err": float(err), "argmax": [int(np.argmax(l)) for l in logits],
+                       "device_greedy": dev, "gold": gold, "prompt_len": len(prompt),
+                       "kernels_per_step": ctx.kernels_per_step(),
+                       "step_kernel": ctx.step_kernel()}, f)
+    ctx.close()
+    ctx2.close()
+    model.close()
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()
