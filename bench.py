@@ -34,9 +34,10 @@ SEED = 20261201
 # profiles/gemv_q4_0_gateup_22016x4096.md.
 GEMV_TRAFFIC_BYTES = 50.79e6
 # The same counters for one launch of the persistent decode-step kernel
-# (Llama-2-7B shape, Q4_0), from profiles/decode_step_kernel_llama2-7b-q4_0.md;
-# None until that capture exists.
-STEP_TRAFFIC_BYTES = None
+# (Llama-2-7B shape, Q4_0, context ~520), from the 2- and 4-layer captures in
+# profiles/decode_step_kernel_llama2-7b-q4_0.md scaled to 32 layers (traffic
+# grows linearly with layers: 77.6 MB + 131.1 MB per layer).
+STEP_TRAFFIC_BYTES = 4.273e9
 
 
 def parse_args():
@@ -242,7 +243,9 @@ def gemv_roofline(torch, mlb, cfg, qtype, world, peak):
     ms = time_launches(torch, lambda i: mats[i % copies].gemv(x, y), 8 * copies)
     achieved = nbytes / (ms * 1e-3) / 1e9
     return {"bound": "hbm", "achieved": achieved, "peak": peak[0], "unit": "GB/s",
-            "frac": achieved / peak[0], "traffic": GEMV_TRAFFIC_BYTES,
+            "frac": achieved / peak[0],
+            # the captured traffic is for the single-GPU shape (22016 x 4096)
+            "traffic": GEMV_TRAFFIC_BYTES if world == 1 else None,
             "kernel": f"gemv_sb_kernel<{C.QTYPE_NAMES[qtype]}> {n}x{k}",
             "bytes_per_launch": nbytes, "us_per_launch": ms * 1e3,
             "peak_source": peak[1] + " (MEASURED_PEAKS.json hbm_gbs, burst)"}
