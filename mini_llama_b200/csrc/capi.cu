@@ -494,7 +494,7 @@ int mlb_forward_token_device(mlb_context* c, int token, int pos, const float** l
   return guarded([&] {
     if (!c) invalid("ForwardToken: null context");
     context_step_async(*c->impl, token, pos);
-    if (logits_dev) *logits_dev = c->impl->logits.as<float>();
+    if (logits_dev) *logits_dev = c->impl->logits_dev();
   });
 }
 

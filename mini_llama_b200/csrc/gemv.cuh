@@ -45,6 +45,21 @@ enum EpiKind : int {
   kEpiResidual = 1, // y[r, row] = resid[r, row] + v
   kEpiQkv = 2,      // + bias, RoPE, q -> q_out, k/v -> KV cache slot (layer, *pos)
   kEpiSwiglu = 3,   // tile rows 0..7 gate, 8..15 up -> y[r, 8t+i] = silu(g) * u
+  kEpiTpPartial = 4,  // tensor parallel: v -> every rank's partial slot [tp_slot][me][row]
+};
+
+// Rank-to-rank exchange of one tensor-parallel context: each rank owns one
+// exchange buffer, and every rank's buffer is mapped into every process
+// (peers[r]; peers[me] is the local one). Byte offsets inside a buffer:
+// partial sums [2 slots][n][dim] as tagged 8-byte words {fp32 bits, exchange
+// step + 1} (an 8-byte store arrives whole, so the data is its own signal),
+// full logits [vocab] fp32, argmax keys [n] u64 and key counters [n] u32
+// (kflags[r]: rank r's greedy keys delivered, one per decode step).
+constexpr int kMaxTp = 8;
+struct TpXchg {
+  int n, me, dim, vocab;
+  long long parts_off, logits_off, keys_off, kflags_off;
+  uint8_t* peers[kMaxTp];
 };
 
 struct EpiParams {
@@ -71,6 +86,12 @@ struct EpiParams {
   // (vocabulary shard start under tensor parallelism).
   unsigned long long* argmax_key;
   int argmax_base;
+  // Tensor parallel (step kernel): kEpiTpPartial writes partial sums into
+  // slot tp_slot of every rank; kEpiStore with tp set writes the logits rows
+  // (global index argmax_base + row) into every rank's exchange buffer.
+  const TpXchg* tp;
+  int tp_slot;
+  unsigned int tp_tag;  // kEpiTpPartial: tag of this exchange step (set on the device)
 };
 
 #if defined(__CUDACC__)

@@ -204,7 +204,25 @@ __device__ void epilogue_row(const EpiParams& p, int tile, int row, int r, const
   int grow = tile * 16 + row;
   switch (p.kind) {
     case kEpiStore:
-      if (grow < p.n_out) p.y[(size_t)r * p.ldy + grow] = v;
+      if (grow < p.n_out) {
+        if (p.tp) {
+          const long long o = p.tp->logits_off + (long long)(p.argmax_base + grow) * 4;
+          for (int rr = 0; rr < p.tp->n; ++rr) *reinterpret_cast<float*>(p.tp->peers[rr] + o) = v;
+        } else {
+          p.y[(size_t)r * p.ldy + grow] = v;
+        }
+      }
+      break;
+    case kEpiTpPartial:
+      if (grow < p.n_out) {
+        const TpXchg* x = p.tp;
+        const long long o =
+            x->parts_off + ((long long)(p.tp_slot * x->n + x->me) * x->dim + grow) * 8;
+        for (int rr = 0; rr < x->n; ++rr)
+          asm volatile("st.relaxed.sys.global.v2.u32 [%0], {%1, %2};" ::"l"(x->peers[rr] + o),
+                       "r"(__float_as_uint(v)), "r"(p.tp_tag)
+                       : "memory");
+      }
       break;
     case kEpiResidual:
       if (grow < p.n_out)
@@ -425,10 +443,52 @@ constexpr int kStageBatch = 4;  // float4 of x each thread loads per round trip
 // then the warp sums in warp order, the same order as norm_inv_rms; longer
 // rows take norm_inv_rms's extra pass. A norm needs the CTA to stage all of K
 // (g0 .. g1 cover every chunk group). The caller synchronises afterwards.
+// Tensor-parallel form: x is base + parts[0] + ... + parts[nparts - 1] (rows of
+// length ldp of tagged words, summed in rank order, so every rank stages the
+// same values); each word is read until it carries `tag` (bounded: on
+// timeout the status records it and *failed is set). When store is non-null
+// this CTA writes its 1/gridDim slice of that sum there (the residual stream
+// for later phases). Needs the whole K staged.
+struct TpSum {
+  const uint2* parts;
+  int nparts, ldp;
+  unsigned int tag;
+  float* store;
+  DeviceStatus* status;
+  int* failed;  // shared flag, set to 1 on timeout
+};
+
+// Adds rank rr's tagged partial sums of inputs k0 .. k0 + 3 to v, waiting
+// (bounded) until all four words carry the tag.
+__device__ __forceinline__ void tp_add_quad(const TpSum& t, int rr, int k0, int k, float4& v) {
+  const uint2* w = t.parts + (size_t)rr * t.ldp + k0;
+  float e[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+  const long long t0 = clock64();
+  for (int i = 0; i < 4; ++i) {
+    if (k0 + i >= k) break;
+    uint32_t val, tg;
+    while (true) {
+      asm volatile("ld.relaxed.sys.global.v2.u32 {%0, %1}, [%2];"
+                   : "=r"(val), "=r"(tg) : "l"(w + i) : "memory");
+      if (tg == t.tag) break;
+      if (clock64() - t0 > 4000000000LL || *(volatile int*)t.failed) {
+        if (t.status && atomicCAS(&t.status->code, 0, MLB_ERR_TIMEOUT) == 0)
+          atomicExch(&t.status->where, 400);
+        *(volatile int*)t.failed = 1;
+        val = 0u;
+        break;
+      }
+    }
+    e[i] = __uint_as_float(val);
+  }
+  v.x += e[0]; v.y += e[1]; v.z += e[2]; v.w += e[3];
+}
+
 template <int QT>
 __device__ __forceinline__ void stage_x_m1(const float* x, int k, const float* norm_w, float eps,
                                            int gc, int nchunks, int g0, int g1, uint32_t* frag,
-                                           float* side, float* part, float* inv_rms) {
+                                           float* side, float* part, float* inv_rms,
+                                           const TpSum* tps = nullptr) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nthr = blockDim.x;
   const int c0 = g0 * gc, c1 = min(nchunks, (g1 + 1) * gc);
   const int nq = (c1 - c0) * 64;
@@ -445,6 +505,19 @@ __device__ __forceinline__ void stage_x_m1(const float* x, int k, const float* n
       w[j] = make_float4(0.f, 0.f, 0.f, 0.f);
       if (idx < nq) {
         v[j] = load_quad(x, kbase + idx * 4, k, false);
+        if (tps) {
+          for (int rr = 0; rr < tps->nparts; ++rr) tp_add_quad(*tps, rr, kbase + idx * 4, k, v[j]);
+          if (tps->store) {  // this CTA's slice of the summed row
+            const int lo = (int)((long long)nq * blockIdx.x / gridDim.x);
+            const int hi = (int)((long long)nq * (blockIdx.x + 1) / gridDim.x);
+            if (idx >= lo && idx < hi) {
+              const int k0 = kbase + idx * 4;
+              const float e4[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
+              for (int i = 0; i < 4; ++i)
+                if (k0 + i < k) tps->store[k0 + i] = e4[i];
+            }
+          }
+        }
         if (norm_w) w[j] = load_quad(norm_w, kbase + idx * 4, k, true);
       }
     }
@@ -493,6 +566,21 @@ __device__ __forceinline__ void stage_x_m1(const float* x, int k, const float* n
         if (valid && (q4 & 7) == 0) sd[8 + (q4 >> 3)] = s4;
       }
     }
+  }
+}
+
+// Block-wide: this CTA's 1/gridDim slice (in float4 units, as stage_x_m1
+// cuts it) of x + every rank's partial sums, written to tps.store.
+__device__ __forceinline__ void tp_store_slice(const float* x, int k, const TpSum& tps) {
+  const int nq = (k + kChunkK - 1) / kChunkK * 64;  // quads of whole chunks, as staged
+  const int lo = (int)((long long)nq * blockIdx.x / gridDim.x);
+  const int hi = (int)((long long)nq * (blockIdx.x + 1) / gridDim.x);
+  for (int idx = lo + threadIdx.x; idx < hi; idx += blockDim.x) {
+    float4 v = load_quad(x, idx * 4, k, false);
+    for (int rr = 0; rr < tps.nparts; ++rr) tp_add_quad(tps, rr, idx * 4, k, v);
+    const float e4[4] = {v.x, v.y, v.z, v.w};
+    for (int i = 0; i < 4; ++i)
+      if (idx * 4 + i < k) tps.store[idx * 4 + i] = e4[i];
   }
 }
 

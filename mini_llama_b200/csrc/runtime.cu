@@ -471,6 +471,8 @@ void ContextImpl::release_graphs() {
 
 ContextImpl::~ContextImpl() {
   if (m) cudaSetDevice(m->device);
+  if (stream) cudaStreamSynchronize(stream);
+  for (void* p : tp_opened) cudaIpcCloseMemHandle(p);
   release_graphs();
   if (h_scalars) cudaFreeHost(h_scalars);
   if (h_logits) cudaFreeHost(h_logits);
@@ -549,7 +551,9 @@ void ContextImpl::plan_step() {
     step.ok = false;
     step.why = why;
   };
-  if (m->tp_size != 1) return no("tensor-parallel steps use the per-op path");
+  const bool tp = m->tp_size > 1;
+  if (tp && m->tp_size > kMaxTp) return no("more tensor-parallel ranks than the exchange holds");
+  if (tp && cf.dim > 8192) return no("tensor parallel: dim above 8192");
   std::string why;
   if (!step_attn_ok(m->q_heads, m->kv_heads, D, &why)) return no(why);
   const int grid = sm_count(m->device);
@@ -597,9 +601,25 @@ void ContextImpl::plan_step() {
     p.g.norm_w = norm_w;
     p.g.eps = cf.rms_norm_eps;
     p.g.epi = e;
+    p.g.tp_ar = -1;
+    p.g.x_slot = -1;
+    p.g.x_ar = -1;
+    p.g.x_store = nullptr;
     ph.push_back(p);
   };
   int* d_pos = scalars.as<int>() + 1;
+  if (tp) setup_tp_exchange();
+  const TpXchg* tpd = tp ? tp_desc.as<TpXchg>() : nullptr;
+  // Tensor parallel: exchange step 2l is layer l's wo partial sums (slot 0),
+  // 2l + 1 its w_down partial sums (slot 1). The producing phase ends with the
+  // fused cross-rank barrier; the consuming phase adds every rank's partials
+  // to the residual and keeps the result as the next residual.
+  auto tp_in = [&](StepPhase& p, int slot, int ar, const float* base, float* store) {
+    p.g.x = base;
+    p.g.x_slot = slot;
+    p.g.x_ar = ar;
+    p.g.x_store = store;
+  };
   for (int l = 0; l < cf.n_layers; ++l) {
     const LayerPlan& L = m->layers[l];
     const float* x_in = l == 0 ? nullptr : xa.as<float>();  // null: embedding row
@@ -618,6 +638,7 @@ void ContextImpl::plan_step() {
     e.values = values.as<float>() + (size_t)l * layer_kv;
     e.q_out = q.as<float>();
     gemv(L.qkv, x_in, L.attn_norm.as<float>(), e);
+    if (tp && l > 0) tp_in(ph.back(), 1, 2 * (l - 1) + 1, xb.as<float>(), xa.as<float>());
 
     StepPhase a{};
     a.kind = kPhaseAttn;
@@ -633,12 +654,15 @@ void ContextImpl::plan_step() {
     ph.push_back(a);
 
     EpiParams eo{};
-    eo.kind = kEpiResidual;
+    eo.kind = tp ? kEpiTpPartial : kEpiResidual;
     eo.y = xb.as<float>();
     eo.resid = x_in;  // null: embedding row
     eo.ldy = eo.ldr = cf.dim;
     eo.n_out = cf.dim;
+    eo.tp = tpd;
+    eo.tp_slot = 0;
     gemv(L.wo, attn.as<float>(), nullptr, eo);
+    if (tp) ph.back().g.tp_ar = 2 * l;
 
     EpiParams eg{};
     eg.kind = kEpiSwiglu;
@@ -646,14 +670,18 @@ void ContextImpl::plan_step() {
     eg.ldy = m->ffn_rows;
     eg.n_out = m->ffn_rows;
     gemv(L.gateup, xb.as<float>(), L.ffn_norm.as<float>(), eg);
+    if (tp) tp_in(ph.back(), 0, 2 * l, x_in, xb.as<float>());
 
     EpiParams ed{};
-    ed.kind = kEpiResidual;
+    ed.kind = tp ? kEpiTpPartial : kEpiResidual;
     ed.y = xa.as<float>();
     ed.resid = xb.as<float>();
     ed.ldy = ed.ldr = cf.dim;
     ed.n_out = cf.dim;
+    ed.tp = tpd;
+    ed.tp_slot = 1;
     gemv(L.down, hidden.as<float>(), nullptr, ed);
+    if (tp) ph.back().g.tp_ar = 2 * l + 1;
   }
   EpiParams el{};
   el.kind = kEpiStore;
@@ -661,8 +689,11 @@ void ContextImpl::plan_step() {
   el.ldy = m->vocab_rows;
   el.n_out = m->vocab_rows;
   el.argmax_key = argmax_key.as<unsigned long long>();
-  el.argmax_base = 0;
+  el.argmax_base = m->vocab_row0;
+  el.tp = tpd;
   gemv(m->lm_head, cf.n_layers == 0 ? nullptr : xa.as<float>(), m->final_norm.as<float>(), el);
+  if (tp && cf.n_layers > 0)
+    tp_in(ph.back(), 1, 2 * (cf.n_layers - 1) + 1, xb.as<float>(), nullptr);
 
   step_phases.alloc(ph.size() * sizeof(StepPhase));
   MLB_CUDA(cudaMemcpy(step_phases.p, ph.data(), ph.size() * sizeof(StepPhase),
@@ -706,7 +737,68 @@ void ContextImpl::launch_step(cudaStream_t s) {
   a.attn_counters = step_attn_cnt.as<int>();
   a.sync = step_sync.as<unsigned int>();
   a.status = status.as<DeviceStatus>();
+  if (m->tp_size > 1) {
+    a.tp = tp_desc.as<TpXchg>();
+    a.tp_gen = tp_gen.as<unsigned int>();
+    a.tp_steps = 2 * m->cfg.n_layers;
+  }
   step_launch(step, a, s);
+}
+
+const float* ContextImpl::logits_dev() const {
+  if (use_step && m->tp_size > 1)
+    return reinterpret_cast<const float*>(xchg.as<uint8_t>() + tpx.logits_off);
+  return logits.as<float>();
+}
+
+// Tensor-parallel step kernel: one exchange buffer per rank, its IPC handle
+// gathered over the model's NCCL communicator, every other rank's buffer
+// opened here (peer access over NVLink). Collective: every rank creates its
+// contexts in the same order.
+void ContextImpl::setup_tp_exchange() {
+  const int n = m->tp_size, me = m->tp_rank;
+  const mlb_config& cf = m->cfg;
+  auto al = [](long long v) { return (v + 255) / 256 * 256; };
+  TpXchg x{};
+  x.n = n;
+  x.me = me;
+  x.dim = cf.dim;
+  x.vocab = cf.vocab_size;
+  x.parts_off = 0;
+  x.logits_off = al(2LL * n * cf.dim * 8);  // tagged 8-byte words
+  x.keys_off = al(x.logits_off + (long long)cf.vocab_size * 4);
+  x.kflags_off = al(x.keys_off + (long long)n * 8);
+  const long long total = al(x.kflags_off + (long long)n * 4);
+  xchg.alloc((size_t)total);
+  MLB_CUDA(cudaMemset(xchg.p, 0, (size_t)total));
+  cudaIpcMemHandle_t h;
+  MLB_CUDA(cudaIpcGetMemHandle(&h, xchg.p));
+  DevBuf hb((size_t)n * sizeof(h));
+  MLB_CUDA(cudaMemcpy(hb.as<uint8_t>() + (size_t)me * sizeof(h), &h, sizeof(h),
+                      cudaMemcpyHostToDevice));
+  MLB_NCCL(ncclAllGather(hb.as<uint8_t>() + (size_t)me * sizeof(h), hb.p, sizeof(h), ncclChar,
+                         m->comm, stream));
+  MLB_CUDA(cudaStreamSynchronize(stream));
+  std::vector<cudaIpcMemHandle_t> all(n);
+  MLB_CUDA(cudaMemcpy(all.data(), hb.p, (size_t)n * sizeof(h), cudaMemcpyDeviceToHost));
+  for (int r = 0; r < n; ++r) {
+    if (r == me) {
+      x.peers[r] = xchg.as<uint8_t>();
+      continue;
+    }
+    void* p = nullptr;
+    MLB_CUDA(cudaIpcOpenMemHandle(&p, all[r], cudaIpcMemLazyEnablePeerAccess));
+    tp_opened.push_back(p);
+    x.peers[r] = static_cast<uint8_t*>(p);
+  }
+  tpx = x;
+  tp_desc.alloc(sizeof(TpXchg));
+  MLB_CUDA(cudaMemcpy(tp_desc.p, &x, sizeof(TpXchg), cudaMemcpyHostToDevice));
+  tp_gen.alloc(2 * sizeof(unsigned int));
+  MLB_CUDA(cudaMemset(tp_gen.p, 0, 2 * sizeof(unsigned int)));
+  // every rank's buffer is zeroed and mapped before any rank's first step
+  MLB_NCCL(ncclAllReduce(hb.p, hb.p, 1, ncclChar, ncclMax, m->comm, stream));
+  MLB_CUDA(cudaStreamSynchronize(stream));
 }
 
 // Ends a step: the greedy token of the fused argmax becomes the next input
@@ -945,7 +1037,7 @@ void context_step_async(ContextImpl& c, int token, int pos) {
 void context_forward_token(ContextImpl& c, int token, int pos, float* logits_host) {
   context_step_async(c, token, pos);
   const size_t nb = (size_t)c.m->cfg.vocab_size * 4;
-  MLB_CUDA(cudaMemcpyAsync(c.h_logits, c.logits.p, nb, cudaMemcpyDeviceToHost, c.stream));
+  MLB_CUDA(cudaMemcpyAsync(c.h_logits, c.logits_dev(), nb, cudaMemcpyDeviceToHost, c.stream));
   MLB_CUDA(cudaStreamSynchronize(c.stream));
   c.check_status();
   std::memcpy(logits_host, c.h_logits, nb);

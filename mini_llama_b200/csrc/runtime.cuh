@@ -91,6 +91,13 @@ struct ContextImpl {
   // words and attention workspace. use_step selects it over the per-op graph.
   StepPlan step;
   DevBuf step_phases, step_sync, step_attn_ws, step_attn_cnt;
+  // tensor-parallel step kernel: this rank's exchange buffer, the other
+  // ranks' buffers mapped here, the exchange descriptor and step counter
+  DevBuf xchg, tp_desc, tp_gen;
+  TpXchg tpx{};
+  std::vector<void*> tp_opened;  // peer mappings to close
+  void setup_tp_exchange();
+  const float* logits_dev() const;  // where a step leaves the full logits
   bool use_step = false;
   bool direct_launch = false;  // step kernel launched without a graph
   void plan_step();

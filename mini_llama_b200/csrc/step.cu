@@ -69,6 +69,9 @@ struct StepShared {
   int run_t[kWinRuns], run_grp[kWinRuns], run_cc0[kWinRuns];
   int nruns;
   int flag;
+  unsigned int tp_gen0;  // exchange steps completed before this decode step
+  unsigned int tp_kgen0; // decode steps completed before this one
+  int tp_fail;           // a tagged read gave up
 };
 
 __device__ __forceinline__ unsigned int ld_acquire_u32(const unsigned int* p) {
@@ -114,6 +117,42 @@ __device__ bool grid_barrier(unsigned int* counter, unsigned int k, DeviceStatus
   const int ok = *flag;
   __syncthreads();
   return ok != 0;
+}
+
+__device__ __forceinline__ unsigned int ld_acquire_sys_u32(const unsigned int* p) {
+  unsigned int v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void red_release_sys_add(unsigned int* p, unsigned int v) {
+  asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ unsigned int ld_relaxed_sys_u32(const unsigned int* p) {
+  unsigned int v;
+  asm volatile("ld.relaxed.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Tensor parallel, one thread: wait (bounded) until c[r] >= target for every
+// rank r other than this one (skip: include this rank too), polling relaxed
+// and acquiring once at the end. Returns false on timeout or a recorded error.
+__device__ __forceinline__ bool tp_wait_all(const TpXchg* x, long long off, unsigned int target,
+                                            bool include_self, DeviceStatus* st, int where) {
+  const unsigned int* c = reinterpret_cast<const unsigned int*>(x->peers[x->me] + off);
+  const long long t0 = clock64();
+  for (int r = 0; r < x->n; ++r) {
+    if (r == x->me && !include_self) continue;
+    while ((int)(ld_relaxed_sys_u32(c + r) - target) < 0) {
+      if (*(volatile int*)&st->code != 0) return false;
+      if (clock64() - t0 > kWaitCycles) {
+        record_error(st, MLB_ERR_TIMEOUT, where);
+        return false;
+      }
+    }
+  }
+  asm volatile("fence.acq_rel.sys;" ::: "memory");
+  return true;
 }
 
 // ------------------------------------------------------------ weight ring
@@ -215,13 +254,34 @@ __device__ bool gemv_phase(StepShared& sh, StepPhase& cur, uint8_t* scratch, Rin
   const int G = gridDim.x;
   const int cb = cta_start(blockIdx.x, G, g.ntiles, g.nchunks, g.gc, g.ngroups);
   const int ce = cta_start(blockIdx.x + 1, G, g.ntiles, g.nchunks, g.gc, g.ngroups);
-  if (cb >= ce) return true;
-  const GemvScratch sc = gemv_scratch<QT>(scratch, g);
   const float* x = g.x ? g.x : a.embedding + (size_t)(*a.token) * a.dim;
+  TpSum tps{};
+  if (g.x_slot >= 0) {
+    tps.parts = reinterpret_cast<const uint2*>(a.tp->peers[a.tp->me] + a.tp->parts_off) +
+                (size_t)g.x_slot * a.tp->n * a.tp->dim;
+    tps.nparts = a.tp->n;
+    tps.ldp = a.tp->dim;
+    tps.tag = sh.tp_gen0 + (unsigned int)g.x_ar + 1u;
+    tps.store = g.x_store;
+    tps.status = a.status;
+    tps.failed = &sh.tp_fail;
+  }
+  if (g.tp_ar >= 0 && threadIdx.x == 0)  // this phase's exchange step tag (read after syncs)
+    cur.g.epi.tp_tag = sh.tp_gen0 + (unsigned int)g.tp_ar + 1u;
+  if (cb >= ce) {
+    // no tiles here, but this CTA's slice of the summed residual is still owed
+    if (g.x_slot >= 0 && tps.store) {
+      tp_store_slice(x, g.k, tps);
+      __syncthreads();
+      if (sh.tp_fail) return false;
+    }
+    return true;
+  }
+  const GemvScratch sc = gemv_scratch<QT>(scratch, g);
   const int g0 = sb_decode(cb, g.ntiles, g.nchunks, g.gc).grp;
   const int g1 = sb_decode(ce - 1, g.ntiles, g.nchunks, g.gc).grp;
   stage_x_m1<QT>(x, g.k, g.norm_w, g.eps, g.gc, g.nchunks, g0, g1, sc.frag, sc.side, sh.part,
-                 sh.inv_rms);
+                 sh.inv_rms, g.x_slot >= 0 ? &tps : nullptr);
   // residual of the first layer: the embedding row (patched before the first
   // barrier below, read only after it)
   if (threadIdx.x == 0 && g.epi.kind == kEpiResidual && g.epi.resid == nullptr)
@@ -237,6 +297,7 @@ __device__ bool gemv_phase(StepShared& sh, StepPhase& cur, uint8_t* scratch, Rin
     build_window_par(wb, ce, g.ntiles, g.nchunks, g.gc, g.ngroups, kWinRuns, win_sbs<1>(), rt,
                      &sh.nruns);
     __syncthreads();  // run table (and, first time, the staged x) visible
+    if (sh.tp_fail) return false;  // a tagged read of the staged sum gave up (block-uniform)
     const int nruns = sh.nruns;
     const int we = sh.run_u0[nruns];
     if (!consume_window<QT, 1>(cb, wb, we, g.ntiles, g.nchunks, g.gc, g0, sc.frag, sc.side,
@@ -526,7 +587,12 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
   uint8_t* scratch = reinterpret_cast<uint8_t*>(bars + kStepWarps * kMaxStages);
   StepShared& sh = *reinterpret_cast<StepShared*>(scratch + a.scratch_bytes);
   // an earlier step failed: do nothing (one read, shared by the block)
-  if (threadIdx.x == 0) sh.flag = *(volatile int*)&a.status->code;
+  if (threadIdx.x == 0) {
+    sh.flag = *(volatile int*)&a.status->code;
+    sh.tp_gen0 = a.tp ? *(volatile unsigned int*)a.tp_gen : 0u;
+    sh.tp_fail = 0;
+    sh.tp_kgen0 = a.tp ? *(volatile unsigned int*)(a.tp_gen + 1) : 0u;
+  }
   __syncthreads();
   if (sh.flag != 0) return;
   __syncthreads();
@@ -557,6 +623,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
   for (int i = threadIdx.x; i < kDesc16; i += kStepThreads)
     reinterpret_cast<int4*>(&sh.cur[0])[i] = __ldg(reinterpret_cast<const int4*>(a.phases) + i);
   bool ok = true;
+  unsigned int nbar = 0;  // grid barriers passed (fused TP barriers do not count)
   for (int p = 0; p < a.nphases && ok; ++p) {
     StepPhase& cur = sh.cur[p & 1];
     if (threadIdx.x == 0) sh.flag = 1;
@@ -572,8 +639,12 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
     else
       ok = attn_phase<HG>(sh, cur, scratch, a);
     cp_async_wait_all();
-    if (ok && p + 1 < a.nphases)
-      ok = grid_barrier(&a.sync[0], (unsigned int)(p + 1), a.status, 100 + p, &sh.flag);
+    if (cur.kind == kPhaseGemv && cur.g.tp_ar >= 0) {
+      // tensor parallel: the next phase reads this one's partial sums as
+      // tagged words and waits for the tags itself; no barrier
+    } else if (ok && p + 1 < a.nphases) {
+      ok = grid_barrier(&a.sync[0], ++nbar, a.status, 100 + p, &sh.flag);
+    }
   }
   if (!ok) {
     if (lane == 0) ring_drain(rg.bars, rg.stages, rg.slot, rg.parity, rg.inflight);
@@ -586,7 +657,30 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
     __threadfence();
     if (atomicAdd(&a.sync[1], 1u) == gridDim.x - 1) {
       __threadfence();
-      const unsigned long long key = atomicOr(a.argmax_key, 0ull);
+      unsigned long long key = atomicOr(a.argmax_key, 0ull);
+      if (a.tp) {
+        // the greedy token across vocabulary shards: every rank's key into
+        // every buffer, the last exchange step of the decode step, then the
+        // same maximum on every rank
+        const TpXchg* x = a.tp;
+        for (int r = 0; r < x->n; ++r)
+          reinterpret_cast<unsigned long long*>(x->peers[r] + x->keys_off)[x->me] = key;
+        __threadfence_system();
+        for (int r = 0; r < x->n; ++r)
+          red_release_sys_add(reinterpret_cast<unsigned int*>(x->peers[r] + x->kflags_off) + x->me,
+                              1u);
+        const unsigned int kdone = sh.tp_kgen0 + 1u;
+        if (tp_wait_all(x, x->kflags_off, kdone, true, a.status, 299)) {
+          const unsigned long long* keys =
+              reinterpret_cast<const unsigned long long*>(x->peers[x->me] + x->keys_off);
+          for (int r = 0; r < x->n; ++r) {
+            const unsigned long long kr = __ldcg(keys + r);
+            key = kr > key ? kr : key;
+          }
+        }
+        a.tp_gen[0] = sh.tp_gen0 + (unsigned int)a.tp_steps;
+        a.tp_gen[1] = kdone;
+      }
       const int t = argmax_index_of(key);
       *a.token = t;
       a.tokens[*a.step] = t;

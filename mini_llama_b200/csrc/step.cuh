@@ -23,6 +23,14 @@ struct StepGemv {
   const float* norm_w;  // fused RMSNorm of x when non-null
   float eps;
   EpiParams epi;        // kEpiResidual with resid null: residual = the embedding row
+  // Tensor parallel: tp_ar >= 0 marks a phase whose epilogue writes exchange
+  // step tp_ar of this decode step into every rank as tagged words (no
+  // barrier follows it: readers wait for the tags); when x_slot >= 0 the input
+  // is x (or the embedding row) plus every rank's partial sums of exchange
+  // step x_ar in x_slot, and x_store receives this CTA's slice of that sum.
+  int tp_ar;
+  int x_slot, x_ar;
+  float* x_store;
 };
 
 struct StepAttn {
@@ -60,6 +68,12 @@ struct StepArgs {
   int* attn_counters;       // [KV] (zero between phases)
   unsigned int* sync;       // [0] grid-barrier arrivals, [1] end-of-step arrivals
   DeviceStatus* status;
+  // tensor parallel (null tp on one GPU): the exchange; tp_gen[0] counts the
+  // exchange steps and tp_gen[1] the decode steps completed (same on every
+  // rank); tp_steps exchange steps per decode step (two per layer)
+  const TpXchg* tp;
+  unsigned int* tp_gen;
+  int tp_steps;
 };
 
 // Launch plan of the step kernel for one context.

@@ -1,7 +1,9 @@
 """Tensor-parallel decode on 2 GPUs (skipped with fewer): the golden small
-models sharded over two ranks (NCCL all-reduce after wo and w_down,
-vocab-sharded lm_head with the greedy key reduced by MAX) against the
-reference CPU path's golden logits and token ids."""
+models sharded over two ranks, on both step paths (the persistent kernel with
+its partial sums exchanged over NVLink peer memory, and the per-op graph with
+NCCL all-reduce after wo and w_down), vocab-sharded lm_head with the greedy
+key reduced by MAX, against the reference CPU path's golden logits and token
+ids."""
 import json
 import os
 import socket
@@ -27,19 +29,20 @@ def free_port():
         return s.getsockname()[1]
 
 
+@pytest.mark.parametrize("path", ["step", "per_op"])
 @pytest.mark.parametrize("name", ["small_q4_0_gqa", "small_q4_1_neox_bias"])
-def test_two_rank_decode_matches_reference(name, tmp_path):
+def test_two_rank_decode_matches_reference(name, path, tmp_path):
     if gpus() < 2:
         pytest.skip("needs 2 GPUs")
     out = tmp_path / "tp.json"
     cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run",
            "--nnodes=1", "--nproc-per-node", "2", "--master-addr", "127.0.0.1",
            "--master-port", str(free_port()), os.path.join(ROOT, "tests", "tp_worker.py"),
-           name, str(out)]
+           name, str(out), path]
     r = subprocess.run(cmd, cwd=ROOT, capture_output=True, text=True)
     assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-4000:]
     res = json.loads(out.read_text())
-    assert not res["step_kernel"]  # tensor parallel runs the per-op graph with NCCL
+    assert res["step_kernel"] == (path == "step")
     assert res["max_err"] <= LOGIT_TOL
     n = res["prompt_len"]
     assert res["argmax"] == res["gold"]                    # teacher-forced: same inputs

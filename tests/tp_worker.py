@@ -1,7 +1,9 @@
 """One rank of a tensor-parallel decode run (launched by torch.distributed.run,
 one process per GPU) for tests/test_gpu_tp.py: loads a golden small model
-sharded over WORLD_SIZE ranks and decodes it; rank 0 writes the logits and
-token ids to the JSON file named on the command line."""
+sharded over WORLD_SIZE ranks and decodes it with the step path named on the
+command line ("step": the persistent kernel exchanging partial sums over
+NVLink peer memory; "per_op": one kernel per op with NCCL); rank 0 writes the
+logits and token ids to the JSON file named on the command line."""
 import datetime
 import json
 import os
@@ -20,7 +22,8 @@ from mini_llama_b200 import configs as C  # noqa: E402
 
 
 def main():
-    name, out = sys.argv[1], sys.argv[2]
+    name, out, path = sys.argv[1], sys.argv[2], sys.argv[3]
+    step_kernel = path == "step"
     rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
     local = int(os.environ.get("LOCAL_RANK", rank))
     torch.cuda.set_device(local)
@@ -38,13 +41,13 @@ def main():
     prompt = [int(t) for t in g["prompt"]]
     gold = [int(t) for t in g["tokens"]]
     # teacher-forced logits (every rank runs the same steps: the step holds collectives)
-    ctx = model.context()
+    ctx = model.context(step_kernel=step_kernel)
     logits, tok = [], prompt[0]
     for pos in range(len(gold)):
         logits.append(ctx.forward_token(tok, pos))
         tok = prompt[pos + 1] if pos + 1 < len(prompt) else gold[pos]
     # the on-device greedy loop
-    ctx2 = model.context()
+    ctx2 = model.context(step_kernel=step_kernel)
     for pos, t in enumerate(prompt[:-1]):
         ctx2.forward_token(t, pos)
     dev = ctx2.decode_greedy(prompt[-1], len(prompt) - 1, len(gold) - len(prompt) + 1)
