@@ -47,3 +47,24 @@ def test_two_rank_decode_matches_reference(name, path, tmp_path):
     n = res["prompt_len"]
     assert res["argmax"] == res["gold"]                    # teacher-forced: same inputs
     assert res["device_greedy"] == res["gold"][n - 1:]     # free-running on the device
+
+
+@pytest.mark.parametrize("path", ["step", "per_op"])
+def test_tp_greedy_ids_match_one_gpu(path, tmp_path):
+    """Every available rank count (2, 4, 8): a 7B-shaped model (4 layers)
+    decoded greedily at TP=N gives the single-GPU ids; logits within the bar."""
+    n = gpus()
+    if n < 2:
+        pytest.skip("needs 2 GPUs")
+    world = 8 if n >= 8 else (4 if n >= 4 else 2)
+    out = tmp_path / "tp.json"
+    cmd = ["timeout", "-k", "30", "400", sys.executable, "-m", "torch.distributed.run",
+           "--nnodes=1", "--nproc-per-node", str(world), "--master-addr", "127.0.0.1",
+           "--master-port", str(free_port()), os.path.join(ROOT, "tests", "tp_worker.py"),
+           "synth7b", str(out), path]
+    r = subprocess.run(cmd, cwd=ROOT, capture_output=True, text=True)
+    assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-4000:]
+    res = json.loads(out.read_text())
+    assert res["step_kernel"] == (path == "step")
+    assert res["tp_ids"] == res["ids"]
+    assert res["max_err"] <= LOGIT_TOL

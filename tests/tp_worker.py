@@ -21,6 +21,34 @@ import mini_llama_b200 as mlb  # noqa: E402
 from mini_llama_b200 import configs as C  # noqa: E402
 
 
+def synth_vs_single(out, step_kernel, rank, world, local, nccl_id):
+    """A Llama-2-7B-shaped model cut to 4 layers (seeded on the device, so every
+    rank and the single-GPU copy hold the same weights): greedy ids at TP=world
+    against one GPU."""
+    cfg = dict(C.LLAMA2_7B, n_layers=4, max_seq_len=256)
+    steps = 48
+    model = mlb.CudaModel(cfg, device_id=local, tp_rank=rank, tp_size=world, nccl_id=nccl_id)
+    model.synthesize(C.Q4_0, 77)
+    ctx = model.context(step_kernel=step_kernel)
+    tp_ids = ctx.decode_greedy(11, 0, steps)
+    lg = ctx.forward_token(tp_ids[-1], steps)
+    used = ctx.step_kernel()
+    ctx.close()
+    model.close()
+    dist.barrier()
+    if rank == 0:
+        one = mlb.CudaModel(cfg, device_id=local).synthesize(C.Q4_0, 77)
+        c1 = one.context()
+        ids = c1.decode_greedy(11, 0, steps)
+        l1 = c1.forward_token(ids[-1], steps)
+        with open(out, "w") as f:
+            json.dump({"tp_ids": tp_ids, "ids": ids, "step_kernel": used,
+                       "max_err": float(np.abs(lg - l1).max())}, f)
+        c1.close()
+        one.close()
+    dist.barrier()
+
+
 def main():
     name, out, path = sys.argv[1], sys.argv[2], sys.argv[3]
     step_kernel = path == "step"
@@ -30,6 +58,10 @@ def main():
     dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=120))
     obj = [mlb.nccl_unique_id() if rank == 0 else None]
     dist.broadcast_object_list(obj, src=0)
+    if name == "synth7b":
+        synth_vs_single(out, step_kernel, rank, world, local, obj[0])
+        dist.destroy_process_group()
+        return
     golden = os.path.join(ROOT, "tests", "golden")
     with open(os.path.join(golden, "golden.json")) as f:
         mt = json.load(f)[name]
