@@ -573,6 +573,10 @@ void ContextImpl::plan_step() {
     if (!step_gemv_ok(*q, grid, &why)) return no(why);
     scratch = std::max(scratch, step_gemv_scratch(*q));
   }
+  // every CTA stores its 1/grid slice of the summed residual while staging,
+  // which needs the whole input row (dim) staged as one chunk group
+  if (tp && cf.n_layers > 0 && (m->layers[0].qkv.ngroups > 1 || m->layers[0].gateup.ngroups > 1))
+    return no("tensor parallel with dim above one chunk group");
   const int stride = sb_bytes(qt);
   constexpr size_t kSmemMax = 227 * 1024;
   int stages = 0;
