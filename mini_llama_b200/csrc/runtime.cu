@@ -580,10 +580,11 @@ void ContextImpl::plan_step() {
   const int stride = sb_bytes(qt);
   constexpr size_t kSmemMax = 227 * 1024;
   int stages = 0;
+  const int nph = 5 * cf.n_layers + 1;  // per layer QKV, attention, wo, gate/up, down; lm_head
   for (int s = kRingStages; s >= 1 && !stages; --s)
-    if (step_smem_bytes(scratch, stride, s) <= kSmemMax) stages = s;
+    if (step_smem_bytes(scratch, stride, s, nph) <= kSmemMax) stages = s;
   if (!stages) return no("weight ring and scratch exceed shared memory");
-  const size_t smem = step_smem_bytes(scratch, stride, stages);
+  const size_t smem = step_smem_bytes(scratch, stride, stages, nph);
   if (step_max_blocks_per_sm(qt, m->q_heads / m->kv_heads, smem) < 1)
     return no("the step kernel does not fit on an SM");
 
@@ -699,8 +700,13 @@ void ContextImpl::plan_step() {
   if (tp && cf.n_layers > 0)
     tp_in(ph.back(), 1, 2 * (cf.n_layers - 1) + 1, xb.as<float>(), nullptr);
 
+  if ((int)ph.size() != nph) fail(MLB_ERR_INVALID, "decode step kernel: phase count mismatch");
   step_phases.alloc(ph.size() * sizeof(StepPhase));
   MLB_CUDA(cudaMemcpy(step_phases.p, ph.data(), ph.size() * sizeof(StepPhase),
+                      cudaMemcpyHostToDevice));
+  const std::vector<StepCta> tab = step_cta_table(ph, grid);
+  step_cta.alloc(tab.size() * sizeof(StepCta));
+  MLB_CUDA(cudaMemcpy(step_cta.p, tab.data(), tab.size() * sizeof(StepCta),
                       cudaMemcpyHostToDevice));
   step_sync.alloc(2 * sizeof(unsigned int));
   MLB_CUDA(cudaMemset(step_sync.p, 0, step_sync.bytes));
@@ -718,11 +724,13 @@ void ContextImpl::plan_step() {
   step.smem = smem;
   step.nphases = (int)ph.size();
   step.phases = step_phases.p;
+  step.cta = step_cta.p;
 }
 
 void ContextImpl::launch_step(cudaStream_t s) {
   StepArgs a{};
   a.phases = static_cast<const StepPhase*>(step.phases);
+  a.cta = static_cast<const StepCta*>(step.cta);
   a.nphases = step.nphases;
   a.sb_stride = step.sb_stride;
   a.stages = step.stages;

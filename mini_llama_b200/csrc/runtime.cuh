@@ -90,7 +90,7 @@ struct ContextImpl {
   // Persistent decode-step kernel (single GPU): plan, phase table, grid sync
   // words and attention workspace. use_step selects it over the per-op graph.
   StepPlan step;
-  DevBuf step_phases, step_sync, step_attn_ws, step_attn_cnt;
+  DevBuf step_phases, step_cta, step_sync, step_attn_ws, step_attn_cnt;
   // tensor-parallel step kernel: this rank's exchange buffer, the other
   // ranks' buffers mapped here, the exchange descriptor and step counter
   DevBuf xchg, tp_desc, tp_gen;

@@ -72,6 +72,7 @@ struct StepShared {
   unsigned int tp_gen0;  // exchange steps completed before this decode step
   unsigned int tp_kgen0; // decode steps completed before this one
   int tp_fail;           // a tagged read gave up
+  int pos, token;        // the step's position and input token (read once)
 };
 
 __device__ __forceinline__ unsigned int ld_acquire_u32(const unsigned int* p) {
@@ -169,59 +170,52 @@ struct Ring {
 };
 
 // The producer side: the next super-block this warp will need, over all
-// projection phases in order, as a pointer walk within each phase.
+// projection phases in order, as a pointer walk within each phase. The CTA's
+// per-phase ranges come from its table in shared memory (attention phases have
+// empty ranges), so crossing into the next phase costs no global load.
 struct Producer {
   int p;               // phase of the next super-block (nphases: none left)
   const uint8_t* next; // its address
-  long long step;      // 16 super-blocks of phase p, in bytes
   int left;            // super-blocks of phase p left for this warp
-  int sbb;
 };
 
-__device__ __noinline__ void producer_seek(Producer& pr, const StepPhase* ph, int nph,
-                                           int warp) {
-  const int G = gridDim.x, c = blockIdx.x;
+// Lane 0: from phase pr.p on, the first phase with super-blocks for this warp.
+__device__ __forceinline__ void producer_seek(Producer& pr, const StepCta* tab, int nph,
+                                              int warp, int sbb) {
   while (pr.p < nph) {
-    if (__ldg(&ph[pr.p].kind) == kPhaseGemv) {
-      const StepGemv& g = ph[pr.p].g;
-      const int nt = __ldg(&g.ntiles), nc = __ldg(&g.nchunks), gc = __ldg(&g.gc);
-      const int ng = __ldg(&g.ngroups);
-      const int cb = cta_start(c, G, nt, nc, gc, ng), ce = cta_start(c + 1, G, nt, nc, gc, ng);
-      if (cb + warp < ce) {
-        pr.sbb = __ldg(&g.sbb);
-        pr.next = reinterpret_cast<const uint8_t*>(__ldg(reinterpret_cast<const unsigned long long*>(
-                      &g.w))) + (size_t)(cb + warp) * pr.sbb;
-        pr.step = (long long)kStepWarps * pr.sbb;
-        pr.left = (ce - cb - warp + kStepWarps - 1) / kStepWarps;
-        return;
-      }
+    const StepCta& e = tab[pr.p];
+    const int n = e.ce - e.cb - warp;
+    if (n > 0) {
+      pr.next = e.w + (size_t)warp * sbb;
+      pr.left = (n + kStepWarps - 1) / kStepWarps;
+      return;
     }
-    ++pr.p;
+    pr.p = e.next;
   }
 }
 
 // Lane 0: the producer's next super-block into ring slot `slot`, if any is left.
 __device__ __forceinline__ void producer_issue(Producer& pr, Ring& rg, int slot,
-                                               const StepPhase* ph, int nph, int warp) {
+                                               const StepCta* tab, int nph, int warp, int sbb) {
   if (pr.p >= nph) return;
   uint64_t* bar = rg.bars + slot;
-  mbar_arrive_expect_tx(bar, pr.sbb);
-  bulk_g2s(rg.base + (size_t)slot * rg.stride, pr.next, pr.sbb, bar);
+  mbar_arrive_expect_tx(bar, sbb);
+  bulk_g2s(rg.base + (size_t)slot * rg.stride, pr.next, sbb, bar);
   ++rg.inflight;
-  pr.next += pr.step;
+  pr.next += (size_t)kStepWarps * sbb;
   if (--pr.left == 0) {
-    ++pr.p;
-    producer_seek(pr, ph, nph, warp);
+    pr.p = tab[pr.p].next;
+    producer_seek(pr, tab, nph, warp, sbb);
   }
 }
 
 struct StepRefill {
   Producer* pr;
   Ring* rg;
-  const StepPhase* ph;
-  int nph, warp;
+  const StepCta* tab;
+  int nph, warp, sbb;
   __device__ __forceinline__ void operator()(int slot) {
-    producer_issue(*pr, *rg, slot, ph, nph, warp);
+    producer_issue(*pr, *rg, slot, tab, nph, warp, sbb);
   }
 };
 
@@ -247,14 +241,12 @@ __device__ __forceinline__ GemvScratch gemv_scratch(uint8_t* scratch, const Step
 
 // Returns false (block-uniform) when a wait failed; the caller drains and exits.
 template <int QT>
-__device__ bool gemv_phase(StepShared& sh, StepPhase& cur, uint8_t* scratch, Ring& rg,
-                           Producer& pr, const StepArgs& a) {
+__device__ bool gemv_phase(StepShared& sh, StepPhase& cur, const StepCta& ct, uint8_t* scratch,
+                           Ring& rg, Producer& pr, const StepCta* tab, const StepArgs& a) {
   const StepGemv& g = cur.g;
   const int warp = threadIdx.x >> 5;
-  const int G = gridDim.x;
-  const int cb = cta_start(blockIdx.x, G, g.ntiles, g.nchunks, g.gc, g.ngroups);
-  const int ce = cta_start(blockIdx.x + 1, G, g.ntiles, g.nchunks, g.gc, g.ngroups);
-  const float* x = g.x ? g.x : a.embedding + (size_t)(*a.token) * a.dim;
+  const int cb = ct.cb, ce = ct.ce;
+  const float* x = g.x ? g.x : a.embedding + (size_t)sh.token * a.dim;
   TpSum tps{};
   if (g.x_slot >= 0) {
     tps.parts = reinterpret_cast<const uint2*>(a.tp->peers[a.tp->me] + a.tp->parts_off) +
@@ -278,18 +270,17 @@ __device__ bool gemv_phase(StepShared& sh, StepPhase& cur, uint8_t* scratch, Rin
     return true;
   }
   const GemvScratch sc = gemv_scratch<QT>(scratch, g);
-  const int g0 = sb_decode(cb, g.ntiles, g.nchunks, g.gc).grp;
-  const int g1 = sb_decode(ce - 1, g.ntiles, g.nchunks, g.gc).grp;
+  const int g0 = ct.g0, g1 = ct.g1;
   stage_x_m1<QT>(x, g.k, g.norm_w, g.eps, g.gc, g.nchunks, g0, g1, sc.frag, sc.side, sh.part,
                  sh.inv_rms, g.x_slot >= 0 ? &tps : nullptr);
   // residual of the first layer: the embedding row (patched before the first
   // barrier below, read only after it)
   if (threadIdx.x == 0 && g.epi.kind == kEpiResidual && g.epi.resid == nullptr)
-    cur.g.epi.resid = a.embedding + (size_t)(*a.token) * a.dim;
+    cur.g.epi.resid = a.embedding + (size_t)sh.token * a.dim;
   const EpiParams& epi = cur.g.epi;
   RunTable rt{sh.run_u0, sh.run_t, sh.run_grp, sh.run_cc0};
   const FinishGeom fg{g.ntiles, g.nchunks, g.gc, g.ngroups, 1};
-  StepRefill refill{&pr, &rg, a.phases, a.nphases, warp};
+  StepRefill refill{&pr, &rg, tab, a.nphases, warp, a.sb_stride};
 
   // The CTA range in windows; warp w keeps taking super-blocks cb + w,
   // cb + w + 16, ... across windows (and its producer across phases).
@@ -512,7 +503,7 @@ __device__ bool attn_phase(StepShared& sh, const StepPhase& cur, uint8_t* scratc
   const StepAttn& at = cur.at;
   const int D = at.D, rec = attn_rec(D);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int pos = *a.pos;
+  const int pos = sh.pos;
   const int n = pos + 1;
   const int v_end = at.include_current_v ? (int)n : pos;
   const int G = gridDim.x;
@@ -586,8 +577,17 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
       reinterpret_cast<uint64_t*>(smem + (size_t)kStepWarps * a.stages * a.sb_stride);
   uint8_t* scratch = reinterpret_cast<uint8_t*>(bars + kStepWarps * kMaxStages);
   StepShared& sh = *reinterpret_cast<StepShared*>(scratch + a.scratch_bytes);
+  StepCta* tab = reinterpret_cast<StepCta*>(reinterpret_cast<uint8_t*>(&sh) +
+                                            (sizeof(StepShared) + 15) / 16 * 16);
+  // this CTA's column of the phase table
+  for (int i = threadIdx.x; i < 2 * a.nphases; i += kStepThreads)
+    reinterpret_cast<int4*>(tab)[i] =
+        __ldg(reinterpret_cast<const int4*>(a.cta + (size_t)(i >> 1) * gridDim.x + blockIdx.x) +
+              (i & 1));
   // an earlier step failed: do nothing (one read, shared by the block)
   if (threadIdx.x == 0) {
+    sh.pos = *a.pos;
+    sh.token = *a.token;
     sh.flag = *(volatile int*)&a.status->code;
     sh.tp_gen0 = a.tp ? *(volatile unsigned int*)a.tp_gen : 0u;
     sh.tp_fail = 0;
@@ -611,8 +611,9 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
     for (int s = 0; s < a.stages; ++s) mbar_init(&rg.bars[s], 1);
     fence_mbar_init();
     fence_proxy_async_smem();
-    producer_seek(pr, a.phases, a.nphases, warp);
-    for (int s = 0; s < a.stages; ++s) producer_issue(pr, rg, s, a.phases, a.nphases, warp);
+    producer_seek(pr, tab, a.nphases, warp, a.sb_stride);
+    for (int s = 0; s < a.stages; ++s)
+      producer_issue(pr, rg, s, tab, a.nphases, warp, a.sb_stride);
   }
   __syncwarp();
 
@@ -635,7 +636,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
       cp_async_commit();
     }
     if (cur.kind == kPhaseGemv)
-      ok = gemv_phase<QT>(sh, cur, scratch, rg, pr, a);
+      ok = gemv_phase<QT>(sh, cur, tab[p], scratch, rg, pr, tab, a);
     else
       ok = attn_phase<HG>(sh, cur, scratch, a);
     cp_async_wait_all();
@@ -717,9 +718,34 @@ size_t round_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
 }  // namespace
 
-size_t step_smem_bytes(int scratch_bytes, int sb_stride, int stages) {
+size_t step_smem_bytes(int scratch_bytes, int sb_stride, int stages, int nphases) {
   return (size_t)kStepWarps * stages * sb_stride + (size_t)kStepWarps * kMaxStages * 8 +
-         (size_t)scratch_bytes + round_up(sizeof(StepShared), 16);
+         (size_t)scratch_bytes + round_up(sizeof(StepShared), 16) +
+         (size_t)nphases * sizeof(StepCta);
+}
+
+std::vector<StepCta> step_cta_table(const std::vector<StepPhase>& ph, int grid) {
+  const int nph = (int)ph.size();
+  std::vector<StepCta> t((size_t)nph * grid);
+  int next = nph;  // the first GEMV phase after the current one, walking backwards
+  for (int i = nph - 1; i >= 0; --i) {
+    for (int c = 0; c < grid; ++c) {
+      StepCta& e = t[(size_t)i * grid + c];
+      e = StepCta{};
+      e.next = next;
+      if (ph[i].kind != kPhaseGemv) continue;
+      const StepGemv& g = ph[i].g;
+      e.cb = cta_start(c, grid, g.ntiles, g.nchunks, g.gc, g.ngroups);
+      e.ce = cta_start(c + 1, grid, g.ntiles, g.nchunks, g.gc, g.ngroups);
+      e.w = g.w + (size_t)e.cb * g.sbb;
+      if (e.cb < e.ce) {
+        e.g0 = sb_decode(e.cb, g.ntiles, g.nchunks, g.gc).grp;
+        e.g1 = sb_decode(e.ce - 1, g.ntiles, g.nchunks, g.gc).grp;
+      }
+    }
+    if (ph[i].kind == kPhaseGemv) next = i;
+  }
+  return t;
 }
 
 int step_gemv_scratch(const QMatrix& m) {

@@ -7,6 +7,8 @@
 // phase boundaries (see step.cu).
 #pragma once
 
+#include <vector>
+
 #include "gemv.cuh"
 
 namespace mlb {
@@ -49,8 +51,19 @@ struct alignas(16) StepPhase {  // copied into shared memory 16 bytes at a time
   StepAttn at;
 };
 
+// One CTA's share of one GEMV phase, computed on the host (entry
+// [phase][cta]; entries of attention phases are unused).
+struct alignas(16) StepCta {
+  const uint8_t* w;  // its first super-block
+  int cb, ce;        // super-block range [cb, ce)
+  int g0, g1;        // chunk groups the range spans
+  int next;          // the next GEMV phase (nphases: none)
+  int pad;
+};
+
 struct StepArgs {
   const StepPhase* phases;  // device array
+  const StepCta* cta;       // device array [nphases][grid]
   int nphases;
   int sb_stride;            // bytes per ring slot (largest super-block)
   int stages;               // ring slots per warp
@@ -84,11 +97,12 @@ struct StepPlan {
   size_t smem = 0;
   int nphases = 0;
   void* phases = nullptr;   // device StepPhase array (owned by the context)
+  void* cta = nullptr;      // device StepCta array [nphases][grid] (owned by the context)
   size_t attn_ws_floats = 0;
 };
 
 // Shared memory the step kernel needs for a scratch size and ring shape.
-size_t step_smem_bytes(int scratch_bytes, int sb_stride, int stages);
+size_t step_smem_bytes(int scratch_bytes, int sb_stride, int stages, int nphases);
 // Scratch one GEMV phase needs (staged x, run slots, reduction space).
 int step_gemv_scratch(const QMatrix& m);
 // Scratch the attention phase needs.
@@ -97,6 +111,9 @@ int step_attn_scratch(int gq, int D);
 // two chunk groups per CTA range); otherwise sets why.
 bool step_gemv_ok(const QMatrix& m, int grid, std::string* why);
 bool step_attn_ok(int H, int KV, int D, std::string* why);
+
+// The per-CTA table of a phase list on `grid` CTAs.
+std::vector<StepCta> step_cta_table(const std::vector<StepPhase>& ph, int grid);
 
 // Launches one step (cooperative launch, capturable in a CUDA graph).
 void step_launch(const StepPlan& plan, const StepArgs& args, cudaStream_t stream);
