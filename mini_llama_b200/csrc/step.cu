@@ -422,8 +422,8 @@ __device__ __forceinline__ void attn_warp(const StepAttn& at, const AttnScratch&
     }
     // lane i < NV keeps (m, l) of query head hg + i / PB
     float m_run = -INFINITY, l_run = 0.0f;
-    for (int tb = t0 + warp * PB; tb < t1; tb += kStepWarps * PB) {
-      float4 kx[PB], vx[PB];
+    // K and V rows of block tb (zero past the slice)
+    auto load_block = [&](int tb, float4 (&kx)[PB], float4 (&vx)[PB]) {
 #pragma unroll
       for (int j = 0; j < PB; ++j) {
         const int t = tb + j;
@@ -432,6 +432,24 @@ __device__ __forceinline__ void attn_warp(const StepAttn& at, const AttnScratch&
         vx[j] = (dl && t < t1 && t < v_end)
                     ? __ldcg(reinterpret_cast<const float4*>(vbase + (size_t)t * row))
                     : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    };
+    // narrow passes keep the next block's rows in flight while this one is
+    // computed (wider passes have no registers to spare)
+    constexpr bool kPipe = HG <= 2;
+    float4 kn[PB], vn[PB];
+    if (kPipe) load_block(t0 + warp * PB, kn, vn);
+    for (int tb = t0 + warp * PB; tb < t1; tb += kStepWarps * PB) {
+      float4 kx[PB], vx[PB];
+      if (kPipe) {
+#pragma unroll
+        for (int j = 0; j < PB; ++j) {
+          kx[j] = kn[j];
+          vx[j] = vn[j];
+        }
+        if (tb + kStepWarps * PB < t1) load_block(tb + kStepWarps * PB, kn, vn);
+      } else {
+        load_block(tb, kx, vx);
       }
       float dv[NV];
 #pragma unroll
@@ -498,7 +516,7 @@ __device__ __forceinline__ void attn_warp(const StepAttn& at, const AttnScratch&
 }
 
 template <int HG>
-__device__ bool attn_phase(StepShared& sh, const StepPhase& cur, uint8_t* scratch,
+__device__ __noinline__ bool attn_phase(StepShared& sh, const StepPhase& cur, uint8_t* scratch,
                            const StepArgs& a) {
   const StepAttn& at = cur.at;
   const int D = at.D, rec = attn_rec(D);
@@ -548,13 +566,19 @@ __device__ bool attn_phase(StepShared& sh, const StepPhase& cur, uint8_t* scratc
         acc = fmaf(s.wpart[((size_t)i * gq + h) * rec + kRecO + d], s.ew[h * kMaxGrid + i], acc);
       dst[h * rec + kRecO + d] = acc;
     }
-    __threadfence();
+    // thread 0 publishes the CTA's record (bar.sync, then its fence: the
+    // pattern of a grid barrier) and, as the head's last slice, acquires the
+    // others' before the block reads them
     __syncthreads();
-    if (threadIdx.x == 0) sh.flag = atomicAdd(&a.attn_counters[kvh], 1) == pph - 1;
+    if (threadIdx.x == 0) {
+      __threadfence();
+      const bool last = atomicAdd(&a.attn_counters[kvh], 1) == pph - 1;
+      if (last) __threadfence();
+      sh.flag = last;
+    }
     __syncthreads();
     if (sh.flag) {
       // the last slice of the head to finish combines all slices, in order
-      __threadfence();
       attn_combine(
           s, D, gq, pph,
           [&](int h, int i) { return a.attn_ws + ((size_t)(kvh * pph + i) * gq + h) * rec; },
