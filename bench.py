@@ -456,18 +456,31 @@ def run_gemv_sweep(args):
             kind, lib, threads = "reference", r, r.threads()
         else:
             kind, lib, threads = "port", oracle.port(), 1
-        qtype = qnames[head["q"]]
-        w = C.synth_tensor(SEED, C.W_WQ, 0, qtype, head["n"], k, threads=cpu_threads())
+        # every (format, N) of the sweep at M = 1, ~2 s each; a batch of M rows is
+        # M calls on the reference's CPU path (its batch loop is sequential)
         x = np.random.default_rng(0).normal(0, 1, k).astype(np.float32)
-        t0 = time.perf_counter()
-        reps = 0
-        while time.perf_counter() - t0 < 10.0:
-            lib.linear(qtype, x, w, head["n"])
-            reps += 1
-        secs = (time.perf_counter() - t0) / reps
-        cpu = {"value": (w.nbytes + k * 4 + head["n"] * 4) / secs / 1e9, "unit": "GB/s",
+        single = {}
+        for qn in args.sweep_q.split(","):
+            qtype = qnames[qn]
+            for n in [int(v) for v in args.sweep_n.split(",")]:
+                w = C.synth_tensor(SEED, C.W_WQ, 0, qtype, n, k, threads=cpu_threads())
+                lib.linear(qtype, x, w, n)  # warm
+                t0 = time.perf_counter()
+                reps = 0
+                while time.perf_counter() - t0 < 2.0:
+                    lib.linear(qtype, x, w, n)
+                    reps += 1
+                single[(qn, n)] = ((time.perf_counter() - t0) / reps, reps, w.nbytes)
+        for r in rows:
+            secs, _, wb = single[(r["q"], r["n"])]
+            r["cpu_us"] = r["m"] * secs * 1e6
+            r["cpu_gbs"] = (wb + k * 4 + r["n"] * 4) / secs / 1e9
+        secs, reps, wb = single[(head["q"], head["n"])]
+        cpu = {"value": (wb + k * 4 + head["n"] * 4) / secs / 1e9, "unit": "GB/s",
                "cores": threads, "kind": kind,
-               "sample": f"{reps} LinearQ40 calls, {head['n']}x{k} M=1 (~10 s)"}
+               "sample": f"{reps} linear calls of {head['q']} {head['n']}x{k} M=1 (~2 s); "
+                         "every sweep row carries cpu_us / cpu_gbs from the same ~2 s timing "
+                         "of its (format, N) at M=1, times M rows"}
     print(json.dumps({
         "metric": "quant GEMV achieved HBM GB/s", "value": head["gbs"], "unit": "GB/s",
         "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": head["us"] / 1e3,
