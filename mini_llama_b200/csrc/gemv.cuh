@@ -92,6 +92,9 @@ struct EpiParams {
   const TpXchg* tp;
   int tp_slot;
   unsigned int tp_tag;  // kEpiTpPartial: tag of this exchange step (set on the device)
+  // kEpiResidual, one batch row: ss_out[tile] = the sum of squares of the
+  // tile's 16 output rows (fixed order), for the next phase's RMSNorm
+  float* ss_out;
 };
 
 #if defined(__CUDACC__)

@@ -781,6 +781,20 @@ __device__ __forceinline__ void finish_runs(const float* parts, float* red, cons
         int row = i / M, rb = i - row * M;
         if (rb < fg.rows) epilogue_row<M>(epi, t, row, rb, myred);
       }
+      if (M == 1 && epi.ss_out && epi.kind == kEpiResidual) {
+        // lane r < 16 wrote row r above; its square, summed over the 16 rows
+        // by a fixed tree (lanes 16.. add zeros and are not read)
+        float sq = 0.0f;
+        if (lane < 16 && t * 16 + lane < epi.n_out) {
+          const float yv = epi.y[t * 16 + lane];
+          sq = yv * yv;
+        }
+        sq += __shfl_xor_sync(0xffffffffu, sq, 8);
+        sq += __shfl_xor_sync(0xffffffffu, sq, 4);
+        sq += __shfl_xor_sync(0xffffffffu, sq, 2);
+        sq += __shfl_xor_sync(0xffffffffu, sq, 1);
+        if (lane == 0) epi.ss_out[t] = sq;
+      }
       if (epi.argmax_key) {
         unsigned long long key = 0ull;
         if (lane < 16 && t * 16 + lane < epi.n_out)

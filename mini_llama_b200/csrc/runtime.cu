@@ -614,6 +614,20 @@ void ContextImpl::plan_step() {
   };
   int* d_pos = scalars.as<int>() + 1;
   if (tp) setup_tp_exchange();
+  // one GPU: the residual epilogues of wo and w_down leave per-tile sums of
+  // squares of x, from which the next RMSNorm reads its statistic
+  const int ss_n = (cf.dim + kTileRows - 1) / kTileRows;
+  float* ss_xa = nullptr;
+  float* ss_xb = nullptr;
+  if (!tp) {
+    ss_x.alloc((size_t)2 * ss_n * 4);
+    ss_xa = ss_x.as<float>();
+    ss_xb = ss_xa + ss_n;
+  }
+  auto ss_in = [&](StepPhase& p, const float* ss) {
+    p.g.ss_in = ss;
+    p.g.ss_n = ss ? ss_n : 0;
+  };
   const TpXchg* tpd = tp ? tp_desc.as<TpXchg>() : nullptr;
   // Tensor parallel: exchange step 2l is layer l's wo partial sums (slot 0),
   // 2l + 1 its w_down partial sums (slot 1). The producing phase ends with the
@@ -644,6 +658,7 @@ void ContextImpl::plan_step() {
     e.q_out = q.as<float>();
     gemv(L.qkv, x_in, L.attn_norm.as<float>(), e);
     if (tp && l > 0) tp_in(ph.back(), 1, 2 * (l - 1) + 1, xb.as<float>(), xa.as<float>());
+    if (l > 0) ss_in(ph.back(), ss_xa);
 
     StepPhase a{};
     a.kind = kPhaseAttn;
@@ -666,6 +681,7 @@ void ContextImpl::plan_step() {
     eo.n_out = cf.dim;
     eo.tp = tpd;
     eo.tp_slot = 0;
+    eo.ss_out = ss_xb;
     gemv(L.wo, attn.as<float>(), nullptr, eo);
     if (tp) ph.back().g.tp_ar = 2 * l;
 
@@ -676,6 +692,7 @@ void ContextImpl::plan_step() {
     eg.n_out = m->ffn_rows;
     gemv(L.gateup, xb.as<float>(), L.ffn_norm.as<float>(), eg);
     if (tp) tp_in(ph.back(), 0, 2 * l, x_in, xb.as<float>());
+    ss_in(ph.back(), ss_xb);
 
     EpiParams ed{};
     ed.kind = tp ? kEpiTpPartial : kEpiResidual;
@@ -685,6 +702,7 @@ void ContextImpl::plan_step() {
     ed.n_out = cf.dim;
     ed.tp = tpd;
     ed.tp_slot = 1;
+    ed.ss_out = ss_xa;
     gemv(L.down, hidden.as<float>(), nullptr, ed);
     if (tp) ph.back().g.tp_ar = 2 * l + 1;
   }
@@ -697,6 +715,7 @@ void ContextImpl::plan_step() {
   el.argmax_base = m->vocab_row0;
   el.tp = tpd;
   gemv(m->lm_head, cf.n_layers == 0 ? nullptr : xa.as<float>(), m->final_norm.as<float>(), el);
+  if (cf.n_layers > 0) ss_in(ph.back(), ss_xa);
   if (tp && cf.n_layers > 0)
     tp_in(ph.back(), 1, 2 * (cf.n_layers - 1) + 1, xb.as<float>(), nullptr);
 

@@ -75,6 +75,7 @@ struct ContextImpl {
   cudaStream_t stream = nullptr;
   DevBuf keys, values;        // [L][S][KV_local][D]
   DevBuf xa, xb, y, q, attn, hidden, logits_local, logits;
+  DevBuf ss_x;  // step kernel: per-tile sums of squares of xa, then of xb
   DevBuf gemv_ws, gemv_cnt, attn_ws, attn_cnt, status;
   DevBuf scalars;             // int: token, pos, step, next token ; then tokens[max_seq]
   DevBuf argmax_key;          // u64 packed (logit, index) of the step's greedy argmax

@@ -60,6 +60,23 @@ struct AttnShape {
   static constexpr int NV = HG * PB;          // scores per block (<= 16)
 };
 
+// A warp's weight-stream producer: its walk over runs (lane 0's, in shared
+// memory; see producer_seek).
+struct Producer {
+  int p;       // phase of the next run (nphases: none left)
+  int seg;     // segment of the CTA range (one per chunk group)
+  int sbase;   // its first super-block, relative to the range start
+  int tw, Tw;  // the window: first tile (segment-relative), tile count
+  int c;       // chunk: the run is chunk c of the window's Tw tiles
+};
+
+// The producer's current run in registers (lane 0's): `left` super-blocks
+// more, `next` the next one's address, `step` bytes between them (one tile).
+struct ProducerRun {
+  const uint8_t* next;
+  int step, left;
+};
+
 // Shared state of one CTA besides the ring and the scratch region.
 struct StepShared {
   StepPhase cur[2];  // this phase's descriptor and the next one's (prefetched)
@@ -73,6 +90,7 @@ struct StepShared {
   unsigned int tp_kgen0; // decode steps completed before this one
   int tp_fail;           // a tagged read gave up
   int pos, token;        // the step's position and input token (read once)
+  Producer prod[kStepWarps];  // each warp's producer (lane 0 reads and writes it)
 };
 
 __device__ __forceinline__ unsigned int ld_acquire_u32(const unsigned int* p) {
@@ -169,53 +187,105 @@ struct Ring {
   int inflight;      // copies issued and not yet consumed (lane 0's count)
 };
 
-// The producer side: the next super-block this warp will need, over all
-// projection phases in order, as a pointer walk within each phase. The CTA's
-// per-phase ranges come from its table in shared memory (attention phases have
-// empty ranges), so crossing into the next phase costs no global load.
-struct Producer {
-  int p;               // phase of the next super-block (nphases: none left)
-  const uint8_t* next; // its address
-  int left;            // super-blocks of phase p left for this warp
-};
+// Tiles in the window of a segment that starts `rem` tiles before the end of
+// the segment: whole tiles, at most kWinRuns of them and at most win_sbs
+// super-blocks (the producer and the consumer use the same rule).
+__device__ __forceinline__ int win_tiles(int rem, int nc) {
+  return max(1, min(min(rem, kWinRuns), win_sbs<1>() / nc));
+}
+
+// The producer side (lane 0's): the next super-block this warp will need,
+// over all projection phases in order. The CTA's per-phase ranges come from
+// its table in shared memory (attention phases have empty ranges), so
+// crossing into the next phase costs no global load. Each segment of a range
+// (one chunk group) runs chunk-major: in each window of tiles, warp w takes
+// chunk w of every tile, then chunk w + 16, ... A run (one chunk of a
+// window's tiles) is a pointer walk held in registers; the walk over runs is
+// kept in shared memory (Producer).
+
+// Lane 0: the first segment from pr.seg on in which this warp has chunks;
+// false when none is left in the phase.
+__device__ __forceinline__ bool producer_segment(Producer& pr, const StepCta& e, int warp) {
+  for (; pr.seg < e.nseg; ++pr.seg) {
+    const int nc = e.nc[pr.seg], T = e.T[pr.seg];
+    if (warp < nc && T > 0) {
+      pr.sbase = pr.seg == 0 ? 0 : e.T[0] * e.nc[0];
+      pr.tw = 0;
+      pr.Tw = win_tiles(T, nc);
+      pr.c = warp;
+      return true;
+    }
+  }
+  return false;
+}
 
 // Lane 0: from phase pr.p on, the first phase with super-blocks for this warp.
 __device__ __forceinline__ void producer_seek(Producer& pr, const StepCta* tab, int nph,
-                                              int warp, int sbb) {
+                                              int warp) {
   while (pr.p < nph) {
-    const StepCta& e = tab[pr.p];
-    const int n = e.ce - e.cb - warp;
-    if (n > 0) {
-      pr.next = e.w + (size_t)warp * sbb;
-      pr.left = (n + kStepWarps - 1) / kStepWarps;
-      return;
-    }
-    pr.p = e.next;
+    pr.seg = 0;
+    if (producer_segment(pr, tab[pr.p], warp)) return;
+    pr.p = tab[pr.p].next;
   }
 }
 
+// Lane 0: the run at the producer's position.
+__device__ __forceinline__ ProducerRun producer_load_run(const Producer& pr, const StepCta* tab,
+                                                         int nph, int sbb) {
+  ProducerRun run{nullptr, 0, 0};
+  if (pr.p >= nph) return run;
+  const StepCta& e = tab[pr.p];
+  const int nc = e.nc[pr.seg];
+  run.next = e.w + ((size_t)pr.sbase + (size_t)pr.tw * nc + pr.c) * sbb;
+  run.step = nc * sbb;
+  run.left = pr.Tw;
+  return run;
+}
+
+// Lane 0: the next run: the warp's next chunk of the window, else the next
+// window, segment or phase (out of line: once per run).
+__device__ __noinline__ ProducerRun producer_next_run(Producer& pr, const StepCta* tab, int nph,
+                                                      int warp, int sbb) {
+  const StepCta& e = tab[pr.p];
+  const int nc = e.nc[pr.seg];
+  pr.c += kStepWarps;
+  if (pr.c >= nc) {
+    pr.c = warp;
+    pr.tw += pr.Tw;
+    if (pr.tw < e.T[pr.seg]) {
+      pr.Tw = win_tiles(e.T[pr.seg] - pr.tw, nc);
+    } else {
+      ++pr.seg;  // segment done: the next one, else the next phase
+      if (!producer_segment(pr, e, warp)) {
+        pr.p = e.next;
+        producer_seek(pr, tab, nph, warp);
+      }
+    }
+  }
+  return producer_load_run(pr, tab, nph, sbb);
+}
+
 // Lane 0: the producer's next super-block into ring slot `slot`, if any is left.
-__device__ __forceinline__ void producer_issue(Producer& pr, Ring& rg, int slot,
-                                               const StepCta* tab, int nph, int warp, int sbb) {
-  if (pr.p >= nph) return;
+__device__ __forceinline__ void producer_issue(Producer& pr, ProducerRun& run, Ring& rg,
+                                               int slot, const StepCta* tab, int nph, int warp,
+                                               int sbb) {
+  if (run.left <= 0) return;
   uint64_t* bar = rg.bars + slot;
   mbar_arrive_expect_tx(bar, sbb);
-  bulk_g2s(rg.base + (size_t)slot * rg.stride, pr.next, sbb, bar);
+  bulk_g2s(rg.base + (size_t)slot * rg.stride, run.next, sbb, bar);
   ++rg.inflight;
-  pr.next += (size_t)kStepWarps * sbb;
-  if (--pr.left == 0) {
-    pr.p = tab[pr.p].next;
-    producer_seek(pr, tab, nph, warp, sbb);
-  }
+  run.next += run.step;
+  if (--run.left == 0) run = producer_next_run(pr, tab, nph, warp, sbb);
 }
 
 struct StepRefill {
   Producer* pr;
+  ProducerRun* run;
   Ring* rg;
   const StepCta* tab;
   int nph, warp, sbb;
   __device__ __forceinline__ void operator()(int slot) {
-    producer_issue(*pr, *rg, slot, tab, nph, warp, sbb);
+    producer_issue(*pr, *run, *rg, slot, tab, nph, warp, sbb);
   }
 };
 
@@ -239,10 +309,122 @@ __device__ __forceinline__ GemvScratch gemv_scratch(uint8_t* scratch, const Step
   return s;
 }
 
+// One warp: the RMSNorm factor 1 / sqrt(mean x^2 + eps) from the producing
+// phase's n per-tile sums of squares, summed in one fixed order and broadcast
+// from lane 0, so every warp of every CTA gets the same bits. Eight
+// independent loads per lane per round (one L2 round trip up to 256 tiles).
+__device__ __forceinline__ float warp_inv_rms(const float* ss, int n, int k, float eps) {
+  const int lane = threadIdx.x & 31;
+  float v = 0.0f;
+  for (int i0 = 0; i0 < n; i0 += 256) {
+    float t[8];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const int i = i0 + lane + 32 * q;
+      t[q] = i < n ? __ldcg(ss + i) : 0.0f;
+    }
+#pragma unroll
+    for (int q = 0; q < 8; ++q) v += t[q];
+  }
+  v = __shfl_sync(0xffffffffu, warp_sum(v), 0);
+  const float t = __fdiv_rn(v, (float)k);
+  return __fdiv_rn(1.0f, sqrtf(__fadd_rn(t, eps)));
+}
+
+// One warp: in each segment of the CTA range, its chunks (warp, warp + 16,
+// ... of the segment's group) of x, times the RMSNorm factor (from ss) and the
+// norm weight when norm_w is set, into the group's B fragments and side data
+// (the same arithmetic as stage_x_m1). Inputs past k stage as zero.
+template <int QT>
+__device__ __forceinline__ void stage_chunks_warp(const float* x, int k, const float* norm_w,
+                                                  const float* ss, int ss_n, float eps,
+                                                  const StepCta& ct, int gc, uint32_t* frag,
+                                                  float* side) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  constexpr int SPC = side_per_chunk<QT, 1>();
+  float inv = 1.0f;
+  bool have_inv = norm_w == nullptr;
+  for (int seg = 0; seg < ct.nseg; ++seg) {
+    const int slot0 = (ct.grp[seg] - ct.grp[0]) * gc;  // staged chunk of the group's chunk 0
+    for (int cc = warp; cc < ct.nc[seg]; cc += kStepWarps) {
+      const int kc = (ct.grp[seg] * gc + cc) * kChunkK;  // first input of the chunk
+      float4 v[2], w[2];
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {  // quads lane and lane + 32 of the chunk
+        const int k0 = kc + (lane + 32 * h) * 4;
+        v[h] = load_quad(x, k0, k, false);
+        w[h] = norm_w ? load_quad(norm_w, k0, k, true) : make_float4(1.f, 1.f, 1.f, 1.f);
+      }
+      if (!have_inv) {  // its loads overlap the ones above
+        inv = warp_inv_rms(ss, ss_n, k, eps);
+        have_inv = true;
+      }
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int q4 = lane + 32 * h;
+        float e[4] = {v[h].x, v[h].y, v[h].z, v[h].w};
+        if (norm_w) {
+          const float wv[4] = {w[h].x, w[h].y, w[h].z, w[h].w};
+#pragma unroll
+          for (int i = 0; i < 4; ++i) e[i] = __fmul_rn(__fmul_rn(e[i], inv), wv[i]);
+        }
+        const float corr = block_sum8(
+            stage_quad<QT, 1>(frag + (size_t)(slot0 + cc) * frag_chunk_u32<1>(), 0, q4, e));
+        float* sd = side + (size_t)(slot0 + cc) * SPC;
+        if ((q4 & 7) == 0) sd[q4 >> 3] = corr;
+        if (QT == MLB_Q4_1) {
+          const float s4 = block_sum8((e[0] + e[1]) + (e[2] + e[3]));
+          if ((q4 & 7) == 0) sd[8 + (q4 >> 3)] = s4;
+        }
+      }
+    }
+  }
+}
+
+// One warp, one chunk-major window of Tw tiles: chunk c = warp, warp + 16, ...
+// of every tile, from the ring in the producer's order; each super-block's
+// partial goes to its window-relative index j nc + c. Returns false (warp-
+// uniform) when a wait gave up.
+template <int QT>
+__device__ __forceinline__ bool consume_chunks(int Tw, int nc, const uint32_t* frag,
+                                               const float* side, float* parts, Ring& rg,
+                                               StepRefill& refill, DeviceStatus* status,
+                                               int where) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int fl = lane < 8 ? lane : (lane & 7);  // lanes past the B columns: any valid data
+  constexpr int SPC = side_per_chunk<QT, 1>();
+  for (int c = warp; c < nc; c += kStepWarps) {
+    uint32_t B[16][2];
+    load_b(frag + (size_t)c * frag_chunk_u32<1>() + fl * kFragLaneStride, B);
+    const float* sd = side + (size_t)c * SPC;
+    for (int j = 0; j < Tw; ++j) {
+      uint64_t* bar = rg.bars + rg.slot;
+      if (!mbar_try_wait(bar, rg.parity) && !mbar_wait_bounded(bar, rg.parity, status, where))
+        return false;
+      float acc0 = 0.0f, acc1 = 0.0f;
+      sb_accumulate<QT, 1>(rg.base + (size_t)rg.slot * rg.stride, lane, B, sd, acc0, acc1);
+      store_sb_partial<1>(parts, j * nc + c, lane, acc0, acc1);
+      // every lane has read the slot; lane 0 reuses it for the stream's next
+      // super-block (the mbarrier orders the copy after the reads)
+      __syncwarp();
+      if (lane == 0) {
+        --rg.inflight;
+        refill(rg.slot);
+      }
+      if (++rg.slot == rg.stages) {
+        rg.slot = 0;
+        rg.parity ^= 1u;
+      }
+    }
+  }
+  return true;
+}
+
 // Returns false (block-uniform) when a wait failed; the caller drains and exits.
 template <int QT>
 __device__ bool gemv_phase(StepShared& sh, StepPhase& cur, const StepCta& ct, uint8_t* scratch,
-                           Ring& rg, Producer& pr, const StepCta* tab, const StepArgs& a) {
+                           Ring& rg, Producer& pr, ProducerRun& run, const StepCta* tab,
+                           const StepArgs& a) {
   const StepGemv& g = cur.g;
   const int warp = threadIdx.x >> 5;
   const int cb = ct.cb, ce = ct.ce;
@@ -270,36 +452,59 @@ __device__ bool gemv_phase(StepShared& sh, StepPhase& cur, const StepCta& ct, ui
     return true;
   }
   const GemvScratch sc = gemv_scratch<QT>(scratch, g);
-  const int g0 = ct.g0, g1 = ct.g1;
-  stage_x_m1<QT>(x, g.k, g.norm_w, g.eps, g.gc, g.nchunks, g0, g1, sc.frag, sc.side, sh.part,
-                 sh.inv_rms, g.x_slot >= 0 ? &tps : nullptr);
-  // residual of the first layer: the embedding row (patched before the first
+  const int g0 = ct.grp[0], g1 = ct.grp[ct.nseg - 1];
+  // Every warp needs only its own chunks of x: it stages them itself and
+  // starts at once (the RMSNorm statistic, when there is one, from the
+  // producing phase's per-tile sums of squares). Otherwise (statistic of the
+  // embedding row, tensor-parallel sums) the block stages all of x first.
+  if (g.x_slot < 0 && (g.norm_w == nullptr || g.ss_in != nullptr)) {
+    stage_chunks_warp<QT>(x, g.k, g.norm_w, g.ss_in, g.ss_n, g.eps, ct, g.gc, sc.frag, sc.side);
+    __syncwarp();
+  } else {
+    stage_x_m1<QT>(x, g.k, g.norm_w, g.eps, g.gc, g.nchunks, g0, g1, sc.frag, sc.side, sh.part,
+                   sh.inv_rms, g.x_slot >= 0 ? &tps : nullptr);
+    __syncthreads();
+    if (sh.tp_fail) return false;  // a tagged read of the staged sum gave up (block-uniform)
+  }
+  // residual of the first layer: the embedding row (patched before the
   // barrier below, read only after it)
   if (threadIdx.x == 0 && g.epi.kind == kEpiResidual && g.epi.resid == nullptr)
     cur.g.epi.resid = a.embedding + (size_t)sh.token * a.dim;
   const EpiParams& epi = cur.g.epi;
   RunTable rt{sh.run_u0, sh.run_t, sh.run_grp, sh.run_cc0};
   const FinishGeom fg{g.ntiles, g.nchunks, g.gc, g.ngroups, 1};
-  StepRefill refill{&pr, &rg, tab, a.nphases, warp, a.sb_stride};
+  StepRefill refill{&pr, &run, &rg, tab, a.nphases, warp, a.sb_stride};
+  constexpr int SPC = side_per_chunk<QT, 1>();
 
-  // The CTA range in windows; warp w keeps taking super-blocks cb + w,
-  // cb + w + 16, ... across windows (and its producer across phases).
-  for (int wb = cb; wb < ce;) {
-    build_window_par(wb, ce, g.ntiles, g.nchunks, g.gc, g.ngroups, kWinRuns, win_sbs<1>(), rt,
-                     &sh.nruns);
-    __syncthreads();  // run table (and, first time, the staged x) visible
-    if (sh.tp_fail) return false;  // a tagged read of the staged sum gave up (block-uniform)
-    const int nruns = sh.nruns;
-    const int we = sh.run_u0[nruns];
-    if (!consume_window<QT, 1>(cb, wb, we, g.ntiles, g.nchunks, g.gc, g0, sc.frag, sc.side,
-                               sc.parts, rg.base, rg.bars, rg.stride, rg.stages, rg.slot,
-                               rg.parity, rg.inflight, a.status, 20, refill))
-      sh.flag = 0;  // set to 1 at the phase start; every writer stores 0
-    __syncthreads();
-    if (!sh.flag) return false;  // block-uniform: read after the barrier
-    finish_runs<1>(sc.parts, sc.red, rt, nruns, wb, fg, a.ws, a.counters, epi);
-    __syncthreads();
-    wb = we;
+  // Each segment in chunk-major windows of whole tiles (the producer walks
+  // the same order).
+  int sbase = cb;
+  for (int seg = 0; seg < ct.nseg; ++seg) {
+    const int nc = ct.nc[seg], T = ct.T[seg], grp = ct.grp[seg];
+    const int slot0 = (grp - g0) * g.gc;
+    for (int tw = 0; tw < T;) {
+      const int Tw = win_tiles(T - tw, nc);
+      const int wb = sbase + tw * nc;
+      if (!consume_chunks<QT>(Tw, nc, sc.frag + (size_t)slot0 * frag_chunk_u32<1>(),
+                              sc.side + (size_t)slot0 * SPC, sc.parts, rg, refill, a.status, 20))
+        sh.flag = 0;  // set to 1 at the phase start; every writer stores 0
+      // run r of the window is tile t0 + tw + r of the group (read by
+      // finish_runs after the barrier)
+      for (int r = threadIdx.x; r <= Tw; r += blockDim.x) {
+        rt.u0[r] = wb + r * nc;
+        if (r < Tw) {
+          rt.t[r] = ct.t0[seg] + tw + r;
+          rt.grp[r] = grp;
+          rt.cc0[r] = 0;
+        }
+      }
+      __syncthreads();
+      if (!sh.flag) return false;  // block-uniform: read after the barrier
+      finish_runs<1>(sc.parts, sc.red, rt, Tw, wb, fg, a.ws, a.counters, epi);
+      __syncthreads();
+      tw += Tw;
+    }
+    sbase += T * nc;
   }
   return true;
 }
@@ -604,10 +809,11 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
   StepCta* tab = reinterpret_cast<StepCta*>(reinterpret_cast<uint8_t*>(&sh) +
                                             (sizeof(StepShared) + 15) / 16 * 16);
   // this CTA's column of the phase table
-  for (int i = threadIdx.x; i < 2 * a.nphases; i += kStepThreads)
-    reinterpret_cast<int4*>(tab)[i] =
-        __ldg(reinterpret_cast<const int4*>(a.cta + (size_t)(i >> 1) * gridDim.x + blockIdx.x) +
-              (i & 1));
+  constexpr int kCta16 = (int)(sizeof(StepCta) / 16);
+  for (int i = threadIdx.x; i < kCta16 * a.nphases; i += kStepThreads)
+    reinterpret_cast<int4*>(tab)[i] = __ldg(
+        reinterpret_cast<const int4*>(a.cta + (size_t)(i / kCta16) * gridDim.x + blockIdx.x) +
+        i % kCta16);
   // an earlier step failed: do nothing (one read, shared by the block)
   if (threadIdx.x == 0) {
     sh.pos = *a.pos;
@@ -629,15 +835,17 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
   rg.slot = 0;
   rg.parity = 0;
   rg.inflight = 0;
-  Producer pr;
-  pr.p = 0;
+  Producer& pr = sh.prod[warp];
+  ProducerRun run{nullptr, 0, 0};
+  if (lane == 0) pr.p = 0;
   if (lane == 0) {
     for (int s = 0; s < a.stages; ++s) mbar_init(&rg.bars[s], 1);
     fence_mbar_init();
     fence_proxy_async_smem();
-    producer_seek(pr, tab, a.nphases, warp, a.sb_stride);
+    producer_seek(pr, tab, a.nphases, warp);
+    run = producer_load_run(pr, tab, a.nphases, a.sb_stride);
     for (int s = 0; s < a.stages; ++s)
-      producer_issue(pr, rg, s, tab, a.nphases, warp, a.sb_stride);
+      producer_issue(pr, run, rg, s, tab, a.nphases, warp, a.sb_stride);
   }
   __syncwarp();
 
@@ -660,7 +868,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
       cp_async_commit();
     }
     if (cur.kind == kPhaseGemv)
-      ok = gemv_phase<QT>(sh, cur, tab[p], scratch, rg, pr, tab, a);
+      ok = gemv_phase<QT>(sh, cur, tab[p], scratch, rg, pr, run, tab, a);
     else
       ok = attn_phase<HG>(sh, cur, scratch, a);
     cp_async_wait_all();
@@ -762,9 +970,18 @@ std::vector<StepCta> step_cta_table(const std::vector<StepPhase>& ph, int grid) 
       e.cb = cta_start(c, grid, g.ntiles, g.nchunks, g.gc, g.ngroups);
       e.ce = cta_start(c + 1, grid, g.ntiles, g.nchunks, g.gc, g.ngroups);
       e.w = g.w + (size_t)e.cb * g.sbb;
-      if (e.cb < e.ce) {
-        e.g0 = sb_decode(e.cb, g.ntiles, g.nchunks, g.gc).grp;
-        e.g1 = sb_decode(e.ce - 1, g.ntiles, g.nchunks, g.gc).grp;
+      // segments: the range's group-tiles of each chunk group
+      for (int u = e.cb; u < e.ce;) {
+        if (e.nseg == 2) fail(MLB_ERR_INVALID, "decode step kernel: range over three chunk groups");
+        const SbPos sp = sb_decode(u, g.ntiles, g.nchunks, g.gc);
+        const int group_end = (sp.grp + 1) * g.ntiles * g.gc;  // past the group's super-blocks
+        const int end = std::min(e.ce, std::min(group_end, g.ntiles * g.nchunks));
+        e.T[e.nseg] = (end - u) / sp.geff;
+        e.nc[e.nseg] = sp.geff;
+        e.grp[e.nseg] = sp.grp;
+        e.t0[e.nseg] = sp.t;
+        ++e.nseg;
+        u = end;
       }
     }
     if (ph[i].kind == kPhaseGemv) next = i;

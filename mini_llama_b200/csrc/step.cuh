@@ -33,6 +33,10 @@ struct StepGemv {
   int tp_ar;
   int x_slot, x_ar;
   float* x_store;
+  // RMSNorm statistic of x as the producing phase's per-tile sums of squares
+  // (ss_n tiles), or null
+  const float* ss_in;
+  int ss_n;
 };
 
 struct StepAttn {
@@ -52,13 +56,19 @@ struct alignas(16) StepPhase {  // copied into shared memory 16 bytes at a time
 };
 
 // One CTA's share of one GEMV phase, computed on the host (entry
-// [phase][cta]; entries of attention phases are unused).
+// [phase][cta]; entries of attention phases are unused). The range is whole
+// group-tiles; it splits into at most two segments, one per chunk group, each
+// a run of whole tiles of that group.
 struct alignas(16) StepCta {
   const uint8_t* w;  // its first super-block
   int cb, ce;        // super-block range [cb, ce)
-  int g0, g1;        // chunk groups the range spans
   int next;          // the next GEMV phase (nphases: none)
-  int pad;
+  int nseg;          // segments (0 when the range is empty)
+  int T[2];          // tiles of each segment
+  int nc[2];         // chunks per tile in each segment (its group's width)
+  int grp[2];        // chunk group of each segment
+  int t0[2];         // first tile of each segment
+  int pad[2];
 };
 
 struct StepArgs {
