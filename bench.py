@@ -33,11 +33,14 @@ SEED = 20261201
 # (22016 x 4096 Q4_0), from the ncu capture summarised in
 # profiles/gemv_q4_0_gateup_22016x4096.md.
 GEMV_TRAFFIC_BYTES = 50.79e6
-# The same counters for one launch of the persistent decode-step kernel
-# (Llama-2-7B shape, Q4_0, context ~520), from the 2- and 4-layer captures in
-# profiles/decode_step_kernel_llama2-7b-q4_0.md scaled to 32 layers (traffic
-# grows linearly with layers: 77.6 MB + 131.1 MB per layer).
-STEP_TRAFFIC_BYTES = 4.273e9
+# The same counters for one launch of the persistent decode-step kernel on the
+# Llama-2-7B Q4_0 shape, from the 2- and 4-layer captures in
+# profiles/decode_step_kernel_llama2-7b-q4_0.md: 77.6 MB fixed (lm_head,
+# embedding row, activations) plus, per layer, 114.1 MB of weights and small
+# terms and the fp32 K and V rows at the context (17.0 MB at context 520).
+def step_traffic_7b(layers, ctx):
+    return 77.6e6 + layers * (114.08e6 + 2 * 4 * 128 * 32 * ctx)
+
 
 
 def parse_args():
@@ -353,7 +356,8 @@ def run_gpu(args, cfg, qtype, bias, rank, world, local):
     if step_kernel:
         # one launch per step: the persistent kernel is the dominant (only) kernel
         roof = dict(step_roof, kernel=f"decode_step_kernel<{C.QTYPE_NAMES[qtype]}>",
-                    traffic=STEP_TRAFFIC_BYTES)
+                    traffic=(step_traffic_7b(cfg["n_layers"], mid_ctx)
+                             if args.workload == "llama2-7b-q4_0" and world == 1 else None))
     else:
         roof = gemv_roof
 
