@@ -95,6 +95,12 @@ struct EpiParams {
   // kEpiResidual, one batch row: ss_out[tile] = the sum of squares of the
   // tile's 16 output rows (fixed order), for the next phase's RMSNorm
   float* ss_out;
+  // Step kernel (set on the device): resid_s, when set, holds the residual
+  // rows of tiles resid_t0.. (batch row 0) in shared memory; pos_set marks
+  // pos_now as the position (else *pos is read)
+  const float* resid_s;
+  int resid_t0;
+  int pos_set, pos_now;
 };
 
 #if defined(__CUDACC__)

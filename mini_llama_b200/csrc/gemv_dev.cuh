@@ -225,8 +225,11 @@ __device__ void epilogue_row(const EpiParams& p, int tile, int row, int r, const
       }
       break;
     case kEpiResidual:
-      if (grow < p.n_out)
-        p.y[(size_t)r * p.ldy + grow] = __fadd_rn(__ldcg(p.resid + (size_t)r * p.ldr + grow), v);
+      if (grow < p.n_out) {
+        const float rv = p.resid_s ? p.resid_s[grow - p.resid_t0 * 16]
+                                   : __ldcg(p.resid + (size_t)r * p.ldr + grow);
+        p.y[(size_t)r * p.ldy + grow] = __fadd_rn(rv, v);
+      }
       break;
     case kEpiSwiglu: {
       if (row >= 8) break;
@@ -256,7 +259,7 @@ __device__ void epilogue_row(const EpiParams& p, int tile, int row, int r, const
       const int bias_base = sec == 0 ? 0 : (sec == 1 ? p.q_rows : p.q_rows + p.kv_rows);
       int L = logical(local);
       if (p.bias) v = __fadd_rn(v, p.bias[bias_base + L]);
-      int pos = *p.pos;
+      int pos = p.pos_set ? p.pos_now : *p.pos;
       if (sec == 2) {
         p.values[(size_t)pos * p.kv_rows + L] = v;
         break;

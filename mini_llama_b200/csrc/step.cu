@@ -60,6 +60,10 @@ struct AttnShape {
   static constexpr int NV = HG * PB;          // scores per block (<= 16)
 };
 
+// Residual rows a CTA prefetches into shared memory for its residual epilogue
+// (16 tiles; larger ranges read the residual from L2 in the epilogue).
+constexpr int kResidPre = 256;
+
 // A warp's weight-stream producer: its walk over runs (lane 0's, in shared
 // memory; see producer_seek).
 struct Producer {
@@ -91,6 +95,7 @@ struct StepShared {
   int tp_fail;           // a tagged read gave up
   int pos, token;        // the step's position and input token (read once)
   Producer prod[kStepWarps];  // each warp's producer (lane 0 reads and writes it)
+  alignas(16) float resid_pre[kResidPre];  // residual rows of this CTA's tiles (epilogue)
 };
 
 __device__ __forceinline__ unsigned int ld_acquire_u32(const unsigned int* p) {
@@ -470,6 +475,27 @@ __device__ bool gemv_phase(StepShared& sh, StepPhase& cur, const StepCta& ct, ui
   // barrier below, read only after it)
   if (threadIdx.x == 0 && g.epi.kind == kEpiResidual && g.epi.resid == nullptr)
     cur.g.epi.resid = a.embedding + (size_t)sh.token * a.dim;
+  // Epilogue inputs fetched now, so the epilogue after the weight stream does
+  // not wait on L2: the residual rows of a one-segment range (cp.async into
+  // shared memory, complete before the barrier ahead of finish_runs), and the
+  // position from shared memory.
+  if (g.epi.kind == kEpiResidual && ct.nseg == 1 && g.ngroups == 1) {
+    const int t0 = ct.t0[0], nt = ct.T[0];
+    if (nt * 16 <= kResidPre && (t0 + nt) * 16 <= g.epi.n_out) {
+      const float* rs = g.epi.resid ? g.epi.resid : a.embedding + (size_t)sh.token * a.dim;
+      for (int i = threadIdx.x; i < nt * 4; i += blockDim.x)
+        cp_async16(sh.resid_pre + i * 4, rs + (size_t)t0 * 16 + i * 4);
+      cp_async_commit();
+      if (threadIdx.x == 0) {
+        cur.g.epi.resid_s = sh.resid_pre;
+        cur.g.epi.resid_t0 = t0;
+      }
+    }
+  }
+  if (threadIdx.x == 0 && g.epi.kind == kEpiQkv) {
+    cur.g.epi.pos_set = 1;
+    cur.g.epi.pos_now = sh.pos;
+  }
   const EpiParams& epi = cur.g.epi;
   RunTable rt{sh.run_u0, sh.run_t, sh.run_grp, sh.run_cc0};
   const FinishGeom fg{g.ntiles, g.nchunks, g.gc, g.ngroups, 1};
@@ -498,6 +524,7 @@ __device__ bool gemv_phase(StepShared& sh, StepPhase& cur, const StepCta& ct, ui
           rt.cc0[r] = 0;
         }
       }
+      cp_async_wait_all();  // this thread's prefetched residual rows have landed
       __syncthreads();
       if (!sh.flag) return false;  // block-uniform: read after the barrier
       finish_runs<1>(sc.parts, sc.red, rt, Tw, wb, fg, a.ws, a.counters, epi);
