@@ -220,3 +220,22 @@ def test_step_kernel_decode_greedy_matches_forward(cuda):
         host.append(tok)
     b = make_ctx(model, "step")
     assert b.decode_greedy(9, 0, 40) == host
+
+
+@pytest.mark.parametrize("qtype", [C.Q4_0, C.Q8_0])
+def test_step_kernel_two_chunk_groups_matches_per_op_path(cuda, qtype):
+    """A hidden size above 16384 inputs splits w_down's K into chunk groups
+    (66 chunks: 32 + 32 + 2), and with 256 output tiles (768 group-tiles over
+    148 CTAs) many CTA ranges of the step kernel span two group segments whose
+    tiles are finished across CTAs (the 72B shape's w_down): greedy ids equal
+    and logits within the bar of the per-op path over 12 steps."""
+    cfg = dict(vocab_size=512, dim=4096, hidden_dim=16896, n_layers=2, n_heads=32, n_kv_heads=8,
+               head_dim=128, max_seq_len=16, rope_theta=10000.0, rms_norm_eps=1e-5, rope_type=0)
+    model = mlb.CudaModel(cfg).synthesize(qtype, 5)
+    a, b = make_ctx(model, "step"), make_ctx(model, "per_op")
+    tok_a = tok_b = 11
+    for pos in range(12):
+        la, lb = a.forward_token(tok_a, pos), b.forward_token(tok_b, pos)
+        assert np.abs(la - lb).max() <= LOGIT_TOL, pos
+        tok_a, tok_b = int(np.argmax(la)), int(np.argmax(lb))
+        assert tok_a == tok_b, pos
