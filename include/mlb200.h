@@ -80,6 +80,19 @@ int mlb_built(void);
 /* Replaces CudaDeviceCount (include/mini_llama/cuda_runtime.h:27). */
 int mlb_device_count(int* count);
 
+/* Failure-detection self-test; no counterpart in the reference (whose device
+ * code has no waits). Every wait inside the decode-step kernel is bounded: it
+ * gives up after a limit, records MLB_ERR_TIMEOUT and the wait site in the
+ * context's status word, and returns, so a stuck peer or a lost copy becomes
+ * an error status instead of a hung GPU. This runs one of those waits on
+ * `device` against something that never comes, with a limit of `limit_ms`
+ * (0 < limit_ms <= 1000): which = 0 waits on a shared-memory ring slot whose
+ * copy never lands (the weight stream's mbarrier wait), which = 1 on a grid
+ * barrier that no other CTA joins. Writes the recorded status code
+ * (MLB_ERR_TIMEOUT when the wait gave up) and site (900 + which); the
+ * device stays usable. Synchronous. */
+int mlb_wait_selftest(int device, int which, double limit_ms, int* code, int* where);
+
 /* ------------------------------------------------------------------ linear
  * y[rows, out] = x[rows, in] * W^T over raw GGUF blocks on the device.
  * Replaces CudaQ80LinearDeviceInput / CudaQ40LinearDeviceInput /

@@ -22,6 +22,7 @@ from .configs import (F32, Q4_0, Q4_1, Q8_0, W_BK, W_BQ, W_BV, W_DOWN, W_FFN_NOR
 
 ROPE_NORMAL, ROPE_NEOX = 0, 1
 ATTN_CPU_COMPAT, ATTN_STANDARD = 0, 1
+ERR_TIMEOUT = -5  # MLB_ERR_TIMEOUT: a bounded device wait gave up
 
 __all__ = [
     "F32", "Q8_0", "Q4_0", "Q4_1", "ROPE_NORMAL", "ROPE_NEOX", "ATTN_CPU_COMPAT",
@@ -65,6 +66,17 @@ def CudaDeviceCount() -> int:
 
 
 # ------------------------------------------------------------------ linear
+
+def wait_selftest(which: int, limit_ms: float = 1.0, device_id: int = 0):
+    """Runs one of the step kernel's bounded waits against something that
+    never arrives (0: a ring slot's mbarrier, 1: a grid barrier) and returns
+    the (status code, site) it recorded: (MLB_ERR_TIMEOUT, 900 + which) when
+    the wait gave up after limit_ms."""
+    code, where = ctypes.c_int(0), ctypes.c_int(0)
+    check(lib().mlb_wait_selftest(device_id, which, float(limit_ms), ctypes.byref(code),
+                                  ctypes.byref(where)))
+    return code.value, where.value
+
 
 def _linear_device_input(qtype, x, w_dev, block_count, weight_shape, device_id, stream=None):
     torch = _torch()

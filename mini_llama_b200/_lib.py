@@ -40,6 +40,7 @@ SIGNATURES = [
     ("mlb_last_error", ctypes.c_char_p, []),
     ("mlb_built", _c_int, []),
     ("mlb_device_count", _c_int, [_ip]),
+    ("mlb_wait_selftest", _c_int, [_c_int, _c_int, ctypes.c_double, _ip, _ip]),
     ("mlb_linear", _c_int, [_c_int, _vp, _c_int, _c_int, _vp, _c_size_t, _c_int, _vp, _c_int, _vp]),
     ("mlb_linear_host", _c_int, [_c_int, _vp, _c_int, _c_int, _vp, _c_size_t, _c_int, _vp, _vp,
                                  _c_int]),

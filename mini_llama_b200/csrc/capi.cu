@@ -529,6 +529,20 @@ int mlb_context_set_step_kernel(mlb_context* c, int enable) {
 
 int mlb_context_step_kernel(const mlb_context* c) { return c && c->impl->use_step ? 1 : 0; }
 
+int mlb_wait_selftest(int device, int which, double limit_ms, int* code, int* where) {
+  return guarded([&] {
+    if (!code || !where) invalid("mlb_wait_selftest: null output");
+    if (which != 0 && which != 1) invalid("mlb_wait_selftest: which must be 0 or 1");
+    if (!(limit_ms > 0.0) || limit_ms > 1000.0)
+      invalid("mlb_wait_selftest: limit_ms must be in (0, 1000]");
+    set_device(device);
+    int khz = 0;
+    MLB_CUDA(cudaDeviceGetAttribute(&khz, cudaDevAttrClockRate, device));
+    const long long cycles = (long long)(limit_ms * (double)khz);
+    step_wait_selftest(which, cycles > 0 ? cycles : 1, 900 + which, code, where);
+  });
+}
+
 int mlb_nccl_unique_id(void* out128) {
   return guarded([&] {
     if (!out128) invalid("mlb_nccl_unique_id: null output");

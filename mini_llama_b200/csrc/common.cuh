@@ -123,12 +123,14 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
-// Bounded wait: ~2 s worth of polling, then records a timeout and returns false.
+// Bounded wait: `limit` SM cycles of polling (default ~2 s), then records a
+// timeout and returns false.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity,
-                                                  DeviceStatus* status, int where) {
+                                                  DeviceStatus* status, int where,
+                                                  long long limit = 4000000000LL) {
   long long start = clock64();
   while (!mbar_try_wait(bar, parity)) {
-    if (clock64() - start > 4000000000LL) {
+    if (clock64() - start > limit) {
       if (status) {
         atomicExch(&status->code, MLB_ERR_TIMEOUT);
         atomicExch(&status->where, where);

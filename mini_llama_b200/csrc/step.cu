@@ -117,7 +117,7 @@ __device__ __forceinline__ void record_error(DeviceStatus* st, int code, int whe
 // Returns false (block-uniform) when the wait timed out or another CTA
 // recorded an error.
 __device__ bool grid_barrier(unsigned int* counter, unsigned int k, DeviceStatus* st, int where,
-                             int* flag) {
+                             int* flag, long long limit = kWaitCycles) {
   __syncthreads();  // the CTA's writes happen before thread 0's release below
   if (threadIdx.x == 0) {
     asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(counter) : "memory");
@@ -129,7 +129,7 @@ __device__ bool grid_barrier(unsigned int* counter, unsigned int k, DeviceStatus
         ok = 0;
         break;
       }
-      if (clock64() - t0 > kWaitCycles) {
+      if (clock64() - t0 > limit) {
         record_error(st, MLB_ERR_TIMEOUT, where);
         ok = 0;
         break;
@@ -976,6 +976,51 @@ void* step_kernel_ptr(int qtype, int gq) {
 size_t round_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
 }  // namespace
+
+namespace {
+
+// The step kernel's two waits, each made to wait for something that never
+// comes: which = 0 an mbarrier phase that nothing completes (a ring slot whose
+// copy never lands), which = 1 a grid barrier that the launch's only CTA can
+// never fill (a CTA that never arrives). Each gives up after `limit` cycles
+// and records MLB_ERR_TIMEOUT at `where` in *st.
+__global__ void wait_selftest_kernel(DeviceStatus* st, unsigned int* counter, int which,
+                                     long long limit, int where) {
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ int flag;
+  if (which == 0) {
+    if (threadIdx.x == 0) {
+      mbar_init(&bar, 1);
+      fence_mbar_init();
+    }
+    __syncthreads();
+    if (threadIdx.x == 0 && !mbar_try_wait(&bar, 0)) mbar_wait_bounded(&bar, 0, st, where, limit);
+  } else {
+    grid_barrier(counter, 2, st, where, &flag, limit);
+  }
+}
+
+}  // namespace
+
+void step_wait_selftest(int which, long long limit_cycles, int where, int* code, int* at) {
+  DeviceStatus* st = nullptr;
+  unsigned int* counter = nullptr;
+  MLB_CUDA(cudaMalloc(&st, sizeof(DeviceStatus)));
+  cudaError_t e = cudaMalloc(&counter, sizeof(unsigned int));
+  if (e == cudaSuccess) e = cudaMemset(st, 0, sizeof(DeviceStatus));
+  if (e == cudaSuccess) e = cudaMemset(counter, 0, sizeof(unsigned int));
+  if (e == cudaSuccess) {
+    wait_selftest_kernel<<<1, 32>>>(st, counter, which, limit_cycles, where);
+    e = cudaGetLastError();
+  }
+  DeviceStatus h{};
+  if (e == cudaSuccess) e = cudaMemcpy(&h, st, sizeof(h), cudaMemcpyDeviceToHost);
+  cudaFree(counter);
+  cudaFree(st);
+  MLB_CUDA(e);
+  *code = h.code;
+  *at = h.where;
+}
 
 size_t step_smem_bytes(int scratch_bytes, int sb_stride, int stages, int nphases) {
   return (size_t)kStepWarps * stages * sb_stride + (size_t)kStepWarps * kMaxStages * 8 +

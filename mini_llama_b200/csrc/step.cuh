@@ -125,6 +125,11 @@ bool step_attn_ok(int H, int KV, int D, std::string* why);
 // The per-CTA table of a phase list on `grid` CTAs.
 std::vector<StepCta> step_cta_table(const std::vector<StepPhase>& ph, int grid);
 
+// Makes one of the step kernel's bounded waits run out on the current device
+// (which = 0: a ring mbarrier, 1: a grid barrier) with a limit of
+// limit_cycles SM cycles; returns the recorded status code and site.
+void step_wait_selftest(int which, long long limit_cycles, int where, int* code, int* at);
+
 // Launches one step (cooperative launch, capturable in a CUDA graph).
 void step_launch(const StepPlan& plan, const StepArgs& args, cudaStream_t stream);
 // Resident blocks of the step kernel per SM with `smem` bytes of shared memory.
