@@ -184,3 +184,49 @@ def test_two_gloo_ranks_match_the_unsharded_layer(tmp_path):
     lg32 = logits.astype(np.float32)
     assert lg32[2] == lg32[7] == lg32.max()          # tied across the two shards
     assert int(got["token"]) == 2                    # lowest index wins
+
+
+# ------------------------------------------------- a rank that fails (host side)
+
+def failing_rank_main(rank, world, port, out_dir):
+    """Rank 1 raises before the all-reduce that exchanges per-rank step times
+    (bench.py's max over ranks); rank 0 must see an error from its collective
+    within the process group's timeout and record it, not wait for ever."""
+    import datetime
+    import os
+    import time
+
+    import torch
+    import torch.distributed as dist
+
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
+                            world_size=world, timeout=datetime.timedelta(seconds=10))
+    if rank == 1:
+        raise RuntimeError("injected failure on rank 1")
+    t0 = time.perf_counter()
+    try:
+        t = torch.tensor([1.0])
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        outcome = "completed"
+    except Exception as e:  # the failure surfaces as an error on the survivor
+        outcome = "error: " + type(e).__name__
+    with open(os.path.join(out_dir, "rank0.txt"), "w") as f:
+        f.write(f"{outcome}\n{time.perf_counter() - t0:.2f}\n")
+
+
+def test_failed_rank_surfaces_as_an_error(tmp_path):
+    import torch.multiprocessing as mp
+
+    ctx = mp.start_processes(failing_rank_main, args=(2, free_port(), str(tmp_path)), nprocs=2,
+                             join=False, start_method="spawn")
+    for p in ctx.processes:  # each ends by itself: rank 1 raises, rank 0 times out or errors
+        p.join(timeout=120)
+    alive = [p for p in ctx.processes if p.is_alive()]
+    for p in alive:
+        p.kill()
+    assert not alive, "a rank did not end after its peer failed"
+    assert ctx.processes[1].exitcode != 0          # the injected failure
+    assert ctx.processes[0].exitcode == 0          # the survivor handled it
+    outcome, secs = (tmp_path / "rank0.txt").read_text().split("\n")[:2]
+    assert outcome.startswith("error"), outcome     # its collective failed ...
+    assert float(secs) < 30.0                       # ... within the process-group timeout
