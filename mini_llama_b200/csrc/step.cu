@@ -776,19 +776,23 @@ __device__ __noinline__ bool attn_phase(StepShared& sh, const StepPhase& cur, ui
     }
     // this piece's record: the warps combined, unnormalised (m, l, o)
     float* dst = a.attn_ws + (size_t)item * gq * rec;
-    if ((int)threadIdx.x < gq) {
-      const int h = threadIdx.x;
-      float m = -INFINITY;
-      for (int i = 0; i < kStepWarps; ++i) m = fmaxf(m, s.wpart[((size_t)i * gq + h) * rec]);
-      float l = 0.0f;
-      for (int i = 0; i < kStepWarps; ++i) {
-        const float* r = s.wpart + ((size_t)i * gq + h) * rec;
-        const float e = r[0] == -INFINITY ? 0.0f : expf(r[0] - m);
-        s.ew[h * kMaxGrid + i] = e;
-        l = fmaf(r[1], e, l);
+    if (warp < gq) {  // warp h combines the 16 warp records of query head h
+      const int h = warp;
+      const bool has = lane < kStepWarps;
+      const float* r = s.wpart + ((size_t)(has ? lane : 0) * gq + h) * rec;
+      const float mi = has ? r[0] : -INFINITY;
+      float m = mi;
+#pragma unroll
+      for (int off = 8; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+      const float e = (has && mi != -INFINITY) ? expf(mi - m) : 0.0f;
+      float l = has ? r[1] * e : 0.0f;
+#pragma unroll
+      for (int off = 8; off > 0; off >>= 1) l += __shfl_xor_sync(0xffffffffu, l, off);
+      if (has) s.ew[h * kMaxGrid + lane] = e;
+      if (lane == 0) {
+        dst[h * rec] = m;
+        dst[h * rec + 1] = l;
       }
-      dst[h * rec] = m;
-      dst[h * rec + 1] = l;
     }
     __syncthreads();
     for (int idx = threadIdx.x; idx < gq * D; idx += kStepThreads) {
