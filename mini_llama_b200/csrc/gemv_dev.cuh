@@ -720,10 +720,21 @@ __device__ __forceinline__ void finish_runs(const float* parts, float* red, cons
   for (int rr = warp; rr < nruns; rr += kGemvWarps) {
     const int t = rt.t[rr], grp = rt.grp[rr];
     const int p0 = rt.u0[rr] - wb, len = rt.u0[rr + 1] - rt.u0[rr];
-    for (int i = lane; i < 16 * M; i += 32) {
+    if (M == 1) {
+      // one row per lane pair: lane r sums the first half of the row's
+      // partials, lane r + 16 the second; the halves add in that order
+      const int i = lane & 15, half = len >> 1;
+      const int j0 = lane < 16 ? 0 : half, j1 = lane < 16 ? half : len;
       float s = 0.0f;
-      for (int j = 0; j < len; ++j) s += parts[(size_t)(p0 + j) * 16 * M + i];
-      myred[i] = s;
+      for (int j = j0; j < j1; ++j) s += parts[(size_t)(p0 + j) * 16 + i];
+      const float hi = __shfl_down_sync(0xffffffffu, s, 16);
+      if (lane < 16) myred[i] = s + hi;
+    } else {
+      for (int i = lane; i < 16 * M; i += 32) {
+        float s = 0.0f;
+        for (int j = 0; j < len; ++j) s += parts[(size_t)(p0 + j) * 16 * M + i];
+        myred[i] = s;
+      }
     }
     __syncwarp();
     bool finish = fg.ngroups == 1;
