@@ -143,11 +143,6 @@ __device__ bool grid_barrier(unsigned int* counter, unsigned int k, DeviceStatus
   return ok != 0;
 }
 
-__device__ __forceinline__ unsigned int ld_acquire_sys_u32(const unsigned int* p) {
-  unsigned int v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
 __device__ __forceinline__ void red_release_sys_add(unsigned int* p, unsigned int v) {
   asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
