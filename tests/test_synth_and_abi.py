@@ -94,3 +94,43 @@ def test_workload_shapes_are_block_aligned(name, cfg_q):
     assert cfg["dim"] % 32 == 0 and cfg["hidden_dim"] % 32 == 0
     assert cfg["n_heads"] % cfg["n_kv_heads"] == 0
     assert cfg["n_heads"] * cfg["head_dim"] == cfg["dim"]
+
+
+def test_c_abi_rejects_injected_faults_without_touching_a_device():
+    """Host-side fault injection through the C ABI: every bad argument returns
+    an error status with the reference's kind of message, before any device
+    call (so it runs with no GPU)."""
+    lib = _lib.lib()
+    bad = ctypes.c_void_p(1)  # never dereferenced: the checks come first
+
+    def err(rc, text, code=-1):
+        assert rc == code, (rc, lib.mlb_last_error())
+        assert text.encode() in lib.mlb_last_error(), lib.mlb_last_error()
+
+    err(lib.mlb_linear(99, bad, 1, 64, bad, 2, 1, bad, 0, None), "unsupported quant type 99")
+    err(lib.mlb_linear(C.Q8_0, bad, 0, 64, bad, 2, 1, bad, 0, None), "empty tensors")
+    err(lib.mlb_linear(C.Q4_0, bad, 1, 64, bad, 3, 1, bad, 0, None), "block count mismatch")
+    err(lib.mlb_linear(C.Q4_0, None, 1, 64, bad, 2, 1, bad, 0, None), "pointer is null")
+    err(lib.mlb_qmatrix_gemv(None, bad, 1, bad, None), "null pointer")
+    cfg = _lib.MlbConfig(vocab_size=10, dim=64, hidden_dim=96, n_layers=1, n_heads=4,
+                         n_kv_heads=3, head_dim=16, max_seq_len=8, rope_theta=1e4,
+                         rms_norm_eps=1e-5, rope_type=0)
+    out = ctypes.c_void_p()
+    err(lib.mlb_model_create(ctypes.byref(cfg), 0, 0, 1, None, ctypes.byref(out)),
+        "n_heads must be divisible by n_kv_heads")
+    cfg.n_kv_heads, cfg.dim = 2, 0
+    err(lib.mlb_model_create(ctypes.byref(cfg), 0, 0, 1, None, ctypes.byref(out)),
+        "config dimensions must be positive")
+    cfg.dim, cfg.head_dim = 64, 18
+    err(lib.mlb_model_create(ctypes.byref(cfg), 0, 0, 1, None, ctypes.byref(out)),
+        "head_dim must be a multiple of 4")
+    cfg.head_dim = 16
+    err(lib.mlb_model_create(ctypes.byref(cfg), 0, 2, 2, None, ctypes.byref(out)),
+        "bad tensor-parallel rank/size")
+    err(lib.mlb_model_create(None, 0, 0, 1, None, ctypes.byref(out)), "null config")
+    err(lib.mlb_forward_token(None, 1, 0, bad), "null pointer")
+    err(lib.mlb_context_sync(None), "null context")
+    err(lib.mlb_context_set_step_kernel(None, 1), "null context")
+    code, where = ctypes.c_int(0), ctypes.c_int(0)
+    err(lib.mlb_wait_selftest(0, 2, 1.0, ctypes.byref(code), ctypes.byref(where)),
+        "which must be 0 or 1")
