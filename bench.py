@@ -82,7 +82,7 @@ def measured_peaks():
 class Clocks:
     """nvidia-smi samples during the timed region."""
 
-    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+    Q = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
          "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
@@ -110,15 +110,27 @@ class Clocks:
             except Exception:
                 self.proc.kill()
 
-    def summary(self):
+    def summary(self, windows=None):
+        """Median SM clock, max clock and throttle reasons over the samples;
+        with windows (host (start, end) times), only samples taken inside one."""
+        import datetime
+
         self.f.flush()
         self.f.seek(0)
         sm, mx, reasons = [], [], set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for line in self.f.read().splitlines():
             parts = [x.strip() for x in line.split(",")]
-            if len(parts) < 9:
+            if len(parts) < 10:
                 continue
+            if windows is not None:
+                try:
+                    t = datetime.datetime.strptime(parts[0], "%Y/%m/%d %H:%M:%S.%f").timestamp()
+                except ValueError:
+                    continue
+                if not any(a <= t <= b for a, b in windows):
+                    continue
+            parts = parts[1:]
             try:
                 sm.append(float(parts[1]))
                 mx.append(float(parts[2]))
@@ -211,9 +223,11 @@ def run_reference(args, cfg, qtype, bias, world, rank):
 
 # ---------------------------------------------------------------- GPU arm
 
-def time_launches(torch, launch, n):
+def time_launches(torch, launch, n, min_seconds=0.0):
     """Average device time of one launch: n launches captured in a CUDA graph
-    (no host launch latency between them), replayed and timed with events."""
+    (no host launch latency between them), replayed and timed with events;
+    the graph is replayed until the timed region lasts min_seconds (so clock
+    samples can land in it)."""
     launch(0)  # first call outside capture: one-time kernel attributes
     torch.cuda.synchronize()
     s = torch.cuda.Stream()
@@ -226,11 +240,19 @@ def time_launches(torch, launch, n):
     torch.cuda.synchronize()
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     cur = torch.cuda.current_stream()
+    reps = 1
+    if min_seconds > 0:  # one replay's duration sets the count
+        a.record(cur)
+        g.replay()
+        b.record(cur)
+        torch.cuda.synchronize()
+        reps = max(1, int(min_seconds * 1e3 / max(a.elapsed_time(b), 1e-3)) + 1)
     a.record(cur)
-    g.replay()
+    for _ in range(reps):
+        g.replay()
     b.record(cur)
     torch.cuda.synchronize()
-    return a.elapsed_time(b) / n
+    return a.elapsed_time(b) / (n * reps)
 
 
 def gemv_roofline(torch, mlb, cfg, qtype, world, peak):
@@ -426,6 +448,7 @@ def run_gemv_sweep(args):
     qnames = {v: k for k, v in C.QTYPE_NAMES.items()}
     k = 4096
     rows = []
+    windows = []  # host times of the timed loops (clock samples are kept from these)
     with Clocks([0]) as clk:
         for qn in args.sweep_q.split(","):
             qtype = qnames[qn]
@@ -441,8 +464,10 @@ def run_gemv_sweep(args):
                         mats[i % copies].gemv(x, y)
                     torch.cuda.synchronize()
                     torch.cuda.profiler.start()
+                    t0 = time.time()
                     us = 1e3 * time_launches(torch, lambda i: mats[i % copies].gemv(x, y),
-                                             args.steps)
+                                             args.steps, min_seconds=0.4)
+                    windows.append((t0, time.time()))
                     torch.cuda.profiler.stop()
                     nbytes = wbytes + m * k * 4 + m * n * 4
                     rows.append({"q": qn, "n": n, "k": k, "m": m, "us": us,
@@ -494,7 +519,7 @@ def run_gemv_sweep(args):
                    "l2": "rotating weight copies > 2x L2"},
         "roofline": {"bound": "hbm", "achieved": head["gbs"], "peak": peak[0], "unit": "GB/s",
                      "frac": head["frac"], "traffic": None},
-        "sweep": rows, "cpu_baseline": cpu, "clocks": clk.summary(),
+        "sweep": rows, "cpu_baseline": cpu, "clocks": clk.summary(windows),
         "gpu_launches": args.steps * len(rows)}))
 
 
