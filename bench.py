@@ -1,14 +1,18 @@
 #!/usr/bin/env python
 """Decode benchmark: tokens/s of the B200 decode path (default: Llama-2-7B shape,
-Q4_0, batch 1, KV cache prefilled to 512 positions) on N GPUs.
+Q4_0, batch 1, KV cache at depth 512) on N GPUs.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
                     [--workload NAME] [--ctx C]
 
-N > 1 runs under torchrun, one rank per GPU, tensor parallel over NCCL. Prints
-one JSON line (rank 0). The reference arm (--impl reference) times the
-reference's own CPU ForwardToken (oracle/_ref, built from the reference's
-sources) on the same synthetic model.
+N > 1 runs under torchrun, one rank per GPU, tensor parallel. Prints one JSON
+line (rank 0). The decode state at depth C is the seeded K/V fill
+(mlb_context_fill_kv on the GPU; the same values written through the
+reference's KvCache::Write on the CPU), so both arms decode from identical
+states and their greedy ids are compared. The reference arm (--impl
+reference) times the reference's own CPU ForwardToken (oracle/_ref, built from
+the reference's sources; its model is generated and quantised inside that
+library, so no library of this project is loaded in that arm).
 """
 from __future__ import annotations
 
@@ -26,21 +30,26 @@ import numpy as np
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
-from mini_llama_b200 import configs as C  # noqa: E402
+from mini_llama_b200 import configs as C  # noqa: E402  (shapes only: loads no library)
 
 SEED = 20261201
-# dram__bytes_read.sum + dram__bytes_write.sum of one gate/up GEMV launch
-# (22016 x 4096 Q4_0), from the ncu capture summarised in
-# profiles/gemv_q4_0_gateup_22016x4096.md.
-GEMV_TRAFFIC_BYTES = 50.79e6
-# The same counters for one launch of the persistent decode-step kernel on the
-# Llama-2-7B Q4_0 shape, from the 2- and 4-layer captures in
-# profiles/decode_step_kernel_llama2-7b-q4_0.md: 77.6 MB fixed (lm_head,
-# embedding row, activations) plus, per layer, 114.1 MB of weights and small
-# terms and the fp32 K and V rows at the context (17.0 MB at context 520).
-def step_traffic_7b(layers, ctx):
-    return 77.6e6 + layers * (114.08e6 + 2 * 4 * 128 * 32 * ctx)
+KV_SEED = SEED + 1   # seeded K/V rows of the prefilled context
+KV_SCALE = 1.25      # their scale (the K/V rows of these models are ~N(0, 1.28^2))
+N_CHECK = 16         # greedy ids compared against the single-GPU / CPU reference run
 
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one launch of
+# the standalone gate/up GEMV 22016 x 4096 Q4_0, from an ncu capture of that
+# launch: it equals the algorithmic bytes (weights + x + y) to 0.01%.
+GEMV_TRAFFIC_BYTES = 50.79e6
+
+
+def step_traffic_7b(layers, ctx):
+    """DRAM bytes of one decode-step launch on the Llama-2-7B Q4_0 shape,
+    modelled from ncu captures of the step kernel on 2- and 4-layer cases:
+    77.6 MB fixed (lm_head, embedding row, activations) plus, per layer,
+    114.1 MB of weights and small terms and the fp32 K and V rows read at the
+    context (2 * 4 * 128 * 32 bytes per position)."""
+    return 77.6e6 + layers * (114.08e6 + 2 * 4 * 128 * 32 * ctx)
 
 
 def parse_args():
@@ -51,9 +60,12 @@ def parse_args():
     p.add_argument("--impl", choices=["b200", "reference"], default="b200")
     p.add_argument("--workload", choices=sorted(C.WORKLOADS) + ["gemv-sweep"],
                    default="llama2-7b-q4_0")
+    p.add_argument("--also", type=str, default="qwen2-72b-q4_1",
+                   help="second workload timed in the same run (comma list; 'none' for none)")
     p.add_argument("--sweep-n", type=str, default="4096,11008,14336")
     p.add_argument("--sweep-m", type=str, default="1,4,16,64")
     p.add_argument("--sweep-q", type=str, default="q4_0,q4_1,q8_0")
+    p.add_argument("--no-sweep", action="store_true", help="skip the GEMV sweep of the N=1 line")
     p.add_argument("--ctx", type=int, default=512, help="KV positions filled before timing")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--layers", type=int, default=0,
@@ -80,7 +92,7 @@ def measured_peaks():
 # ----------------------------------------------------------------- clocks
 
 class Clocks:
-    """nvidia-smi samples during the timed region."""
+    """nvidia-smi samples (read-only query) during the timed region."""
 
     Q = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -146,78 +158,78 @@ class Clocks:
                 "samples": len(sm)}
 
 
-# -------------------------------------------------------------- CPU legs
+# ----------------------------------------------------- reference CPU path
 
 def cpu_threads():
     return len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
 
 
-def build_cpu_model(cfg, qtype, bias):
-    """The reference's own CPU implementation when built (oracle/_ref), else the
-    C restatement; both get the generator's exact bytes."""
+def cpu_decode(cfg, qtype, bias, ctx0, n_max, budget_s, warm=1):
+    """The reference's own CPU ForwardToken (oracle/_ref) on the seeded model,
+    decoding greedily from the seeded K/V state at depth ctx0: `warm` untimed
+    tokens, then up to n_max timed tokens or budget_s seconds. The model is
+    generated and quantised inside oracle/_ref (the reference's quantisers), so
+    this loads no library of this project."""
     import oracle
 
+    tok = C.prompt_ids(SEED, 1, cfg["vocab_size"])[0]
     if oracle.ref_available():
         r = oracle.ref()
         r.set_threads(cpu_threads())
-        kind, lib, threads = "reference", r, r.threads()
-    else:
-        kind, lib, threads = "port", oracle.port(), 1
-    m = lib.model(cfg)
-    for k, layer, qt, rows, cols, arr in C.host_weights(cfg, qtype, SEED, bias,
-                                                        threads=cpu_threads()):
-        m.set_weight(k, layer, qt, rows, cols, arr)
-    return m, kind, threads
-
-
-def time_cpu_tokens(m, cfg, n_warm, n_max, budget_s):
-    """Greedy CPU decode from position 0: n_warm untimed, then up to n_max timed
-    tokens or until budget_s of CPU time."""
-    tok = C.prompt_ids(SEED, 1, cfg["vocab_size"])[0]
-    pos = 0
-    for _ in range(n_warm):
+        kind, threads = "reference", r.threads()
+        m = r.model(cfg).synthesize(qtype, SEED, bias, threads=cpu_threads())
+        m.fill_kv(ctx0, KV_SEED, KV_SCALE)
+    else:  # pragma: no cover - the reference tree was absent at build time
+        raise RuntimeError("oracle/_ref (the reference's CPU build) is missing")
+    ids, per_tok = [], []
+    pos = ctx0
+    for _ in range(warm):
         tok = int(np.argmax(m.forward_token(tok, pos)))
+        ids.append(tok)
         pos += 1
     t0 = time.perf_counter()
     n = 0
     while n < n_max:
+        t1 = time.perf_counter()
         tok = int(np.argmax(m.forward_token(tok, pos)))
+        per_tok.append(time.perf_counter() - t1)
+        ids.append(tok)
         pos += 1
         n += 1
         if time.perf_counter() - t0 > budget_s:
             break
-    return n, time.perf_counter() - t0
+    secs = time.perf_counter() - t0
+    del m
+    return {"ids": ids, "n": n, "secs": secs, "per_tok_median_s": statistics.median(per_tok),
+            "kind": kind, "threads": threads, "pos0": ctx0 + warm, "pos1": pos}
 
 
 def run_reference(args, cfg, qtype, bias, world, rank):
     if rank != 0:
         return
-    metric = "decode tok/s"
     try:
-        m, kind, threads = build_cpu_model(cfg, qtype, bias)
+        r = cpu_decode(cfg, qtype, bias, args.ctx, args.steps, 150.0, warm=max(1, min(args.warmup, 2)))
     except Exception as e:  # pragma: no cover
         print(json.dumps({"impl": "reference", "unavailable": f"reference CPU build failed: {e}"}))
         return
-    t_first = time.perf_counter()
-    n_w, _ = time_cpu_tokens(m, cfg, 0, 1, 1e9)
-    per_tok = time.perf_counter() - t_first
-    budget = 150.0
-    steps = max(1, min(args.steps, int(budget / max(per_tok, 1e-3))))
-    warm = max(0, min(args.warmup - 1, 2))
-    n, secs = time_cpu_tokens(m, cfg, warm, steps, budget)
-    v = n / secs
-    sample = (f"{n} greedy decode tokens of the full model from position {warm + 1} "
-              f"(bounded to ~{int(budget)} s), {threads} threads")
+    v = r["n"] / r["secs"]
+    sample = (f"{r['n']} greedy decode tokens of the full model at positions "
+              f"{r['pos0']}..{r['pos1'] - 1} after the seeded K/V fill to depth {args.ctx} "
+              f"(bounded to ~150 s), {r['threads']} threads; median per token "
+              f"{r['per_tok_median_s'] * 1e3:.0f} ms")
     print(json.dumps({
-        "impl": "reference", "metric": metric, "value": v, "unit": "tok/s", "n_gpus": world,
-        "steps": n, "warmup": warm + 1, "ms_per_step": 1000.0 * secs / n,
-        "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-        "dtype": C.QTYPE_NAMES[qtype] + "/fp32", "data": "synthetic (seeded N(0,0.02) weights)",
-        "config": {"workload": args.workload, "batch": 1, "ctx": "0..%d" % (warm + n),
+        "impl": "reference", "metric": "decode tok/s", "value": v, "unit": "tok/s",
+        "n_gpus": world, "steps": r["n"], "warmup": max(1, min(args.warmup, 2)),
+        "ms_per_step": 1000.0 * r["secs"] / r["n"], "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": C.QTYPE_NAMES[qtype] + "/fp32",
+        "data": "synthetic (seeded N(0,0.02) weights quantised by the reference's quantisers; "
+                "seeded K/V rows to the context depth)",
+        "config": {"workload": args.workload, "batch": 1, "ctx": args.ctx,
                    "parallelism": "cpu threads"},
-        "cpu_baseline": {"value": v, "unit": "tok/s", "cores": threads, "kind": kind,
+        "cpu_baseline": {"value": v, "unit": "tok/s", "cores": r["threads"], "kind": r["kind"],
                          "sample": sample},
         "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "greedy_ids": r["ids"][:N_CHECK],
     }))
 
 
@@ -227,7 +239,8 @@ def time_launches(torch, launch, n, min_seconds=0.0):
     """Average device time of one launch: n launches captured in a CUDA graph
     (no host launch latency between them), replayed and timed with events;
     the graph is replayed until the timed region lasts min_seconds (so clock
-    samples can land in it)."""
+    samples can land in it). Returns (ms per launch, host (start, end) of the
+    timed replays)."""
     launch(0)  # first call outside capture: one-time kernel attributes
     torch.cuda.synchronize()
     s = torch.cuda.Stream()
@@ -247,17 +260,18 @@ def time_launches(torch, launch, n, min_seconds=0.0):
         b.record(cur)
         torch.cuda.synchronize()
         reps = max(1, int(min_seconds * 1e3 / max(a.elapsed_time(b), 1e-3)) + 1)
+    h0 = time.time()
     a.record(cur)
     for _ in range(reps):
         g.replay()
     b.record(cur)
     torch.cuda.synchronize()
-    return a.elapsed_time(b) / (n * reps)
+    return a.elapsed_time(b) / (n * reps), (h0, time.time())
 
 
 def gemv_roofline(torch, mlb, cfg, qtype, world, peak):
-    """Live per-launch timing of the dominant kernel: the fused gate/up GEMV of
-    this rank's shard, rotating over copies that together exceed L2."""
+    """Live per-launch timing of the standalone fused gate/up GEMV of this
+    rank's shard, rotating over copies that together exceed L2."""
     F = cfg["hidden_dim"] // world
     n, k = 2 * F, cfg["dim"]
     nbytes = n * ((k + 31) // 32) * C.BLOCK_BYTES[qtype] + k * 4 + (n // 2) * 4
@@ -265,15 +279,207 @@ def gemv_roofline(torch, mlb, cfg, qtype, world, peak):
     mats = [mlb.QMatrix.synthesize(qtype, n, k, SEED, 900 + i, raw=False) for i in range(copies)]
     x = torch.randn(1, k, device="cuda")
     y = torch.empty(1, n, device="cuda")
-    ms = time_launches(torch, lambda i: mats[i % copies].gemv(x, y), 8 * copies)
+    ms, _ = time_launches(torch, lambda i: mats[i % copies].gemv(x, y), 8 * copies)
     achieved = nbytes / (ms * 1e-3) / 1e9
+    single = world == 1 and n == 22016 and k == 4096 and qtype == C.Q4_0
     return {"bound": "hbm", "achieved": achieved, "peak": peak[0], "unit": "GB/s",
             "frac": achieved / peak[0],
-            # the captured traffic is for the single-GPU shape (22016 x 4096)
-            "traffic": GEMV_TRAFFIC_BYTES if world == 1 else None,
+            "traffic": GEMV_TRAFFIC_BYTES if single else None,
+            "traffic_source": "ncu capture of one launch of this shape" if single else None,
             "kernel": f"gemv_sb_kernel<{C.QTYPE_NAMES[qtype]}> {n}x{k}",
             "bytes_per_launch": nbytes, "us_per_launch": ms * 1e3,
             "peak_source": peak[1] + " (MEASURED_PEAKS.json hbm_gbs, burst)"}
+
+
+def gemv_sweep(torch, mlb, args, peak, with_cpu=True):
+    """The K = 4096 quantised GEMV/GEMM sweep: N x M over Q4_0/Q4_1/Q8_0 on raw
+    random GGUF blocks (fp16 scale |N(0,1)|*0.01, uniform codes), x ~ N(0,1).
+    Each launch reads another copy of the weights (copies > 2x L2). Per row:
+    device time, achieved GB/s and fraction of the measured copy bandwidth, and
+    (with_cpu) the reference CPU path's time for the same M rows."""
+    qnames = {v: k for k, v in C.QTYPE_NAMES.items()}
+    k = 4096
+    rows, windows = [], []
+    for qn in args.sweep_q.split(","):
+        qtype = qnames[qn]
+        for n in [int(v) for v in args.sweep_n.split(",")]:
+            wbytes = n * (k // 32) * C.BLOCK_BYTES[qtype]
+            copies = max(2, int(np.ceil(260e6 / wbytes)))
+            mats = [mlb.QMatrix.synthesize(qtype, n, k, SEED, 7000 + i, raw=True)
+                    for i in range(copies)]
+            for m in [int(v) for v in args.sweep_m.split(",")]:
+                x = torch.randn(m, k, device="cuda")
+                y = torch.empty(m, n, device="cuda")
+                for i in range(3):
+                    mats[i % copies].gemv(x, y)
+                torch.cuda.synchronize()
+                ms, win = time_launches(torch, lambda i: mats[i % copies].gemv(x, y),
+                                        4 * copies, min_seconds=0.25)
+                windows.append(win)
+                nbytes = wbytes + m * k * 4 + m * n * 4
+                us = ms * 1e3
+                rows.append({"q": qn, "n": n, "k": k, "m": m, "us": us,
+                             "gbs": nbytes / (us * 1e-6) / 1e9,
+                             "frac": nbytes / (us * 1e-6) / 1e9 / peak[0]})
+            del mats
+    cpu = None
+    if with_cpu:
+        import oracle
+
+        if oracle.ref_available():
+            r = oracle.ref()
+            r.set_threads(cpu_threads())
+            kind, lib, threads = "reference", r, r.threads()
+        else:  # pragma: no cover
+            kind, lib, threads = "port", oracle.port(), 1
+        # every (format, N) at M = 1 for ~1.5 s; M rows cost M calls on the
+        # reference's CPU path (its batch loop is sequential)
+        x = np.random.default_rng(0).normal(0, 1, k).astype(np.float32)
+        single = {}
+        for qn in args.sweep_q.split(","):
+            qtype = qnames[qn]
+            for n in [int(v) for v in args.sweep_n.split(",")]:
+                w = np.random.default_rng(n).integers(0, 256, (n, (k // 32) * C.BLOCK_BYTES[qtype]),
+                                                      dtype=np.uint8)
+                nh = 2 if qtype == C.Q4_1 else 1
+                sc = (np.abs(np.random.default_rng(n + 1).normal(0, 1, (n, k // 32, nh))) * 0.01
+                      ).astype(np.float16)
+                w.reshape(n, k // 32, -1)[:, :, :2 * nh] = sc.view(np.uint8).reshape(n, k // 32, 2 * nh)
+                lib.linear(qtype, x, w, n)  # warm
+                t0 = time.perf_counter()
+                reps = 0
+                while time.perf_counter() - t0 < 1.5:
+                    lib.linear(qtype, x, w, n)
+                    reps += 1
+                single[(qn, n)] = ((time.perf_counter() - t0) / reps, reps, w.nbytes)
+        for r_ in rows:
+            secs, _, wb = single[(r_["q"], r_["n"])]
+            r_["cpu_us"] = r_["m"] * secs * 1e6
+            r_["cpu_gbs"] = (wb + k * 4 + r_["n"] * 4) / secs / 1e9
+        head = next(r_ for r_ in rows if r_["q"] == "q4_0" and r_["m"] == 1)
+        secs, reps, wb = single[(head["q"], head["n"])]
+        cpu = {"value": (wb + k * 4 + head["n"] * 4) / secs / 1e9, "unit": "GB/s",
+               "cores": threads, "kind": kind,
+               "sample": f"{reps} linear calls of {head['q']} {head['n']}x{k} M=1 (~1.5 s); "
+                         "every row's cpu_us is its (format, N) at M=1 times M"}
+    return rows, windows, cpu
+
+
+def measure_workload(torch, mlb, dist, args, name, cfg, qtype, bias, rank, world, local,
+                     steps, warmup, peak, check_single):
+    """One decode workload on this rank: seeded model and K/V state at depth
+    args.ctx, `warmup` untimed greedy steps, `steps` timed ones (CUDA events
+    on the context stream, max over ranks), then the e2e loop through
+    mlb_forward_token with host logits. check_single: rank 0 also decodes the
+    first greedy ids on one GPU (tensor-parallel runs) for the id self-check."""
+    barrier = lambda: (torch.cuda.synchronize(), dist.barrier() if dist else None)  # noqa: E731
+
+    def max_over_ranks(v):
+        if not dist:
+            return v
+        t = torch.tensor([v], dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    nccl_id = None
+    if world > 1:
+        obj = [mlb.nccl_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        nccl_id = obj[0]
+    model = mlb.CudaModel(cfg, device_id=local, tp_rank=rank, tp_size=world, nccl_id=nccl_id)
+    model.synthesize(qtype, SEED, with_bias=bias)
+    resident, step_weights = model.bytes()
+    ctx = model.context(mlb.ATTN_CPU_COMPAT, step_kernel=False if args.per_op else None)
+    step_kernel = ctx.step_kernel()
+    stream = torch.cuda.ExternalStream(ctx.stream())
+    tok0 = C.prompt_ids(SEED, 1, cfg["vocab_size"])[0]
+    ctx0 = args.ctx
+    if ctx0 + warmup + 2 * steps + 2 > cfg["max_seq_len"]:
+        raise SystemExit("context too long for max_seq_len")
+    ctx.fill_kv(ctx0, KV_SEED, KV_SCALE)
+    ids = ctx.decode_greedy(tok0, ctx0, warmup) if warmup else []
+    pos = ctx0 + warmup
+    tok = ids[-1] if ids else tok0
+    barrier()
+
+    with Clocks([local]) as clk:
+        barrier()
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        h0 = time.time()
+        ev0.record(stream)
+        ids += ctx.decode_greedy(tok, pos, steps)
+        ev1.record(stream)
+        torch.cuda.synchronize()
+        h1 = time.time()
+        barrier()
+    ms = max_over_ranks(ev0.elapsed_time(ev1))
+    clocks = clk.summary([(h0, h1)])
+    pos += steps
+    ctx_end = pos
+    tok = ids[-1]
+
+    # e2e: ForwardToken through the C ABI, host logits every step
+    for _ in range(2):
+        tok = int(np.argmax(ctx.forward_token(tok, pos)))
+        pos += 1
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        lg = ctx.forward_token(tok, pos)
+        tok = int(np.argmax(lg))
+        pos += 1
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1))
+    kpl = ctx.kernels_per_step()
+    ctx.close()
+    model.close()
+
+    # the tensor-parallel ids against one GPU decoding from the same state
+    tp_check = None
+    if check_single and world > 1:
+        if rank == 0:
+            n = min(N_CHECK, len(ids))
+            one = mlb.CudaModel(cfg, device_id=local).synthesize(qtype, SEED, with_bias=bias)
+            c1 = one.context(mlb.ATTN_CPU_COMPAT)
+            c1.fill_kv(ctx0, KV_SEED, KV_SCALE)
+            ids1 = c1.decode_greedy(tok0, ctx0, n)
+            c1.close()
+            one.close()
+            tp_check = {"tp_ids_match": ids1 == ids[:n], "n": n,
+                        "against": "one GPU (step kernel) from the same seeded state"}
+        barrier()
+
+    kv_per_pos = 2 * cfg["n_layers"] * (cfg["n_kv_heads"] // world) * cfg["head_dim"] * 4
+    mid_ctx = (ctx0 + warmup + ctx_end) / 2
+    step_bytes = step_weights + kv_per_pos * mid_ctx
+    step_s = ms / 1e3 / steps
+    roof = {"bound": "hbm", "achieved": step_bytes / step_s / 1e9, "peak": peak[0],
+            "unit": "GB/s", "frac": step_bytes / step_s / 1e9 / peak[0],
+            "bytes_per_launch": step_bytes, "us_per_launch": step_s * 1e6,
+            "kernel": (f"decode_step_kernel<{C.QTYPE_NAMES[qtype]}>" if step_kernel
+                       else "per-op graph"),
+            "note": "algorithmic bytes: GGUF weight bytes of this rank + fp32 K and V read per "
+                    "token at the mean timed context; time: CUDA events on the context stream "
+                    "around the timed greedy steps (one step-kernel launch per step)",
+            "peak_source": peak[1] + " (MEASURED_PEAKS.json hbm_gbs, burst)"}
+    if step_kernel and name == "llama2-7b-q4_0" and world == 1 and not args.layers:
+        roof["traffic"] = step_traffic_7b(cfg["n_layers"], mid_ctx)
+        roof["traffic_source"] = "modelled from ncu captures of 2- and 4-layer cases"
+    else:
+        roof["traffic"] = None
+    return {
+        "name": name, "value": steps / (ms / 1e3), "ms_per_step": ms / steps, "steps": steps,
+        "warmup": warmup, "ids": ids, "ctx_end": ctx_end, "clocks": clocks,
+        "e2e": {"value": steps / (e2e_ms / 1e3), "unit": "tok/s", "h2d_bytes_per_step": 12,
+                "d2h_bytes_per_step": cfg["vocab_size"] * 4,
+                "api": "mlb_forward_token (host logits)"},
+        "roofline": roof, "kernels_per_step": kpl, "step_kernel": step_kernel,
+        "resident_bytes": resident, "step_weight_bytes": step_weights, "tp_check": tp_check,
+        "gpu_launches": kpl * steps,
+    }
 
 
 def run_gpu(args, cfg, qtype, bias, rank, world, local):
@@ -288,239 +494,126 @@ def run_gpu(args, cfg, qtype, bias, rank, world, local):
 
         import torch.distributed as dist
 
-        dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=180))
-    nccl_id = None
-    if world > 1:
-        obj = [mlb.nccl_unique_id() if rank == 0 else None]
-        dist.broadcast_object_list(obj, src=0)
-        nccl_id = obj[0]
-    model = mlb.CudaModel(cfg, device_id=local, tp_rank=rank, tp_size=world, nccl_id=nccl_id)
-    model.synthesize(qtype, SEED, with_bias=bias)
-    resident, step_weights = model.bytes()
-    ctx = model.context(mlb.ATTN_CPU_COMPAT, step_kernel=False if args.per_op else None)
-    step_kernel = ctx.step_kernel()
-    stream = torch.cuda.ExternalStream(ctx.stream())
-    tok0 = C.prompt_ids(SEED, 1, cfg["vocab_size"])[0]
-    if args.ctx + args.warmup + 2 * args.steps + 2 > cfg["max_seq_len"]:
-        raise SystemExit("context too long for max_seq_len")
-
-    def barrier():
-        torch.cuda.synchronize()
-        if dist:
-            dist.barrier()
-
-    def max_over_ranks(v):
-        if not dist:
-            return v
-        t = torch.tensor([v], dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
-
-    # fill the KV cache to ctx positions (greedy decode from position 0)
-    pos = 0
-    toks = ctx.decode_greedy(tok0, pos, args.ctx) if args.ctx else [tok0]
-    pos += args.ctx
-    tok = toks[-1]
-    # warm-up
-    toks = ctx.decode_greedy(tok, pos, args.warmup)
-    pos += args.warmup
-    tok = toks[-1] if toks else tok
-    barrier()
-
-    # timed: device-resident greedy decode, one graph launch per token
-    with Clocks([local]) as clk:
-        barrier()
-        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        torch.cuda.profiler.start()
-        ev0.record(stream)
-        toks = ctx.decode_greedy(tok, pos, args.steps)
-        ev1.record(stream)
-        torch.cuda.synchronize()
-        torch.cuda.profiler.stop()
-        barrier()
-    ms = max_over_ranks(ev0.elapsed_time(ev1))
-    ctx_end = pos + args.steps
-    pos += args.steps
-    tok = toks[-1]
-    clocks = clk.summary()
-
-    # e2e: ForwardToken through the C ABI, host logits every step
-    for _ in range(2):
-        tok = int(np.argmax(ctx.forward_token(tok, pos)))
-        pos += 1
-    barrier()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(args.steps):
-        lg = ctx.forward_token(tok, pos)
-        tok = int(np.argmax(lg))
-        pos += 1
-    e1.record(stream)
-    torch.cuda.synchronize()
-    barrier()
-    e2e_ms = max_over_ranks(e0.elapsed_time(e1))
-
+        dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=600))
     peak = measured_peaks()
-    gemv_roof = gemv_roofline(torch, mlb, cfg, qtype, world, peak)
-    # whole-step HBM roofline: weights + fp32 KV read at the timed context
-    kv_per_pos = 2 * cfg["n_layers"] * (cfg["n_kv_heads"] // world) * cfg["head_dim"] * 4
-    mid_ctx = (args.ctx + args.warmup + ctx_end) / 2
-    step_bytes = step_weights + kv_per_pos * mid_ctx
-    step_s = ms / 1e3 / args.steps
-    kpl = ctx.kernels_per_step()
-    step_roof = {"bound": "hbm", "achieved": step_bytes / step_s / 1e9, "peak": peak[0],
-                 "unit": "GB/s", "frac": step_bytes / step_s / 1e9 / peak[0],
-                 "bytes_per_launch": step_bytes, "us_per_launch": step_s * 1e6,
-                 "note": "algorithmic bytes: GGUF weight bytes of this rank + fp32 K and V "
-                         "read per token at the mean timed context; time: CUDA events on "
-                         "the context stream around the timed greedy steps",
-                 "peak_source": peak[1] + " (MEASURED_PEAKS.json hbm_gbs, burst)"}
-    if step_kernel:
-        # one launch per step: the persistent kernel is the dominant (only) kernel
-        roof = dict(step_roof, kernel=f"decode_step_kernel<{C.QTYPE_NAMES[qtype]}>",
-                    traffic=(step_traffic_7b(cfg["n_layers"], mid_ctx)
-                             if args.workload == "llama2-7b-q4_0" and world == 1 else None))
-    else:
-        roof = gemv_roof
-
-    cpu = None
-    if world == 1 and rank == 0 and not args.no_cpu_baseline:
+    head = measure_workload(torch, mlb, dist, args, args.workload, cfg, qtype, bias, rank, world,
+                            local, args.steps, args.warmup, peak, check_single=True)
+    extras = []
+    for name in [] if args.also in ("", "none") or args.layers else args.also.split(","):
+        if name == args.workload:
+            continue
+        ecfg, eq, eb = C.WORKLOADS[name]
         try:
-            m, kind, threads = build_cpu_model(cfg, qtype, bias)
-            n, secs = time_cpu_tokens(m, cfg, 1, 64, 20.0)
-            cpu = {"value": n / secs, "unit": "tok/s", "cores": threads, "kind": kind,
-                   "sample": f"{n} greedy decode tokens of the full model at positions 1..{n} "
-                             f"(~20 s of CPU time); the timed GPU run is at context "
-                             f"{args.ctx}..{ctx_end}, where attention adds "
-                             f"{kv_per_pos * mid_ctx / 1e9:.2f} GB/token on top of "
-                             f"{step_weights / 1e9:.2f} GB of weights"}
-            del m
-        except Exception as e:
-            cpu = {"value": None, "unit": "tok/s", "cores": 0, "kind": "unavailable",
-                   "sample": str(e)[:200]}
+            extras.append(measure_workload(torch, mlb, dist, args, name, ecfg, eq, eb, rank,
+                                           world, local, min(args.steps, 24),
+                                           max(3, min(args.warmup, 4)), peak, check_single=True))
+        except Exception as e:  # reported, not fatal
+            extras.append({"name": name, "error": str(e)[:300]})
+
+    gemv_roof = sweep = sweep_cpu = None
+    cpu = None
+    if rank == 0 and world == 1:
+        gemv_roof = gemv_roofline(torch, mlb, cfg, qtype, world, peak)
+        if not args.no_sweep and not args.layers:
+            with Clocks([local]) as clk:
+                sweep, windows, sweep_cpu = gemv_sweep(torch, mlb, args, peak,
+                                                       with_cpu=not args.no_cpu_baseline)
+            sweep_clocks = clk.summary(windows)
+        if not args.no_cpu_baseline:
+            try:
+                r = cpu_decode(cfg, qtype, bias, args.ctx, 64, 20.0, warm=1)
+                n_cmp = min(N_CHECK, len(r["ids"]), len(head["ids"]))
+                cpu = {"value": r["n"] / r["secs"], "unit": "tok/s", "cores": r["threads"],
+                       "kind": r["kind"],
+                       "sample": f"{r['n']} greedy decode tokens of the full model at positions "
+                                 f"{r['pos0']}..{r['pos1'] - 1} after the seeded K/V fill to "
+                                 f"depth {args.ctx} (~20 s of CPU time); median per token "
+                                 f"{r['per_tok_median_s'] * 1e3:.0f} ms",
+                       "ids_match_gpu": r["ids"][:n_cmp] == head["ids"][:n_cmp],
+                       "ids_compared": n_cmp}
+            except Exception as e:
+                cpu = {"value": None, "unit": "tok/s", "cores": 0, "kind": "unavailable",
+                       "sample": str(e)[:200]}
 
     if rank == 0:
-        value = args.steps / (ms / 1e3)
+        value = head["value"]
+        parity = {}
+        if head["tp_check"]:
+            parity.update(head["tp_check"])
+        if cpu and "ids_match_gpu" in cpu:
+            parity["ref_ids_match"] = cpu["ids_match_gpu"]
+            parity["ref_ids_compared"] = cpu["ids_compared"]
         line = {
             "metric": "decode tok/s", "value": value, "unit": "tok/s", "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": head["ms_per_step"],
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": C.QTYPE_NAMES[qtype] + "/fp32",
-            "data": "synthetic (seeded N(0,0.02) weights quantised like the reference; "
-                    "random prompt id)",
+            "data": "synthetic (seeded N(0,0.02) weights quantised like the reference; seeded "
+                    "K/V rows to the context depth; seeded prompt id)",
             "config": {"workload": args.workload + (f" ({args.layers} layers)" if args.layers else ""),
-                       "batch": 1, "ctx": args.ctx,
-                       "ctx_end": ctx_end,
+                       "batch": 1, "ctx": args.ctx, "ctx_end": head["ctx_end"],
                        "parallelism": f"tp{world}" if world > 1 else "single gpu",
                        "l2": "no flush: each step streams %.2f GB of weights (> 126 MB L2)"
-                             % (step_weights / 1e9),
+                             % (head["step_weight_bytes"] / 1e9),
                        "attention": "cpu-compat (reference CPU path V sum)",
-                       "step": "persistent kernel" if step_kernel else "one kernel per op"},
-            "e2e": {"value": args.steps / (e2e_ms / 1e3), "unit": "tok/s",
-                    "h2d_bytes_per_step": 12, "d2h_bytes_per_step": cfg["vocab_size"] * 4,
-                    "api": "mlb_forward_token (host logits)"},
-            "roofline": roof,
-            "step_roofline": step_roof,
-            "gemv_roofline": gemv_roof,
+                       "step": "persistent kernel" if head["step_kernel"] else "one kernel per op"},
+            "e2e": head["e2e"],
+            "roofline": head["roofline"],
+            "parity": parity,
+            "greedy_ids": head["ids"][:N_CHECK],
             "cpu_baseline": cpu,
-            "clocks": clocks,
-            "gpu_launches": kpl * args.steps,
-            "kernels_per_step": kpl,
-            "resident_bytes": resident,
+            "clocks": head["clocks"],
+            "gpu_launches": head["gpu_launches"],
+            "kernels_per_step": head["kernels_per_step"],
+            "resident_bytes": head["resident_bytes"],
         }
+        if gemv_roof:
+            line["gemv_roofline"] = gemv_roof
+        if sweep:
+            line["gemv_sweep"] = {"rows": sweep, "cpu_baseline": sweep_cpu,
+                                  "clocks": sweep_clocks,
+                                  "note": "standalone gemv_sb_kernel, K = 4096, raw random GGUF "
+                                          "blocks; bytes = weights + M*K*4 + M*N*4; frac of the "
+                                          "measured copy bandwidth"}
+        for e in extras:
+            key = e["name"].replace("-", "_")
+            if "error" in e:
+                line[key] = {"error": e["error"]}
+                continue
+            line[key] = {"value": e["value"], "unit": "tok/s", "ms_per_step": e["ms_per_step"],
+                         "steps": e["steps"], "warmup": e["warmup"], "batch": 1,
+                         "ctx": args.ctx, "e2e": e["e2e"], "roofline": e["roofline"],
+                         "clocks": e["clocks"], "parity": e["tp_check"],
+                         "greedy_ids": e["ids"][:N_CHECK], "gpu_launches": e["gpu_launches"],
+                         "parallelism": f"tp{world}" if world > 1 else "single gpu"}
         print(json.dumps(line))
-    ctx.close()
-    model.close()
     if dist:
         dist.barrier()
         dist.destroy_process_group()
 
 
 def run_gemv_sweep(args):
-    """Standalone quantised GEMV/GEMM sweep: K = 4096, N x M over the formats,
-    raw random GGUF blocks (fp16 scale |N(0,1)|*0.01, uniform codes), x ~ N(0,1).
-    Each launch reads a different copy of the weights (copies > 2x L2)."""
+    """The sweep alone as its own line (--workload gemv-sweep)."""
     import torch
 
     import mini_llama_b200 as mlb
 
     peak = measured_peaks()
-    qnames = {v: k for k, v in C.QTYPE_NAMES.items()}
-    k = 4096
-    rows = []
-    windows = []  # host times of the timed loops (clock samples are kept from these)
     with Clocks([0]) as clk:
-        for qn in args.sweep_q.split(","):
-            qtype = qnames[qn]
-            for n in [int(v) for v in args.sweep_n.split(",")]:
-                wbytes = n * (k // 32) * C.BLOCK_BYTES[qtype]
-                copies = max(2, int(np.ceil(260e6 / wbytes)))
-                mats = [mlb.QMatrix.synthesize(qtype, n, k, SEED, 7000 + i, raw=True)
-                        for i in range(copies)]
-                for m in [int(v) for v in args.sweep_m.split(",")]:
-                    x = torch.randn(m, k, device="cuda")
-                    y = torch.empty(m, n, device="cuda")
-                    for i in range(args.warmup):
-                        mats[i % copies].gemv(x, y)
-                    torch.cuda.synchronize()
-                    torch.cuda.profiler.start()
-                    t0 = time.time()
-                    us = 1e3 * time_launches(torch, lambda i: mats[i % copies].gemv(x, y),
-                                             args.steps, min_seconds=0.4)
-                    windows.append((t0, time.time()))
-                    torch.cuda.profiler.stop()
-                    nbytes = wbytes + m * k * 4 + m * n * 4
-                    rows.append({"q": qn, "n": n, "k": k, "m": m, "us": us,
-                                 "gbs": nbytes / (us * 1e-6) / 1e9,
-                                 "frac": nbytes / (us * 1e-6) / 1e9 / peak[0]})
-                del mats
+        rows, windows, cpu = gemv_sweep(torch, mlb, args, peak,
+                                        with_cpu=not args.no_cpu_baseline)
     head = next((r for r in rows if r["q"] == "q4_0" and r["m"] == 1 and r["n"] == 11008), rows[0])
-    cpu = None
-    if not args.no_cpu_baseline:
-        import oracle
-
-        if oracle.ref_available():
-            r = oracle.ref()
-            r.set_threads(cpu_threads())
-            kind, lib, threads = "reference", r, r.threads()
-        else:
-            kind, lib, threads = "port", oracle.port(), 1
-        # every (format, N) of the sweep at M = 1, ~2 s each; a batch of M rows is
-        # M calls on the reference's CPU path (its batch loop is sequential)
-        x = np.random.default_rng(0).normal(0, 1, k).astype(np.float32)
-        single = {}
-        for qn in args.sweep_q.split(","):
-            qtype = qnames[qn]
-            for n in [int(v) for v in args.sweep_n.split(",")]:
-                w = C.synth_tensor(SEED, C.W_WQ, 0, qtype, n, k, threads=cpu_threads())
-                lib.linear(qtype, x, w, n)  # warm
-                t0 = time.perf_counter()
-                reps = 0
-                while time.perf_counter() - t0 < 2.0:
-                    lib.linear(qtype, x, w, n)
-                    reps += 1
-                single[(qn, n)] = ((time.perf_counter() - t0) / reps, reps, w.nbytes)
-        for r in rows:
-            secs, _, wb = single[(r["q"], r["n"])]
-            r["cpu_us"] = r["m"] * secs * 1e6
-            r["cpu_gbs"] = (wb + k * 4 + r["n"] * 4) / secs / 1e9
-        secs, reps, wb = single[(head["q"], head["n"])]
-        cpu = {"value": (wb + k * 4 + head["n"] * 4) / secs / 1e9, "unit": "GB/s",
-               "cores": threads, "kind": kind,
-               "sample": f"{reps} linear calls of {head['q']} {head['n']}x{k} M=1 (~2 s); "
-                         "every sweep row carries cpu_us / cpu_gbs from the same ~2 s timing "
-                         "of its (format, N) at M=1, times M rows"}
     print(json.dumps({
         "metric": "quant GEMV achieved HBM GB/s", "value": head["gbs"], "unit": "GB/s",
         "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": head["us"] / 1e3,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": head["q"] + "/fp32", "data": "synthetic raw GGUF blocks",
-        "config": {"workload": "gemv-sweep", "headline": f"{head['q']} {head['n']}x{k} M=1",
+        "config": {"workload": "gemv-sweep", "headline": f"{head['q']} {head['n']}x4096 M=1",
                    "l2": "rotating weight copies > 2x L2"},
         "roofline": {"bound": "hbm", "achieved": head["gbs"], "peak": peak[0], "unit": "GB/s",
                      "frac": head["frac"], "traffic": None},
         "sweep": rows, "cpu_baseline": cpu, "clocks": clk.summary(windows),
-        "gpu_launches": args.steps * len(rows)}))
+        "gpu_launches": len(rows)}))
 
 
 def main():

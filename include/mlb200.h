@@ -179,7 +179,10 @@ int mlb_attention_decode(const float* q_dev, const float* keys_dev,
  * address, so make that first call before any stream capture. All calls share
  * the array: calls that overlap on the GPU (other streams, other threads) race
  * and give wrong results; run them one after another. Asynchronous on `stream`
- * (no host synchronisation). */
+ * (no host synchronisation, unlike mlb_attention_decode): synchronise `stream`
+ * before reading out_dev. The looked-up address is kept for the life of the
+ * process; it does not survive cudaDeviceReset (which reloads the module), so
+ * do not call this after resetting a device it has run on. */
 int mlb_attention_decode_noalloc(const float* q_dev, const float* keys_dev,
                                  const float* values_dev, int n_layers,
                                  int max_seq_len, int layer, int pos, int n_heads,
@@ -203,6 +206,13 @@ int mlb_qmatrix_synthesize(int qtype, int out_features, int in_features,
 /* y[rows, out] = x[rows, in] * W^T, device pointers, on `stream`. */
 int mlb_qmatrix_gemv(mlb_qmatrix* m, const float* x_dev, int rows, float* y_dev,
                      void* stream);
+/* The prepared weight dequantised back to fp32, out_dev[out_features *
+ * in_features] row-major, decoded from the repacked layout the GEMV streams.
+ * Replaces DequantizeFromQ80 / DequantizeFromQ40 / DequantizeFromQ41
+ * (include/mini_llama/quant.h; src/quant.cc:170-361) and gives the same bits:
+ * Q4_0 (q - 8) * d, Q4_1 q * d + m, Q8_0 d * q in fp32. Quantised types only.
+ * Asynchronous on `stream`. */
+int mlb_qmatrix_dequant(const mlb_qmatrix* m, float* out_dev, void* stream);
 /* Algorithmic GGUF bytes of the weight (what a GEMV must stream). */
 size_t mlb_qmatrix_bytes(const mlb_qmatrix* m);
 int mlb_qmatrix_destroy(mlb_qmatrix* m);
@@ -270,6 +280,14 @@ int mlb_context_create(mlb_model* m, int attention_mode, mlb_context** out);
 int mlb_context_destroy(mlb_context* c);
 /* Clears the KV cache (CudaKvCache::Clear, src/cuda_kv_cache.cc:96-110). */
 int mlb_context_reset(mlb_context* c);
+/* Fills positions [0, n_pos) of every layer's K and V cache rows (this rank's
+ * KV heads) with seeded values: element (pos, kv_head, d) of layer l is the
+ * generator's N(0,1) draw at index (pos * n_kv_heads + kv_head) * head_dim + d
+ * of stream 15 * 2^20 + l (K) or 16 * 2^20 + l (V), times scale. A decode
+ * state at depth n_pos for benchmarks and tests without n_pos decode steps.
+ * No reference counterpart (the reference fills its cache only by decoding).
+ * Synchronous. */
+int mlb_context_fill_kv(mlb_context* c, int n_pos, uint64_t seed, float scale);
 
 /* Replaces ForwardToken's device branch (src/forward.cc:776-794): runs one
  * decode step for `token` at `pos` and copies the vocab_size logits to host

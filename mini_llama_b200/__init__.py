@@ -313,9 +313,10 @@ def CudaAttentionDecodeDeviceInput(q, kv_cache: CudaKvCache, layer, pos, n_heads
 class QMatrix:
     """A weight repacked into the B200 GEMV layout (the decode path's format)."""
 
-    def __init__(self, handle, qtype, out_features, in_features):
+    def __init__(self, handle, qtype, out_features, in_features, device_id=0):
         self.h = handle
         self.qtype, self.out_features, self.in_features = qtype, out_features, in_features
+        self.device_id = device_id
 
     @classmethod
     def from_gguf(cls, qtype, blocks, out_features, in_features, device_id=0):
@@ -328,7 +329,7 @@ class QMatrix:
         else:
             check(lib().mlb_qmatrix_create(qtype, _ptr(blocks), 0, out_features, in_features,
                                            device_id, ctypes.byref(h)))
-        return cls(h, qtype, out_features, in_features)
+        return cls(h, qtype, out_features, in_features, device_id)
 
     @classmethod
     def synthesize(cls, qtype, out_features, in_features, seed, stream_id=0, raw=False,
@@ -336,7 +337,7 @@ class QMatrix:
         h = ctypes.c_void_p()
         check(lib().mlb_qmatrix_synthesize(qtype, out_features, in_features, seed, stream_id,
                                            int(raw), device_id, ctypes.byref(h)))
-        return cls(h, qtype, out_features, in_features)
+        return cls(h, qtype, out_features, in_features, device_id)
 
     def gemv(self, x, y=None, stream=None):
         torch = _torch()
@@ -346,6 +347,16 @@ class QMatrix:
                             dtype=torch.float32, device=x.device)
         check(lib().mlb_qmatrix_gemv(self.h, _ptr(x), rows, _ptr(y), _stream(stream)))
         return y
+
+    def dequant(self, out=None, stream=None):
+        """fp32 [out_features, in_features] on the device, decoded from the
+        repacked layout (DequantizeFromQ80/Q40/Q41, src/quant.cc:170-361)."""
+        torch = _torch()
+        if out is None:
+            out = torch.empty((self.out_features, self.in_features), dtype=torch.float32,
+                              device=f"cuda:{self.device_id}")
+        check(lib().mlb_qmatrix_dequant(self.h, _ptr(out), _stream(stream)))
+        return out
 
     def gguf_bytes(self):
         return lib().mlb_qmatrix_bytes(self.h)
@@ -460,6 +471,10 @@ class Context:
         check(lib().mlb_context_reset(self.h))
         self.pos = 0
         self.token_history = []
+
+    def fill_kv(self, n_pos: int, seed: int, scale: float = 1.25):
+        """Seeded K/V rows for positions [0, n_pos) (mlb_context_fill_kv)."""
+        check(lib().mlb_context_fill_kv(self.h, int(n_pos), int(seed), float(scale)))
 
     def stream(self) -> int:
         return lib().mlb_context_stream(self.h) or 0

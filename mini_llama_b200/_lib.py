@@ -65,6 +65,7 @@ SIGNATURES = [
     ("mlb_qmatrix_synthesize", _c_int, [_c_int, _c_int, _c_int, _c_u64, _c_u64, _c_int, _c_int,
                                         ctypes.POINTER(_vp)]),
     ("mlb_qmatrix_gemv", _c_int, [_vp, _vp, _c_int, _vp, _vp]),
+    ("mlb_qmatrix_dequant", _c_int, [_vp, _vp, _vp]),
     ("mlb_qmatrix_bytes", _c_size_t, [_vp]),
     ("mlb_qmatrix_destroy", _c_int, [_vp]),
     ("mlb_tp_plan", _c_int, [ctypes.POINTER(MlbConfig), _c_int, _c_int,
@@ -79,6 +80,7 @@ SIGNATURES = [
     ("mlb_context_create", _c_int, [_vp, _c_int, ctypes.POINTER(_vp)]),
     ("mlb_context_destroy", _c_int, [_vp]),
     ("mlb_context_reset", _c_int, [_vp]),
+    ("mlb_context_fill_kv", _c_int, [_vp, _c_int, _c_u64, _c_float]),
     ("mlb_forward_token", _c_int, [_vp, _c_int, _c_int, _vp]),
     ("mlb_forward_token_device", _c_int, [_vp, _c_int, _c_int, ctypes.POINTER(_vp)]),
     ("mlb_context_sync", _c_int, [_vp]),

@@ -50,12 +50,25 @@ def build_cuda(force: bool = False, verbose: bool = False) -> str:
     if not force and not _stale(LIB, deps):
         return LIB
     inc, lib = _nccl_dirs()
-    cmd = [NVCC, *ARCH, "-O3", "-lineinfo", "-std=c++17", "-shared", "-Xcompiler", "-fPIC",
-           "--expt-relaxed-constexpr", "-I", inc, "-I", os.path.join(ROOT, "include"),
-           "-o", LIB + ".tmp", *srcs, "-L", lib, "-l:libnccl.so.2", "-Xlinker", "-rpath=" + lib]
+    # one nvcc per translation unit, in parallel, then one link
+    objdir = os.path.join(HERE, "_build")
+    os.makedirs(objdir, exist_ok=True)
+    flags = [*ARCH, "-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC",
+             "--expt-relaxed-constexpr", "-I", inc, "-I", os.path.join(ROOT, "include")]
     if verbose:
-        cmd.insert(1, "-Xptxas=-v")
-    subprocess.run(cmd, check=True)
+        flags.insert(0, "-Xptxas=-v")
+    objs = [os.path.join(objdir, os.path.basename(s) + ".o") for s in srcs]
+
+    def compile_one(pair):
+        src, obj = pair
+        subprocess.run([NVCC, *flags, "-c", "-o", obj, src], check=True)
+
+    from concurrent.futures import ThreadPoolExecutor
+
+    with ThreadPoolExecutor(max_workers=min(len(srcs), os.cpu_count() or 4)) as ex:
+        list(ex.map(compile_one, zip(srcs, objs)))
+    subprocess.run([NVCC, *ARCH, "-shared", "-o", LIB + ".tmp", *objs, "-L", lib,
+                    "-l:libnccl.so.2", "-Xlinker", "-rpath=" + lib], check=True)
     os.replace(LIB + ".tmp", LIB)
     return LIB
 

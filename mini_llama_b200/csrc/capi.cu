@@ -54,6 +54,7 @@ void context_step_async(ContextImpl& c, int token, int pos);
 void context_forward_token(ContextImpl& c, int token, int pos, float* logits_host);
 void context_decode_greedy(ContextImpl& c, int token, int pos, int n, int* tokens_host);
 void context_reset(ContextImpl& c);
+void context_fill_kv(ContextImpl& c, int n_pos, uint64_t seed, float scale);
 
 static size_t expected_blocks(int qtype, int out, int in) {
   if (qtype == MLB_F32) return (size_t)out * (size_t)in;
@@ -392,6 +393,14 @@ int mlb_qmatrix_gemv(mlb_qmatrix* m, const float* x, int rows, float* y, void* s
   });
 }
 
+int mlb_qmatrix_dequant(const mlb_qmatrix* m, float* out_dev, void* stream) {
+  return guarded([&] {
+    if (!m || !out_dev) invalid("mlb_qmatrix_dequant: null pointer");
+    set_device(m->device);
+    qmatrix_dequant(m->q, out_dev, static_cast<cudaStream_t>(stream));
+  });
+}
+
 size_t mlb_qmatrix_bytes(const mlb_qmatrix* m) { return m ? m->q.gguf_bytes : 0; }
 
 int mlb_qmatrix_destroy(mlb_qmatrix* m) {
@@ -480,6 +489,13 @@ int mlb_context_reset(mlb_context* c) {
   return guarded([&] {
     if (!c) invalid("mlb_context_reset: null context");
     context_reset(*c->impl);
+  });
+}
+
+int mlb_context_fill_kv(mlb_context* c, int n_pos, uint64_t seed, float scale) {
+  return guarded([&] {
+    if (!c) invalid("mlb_context_fill_kv: null context");
+    context_fill_kv(*c->impl, n_pos, seed, scale);
   });
 }
 

@@ -164,6 +164,71 @@ void qmatrix_repack(const QMatrix& m, const uint8_t* src, size_t src_pitch, cons
   MLB_CUDA(cudaGetLastError());
 }
 
+// ------------------------------------------------------------------ dequant
+
+// Dequantised weights straight from the repacked super-block layout: one
+// thread per (row, GGUF block) of the logical [n, k] matrix reads the codes
+// and scales where the GEMV's lanes read them (repack_kernel's placement) and
+// decodes each 4-bit code through the same magic-exponent half (1024 + q),
+// then forms the value as DequantizeFromQ40/Q41/Q80 do (src/quant.cc:170-361):
+// Q4_0 (q - 8) * d, Q4_1 q * d + m (product and sum each rounded), Q8_0
+// d * q. Inputs past k are not written.
+__global__ void dequant_sb_kernel(int qtype, const uint8_t* sbs, int ntiles, int nchunks, int gc,
+                                  int n, int k, float* out) {
+  const long long tid = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  const int kb = (k + 31) / 32;
+  if (tid >= (long long)n * kb) return;
+  const int R = (int)(tid / kb), blk = (int)(tid - (long long)R * kb);
+  const int t = R >> 4, r16 = R & 15, g = r16 & 7, h = r16 >> 3;
+  const int c = blk >> 3, b = blk & 7;
+  const int sbb = qtype == MLB_Q8_0 ? 4352 : (qtype == MLB_Q4_1 ? 2560 : 2304);
+  const int qbytes = qtype == MLB_Q8_0 ? 4096 : 2048;
+  const uint8_t* sb = sbs + sb_index(t, c, ntiles, nchunks, gc) * sbb;
+  const uint8_t* sc = sb + qbytes + (g * 8 + b) * 4 + 2 * h;
+  const float d = __half2float(__ushort_as_half((unsigned short)(sc[0] | (sc[1] << 8))));
+  float m = 0.0f;
+  if (qtype == MLB_Q4_1) {
+    const uint8_t* mm = sb + 2304 + (g * 8 + b) * 4 + 2 * h;
+    m = __half2float(__ushort_as_half((unsigned short)(mm[0] | (mm[1] << 8))));
+  }
+  float* o = out + (size_t)R * k + (size_t)blk * 32;
+  const int nv = min(32, k - blk * 32);
+  for (int cl = 0; cl < 4; ++cl) {
+    const int lane = g * 4 + cl;
+    if (qtype == MLB_Q8_0) {
+      const int8_t* q = reinterpret_cast<const int8_t*>(sb + (size_t)(b * 32 + lane) * 16 + h * 8);
+      const int ks[8] = {2 * cl, 2 * cl + 1, 2 * cl + 8, 2 * cl + 9,
+                         2 * cl + 16, 2 * cl + 17, 2 * cl + 24, 2 * cl + 25};
+      for (int i = 0; i < 8; ++i)
+        if (ks[i] < nv) o[ks[i]] = __fmul_rn(d, (float)q[i]);
+    } else {
+      const uint8_t* q = sb + (size_t)((b >> 1) * 32 + lane) * 16 + (b & 1) * 8 + h * 4;
+      const int js[4] = {2 * cl, 2 * cl + 8, 2 * cl + 1, 2 * cl + 9};
+      for (int i = 0; i < 4; ++i) {
+        for (int hi = 0; hi < 2; ++hi) {
+          const int pos = js[i] + 16 * hi;
+          if (pos >= nv) continue;
+          const unsigned nib = hi ? (q[i] >> 4) : (q[i] & 15u);
+          const float code = __half2float(__ushort_as_half((unsigned short)(0x6400u | nib)));
+          if (qtype == MLB_Q4_0)
+            o[pos] = __fmul_rn(__fsub_rn(code, 1032.0f), d);
+          else
+            o[pos] = __fadd_rn(__fmul_rn(__fsub_rn(code, 1024.0f), d), m);
+        }
+      }
+    }
+  }
+}
+
+void qmatrix_dequant(const QMatrix& m, float* out, cudaStream_t stream) {
+  if (m.qtype == MLB_F32) invalid("mlb_qmatrix_dequant: F32 weights have no quantised form");
+  const long long total = (long long)m.n * ((m.k + 31) / 32);
+  if (total == 0) return;
+  dequant_sb_kernel<<<(unsigned)((total + 255) / 256), 256, 0, stream>>>(
+      m.qtype, m.data, m.ntiles, m.nchunks, m.gc, m.n, m.k, out);
+  MLB_CUDA(cudaGetLastError());
+}
+
 // ---------------------------------------------------- super-block GEMV kernel
 
 struct GemvKArgs {

@@ -168,6 +168,10 @@ void gemv_launch(const QMatrix& m, const float* x, int rows, int ldx, const Norm
 // Number of kernels gemv_launch issues for `rows` (>= 1).
 int gemv_kernel_count(const QMatrix& m, int rows);
 
+// Dequantised fp32 [n, k] (row-major, device) of a quantised matrix, decoded
+// from its super-block layout.
+void qmatrix_dequant(const QMatrix& m, float* out, cudaStream_t stream);
+
 // Generic GEMV straight over raw GGUF blocks (any shape; the standalone API).
 void gemv_gguf(int qtype, const float* x, int rows, int k, const void* w, int n, float* y,
                cudaStream_t stream);

@@ -1100,3 +1100,45 @@ void context_reset(ContextImpl& c) {
 }
 
 }  // namespace mlb
+
+namespace mlb {
+
+// Positions [0, n_pos) of every layer of this rank's K and V cache from the
+// seeded generator: element (pos, global KV head, d) of layer l is
+// gauss(key, (pos * KV + head) * D + d) * scale, keys of streams 15 * 2^20 + l
+// (K) and 16 * 2^20 + l (V) -- a decode state at depth n_pos without running
+// n_pos steps (the CPU oracle writes the same values).
+__global__ void fill_kv_kernel(float* keys, float* values, int L, int S, int KVl, int KV, int kv0,
+                               int D, int n_pos, uint64_t seed, float scale) {
+  const long long per_layer = (long long)n_pos * KVl * D;
+  const long long total = per_layer * L;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int l = (int)(i / per_layer);
+    const long long r = i - (long long)l * per_layer;
+    const int p = (int)(r / ((long long)KVl * D));
+    const int rem = (int)(r - (long long)p * KVl * D);
+    const int h = rem / D, d = rem - h * D;
+    const uint64_t idx = ((uint64_t)p * KV + (uint64_t)(kv0 + h)) * D + d;
+    const uint64_t kk = synth::stream_key(seed, 15ull * (1ull << 20) + (uint64_t)l);
+    const uint64_t kv = synth::stream_key(seed, 16ull * (1ull << 20) + (uint64_t)l);
+    const size_t o = (((size_t)l * S + p) * KVl + h) * D + d;
+    keys[o] = synth::fmul(synth::gauss(kk, idx), scale);
+    values[o] = synth::fmul(synth::gauss(kv, idx), scale);
+  }
+}
+
+void context_fill_kv(ContextImpl& c, int n_pos, uint64_t seed, float scale) {
+  const mlb_config& cf = c.m->cfg;
+  if (n_pos < 0 || n_pos > cf.max_seq_len) out_of_range("mlb_context_fill_kv: n_pos out of range");
+  set_device(c.m->device);
+  if (n_pos > 0) {
+    fill_kv_kernel<<<sm_count(c.m->device) * 8, 256, 0, c.stream>>>(
+        c.keys.as<float>(), c.values.as<float>(), cf.n_layers, cf.max_seq_len, c.m->kv_heads,
+        cf.n_kv_heads, c.m->kv_head0, cf.head_dim, n_pos, seed, scale);
+    MLB_CUDA(cudaGetLastError());
+  }
+  MLB_CUDA(cudaStreamSynchronize(c.stream));
+}
+
+}  // namespace mlb

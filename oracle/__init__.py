@@ -33,10 +33,9 @@ _vp = ctypes.c_void_p
 
 
 def build(ref: bool = True) -> None:
-    """Build the port (always) and the reference shim (when its tree exists)."""
-    targets = ["port"]
-    if ref and os.path.isdir(os.environ.get("REF_ROOT", "/root/reference") + "/src"):
-        targets.append("ref")
+    """Build the port (always) and the reference shim (when oracle/Makefile
+    finds the reference tree; REF_ROOT in the environment overrides where)."""
+    targets = ["port"] + (["ref-if-present"] if ref else [])
     subprocess.run(["make", "-s", "-C", HERE] + targets, check=True)
 
 
@@ -243,6 +242,9 @@ class Ref(_Lib):
         L.ref_ctx_destroy.argtypes = [_vp]
         L.ref_forward_token.argtypes = [_vp, ctypes.c_int, ctypes.c_int, _f]
         L.ref_set_threads.argtypes = [ctypes.c_int]
+        L.ref_model_synthesize.argtypes = [_vp, ctypes.c_int, ctypes.c_uint64, ctypes.c_int,
+                                           ctypes.c_int]
+        L.ref_ctx_fill_kv.argtypes = [_vp, ctypes.c_int, ctypes.c_uint64, ctypes.c_float]
 
     def set_threads(self, n):
         self.lib.ref_set_threads(n)
@@ -279,11 +281,28 @@ class RefModel:
         self.ref._check(self.ref.lib.ref_model_set_weight(self.h, kind, layer, qtype, rows, cols,
                                                           _ptr(data)))
 
-    def forward_token(self, token, pos):
+    def synthesize(self, qtype, seed, with_bias=False, threads=8):
+        """Every weight from the seeded generator, quantised with the
+        reference's own quantisers (ref_model_synthesize in ref_shim.cc):
+        the bytes the GPU library's CudaModel.synthesize generates."""
+        self.ref._check(self.ref.lib.ref_model_synthesize(self.h, qtype, seed, int(with_bias),
+                                                          threads))
+        return self
+
+    def _context(self):
         if self.ctx is None:
             self.ctx = self.ref.lib.ref_ctx_create(self.h)
             if not self.ctx:
                 raise RuntimeError(self.ref.lib.ref_last_error().decode())
+        return self.ctx
+
+    def fill_kv(self, n_pos, seed, scale=1.25):
+        """Seeded K/V rows for positions [0, n_pos) of every layer, written with
+        KvCache::Write (the values mlb_context_fill_kv writes on the GPU)."""
+        self.ref._check(self.ref.lib.ref_ctx_fill_kv(self._context(), n_pos, seed, scale))
+
+    def forward_token(self, token, pos):
+        self._context()
         out = np.zeros(self.cfg["vocab_size"], np.float32)
         self.ref._check(self.ref.lib.ref_forward_token(self.ctx, token, pos, _fptr(out)))
         return out

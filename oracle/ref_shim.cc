@@ -17,10 +17,19 @@
 #include "mini_llama/quant.h"
 #include "mini_llama/thread_pool.h"
 
+#include <algorithm>
+#include <atomic>
 #include <cstring>
+#include <exception>
+#include <functional>
 #include <memory>
+#include <mutex>
 #include <stdexcept>
 #include <string>
+#include <thread>
+#include <vector>
+
+#include "synth.h"  // the seeded input generator shared with the GPU library
 
 using namespace mini_llama;
 
@@ -257,6 +266,116 @@ int ref_model_config(void* h, int* out11) {
   return 0;
 }
 
+// Every weight of the model from the seeded generator (synth.h, the same
+// definition the GPU library generates from): fp32 values gauss(key, index) *
+// 0.02, quantised here with the reference's own QuantizeToQ80 / QuantizeToQ40
+// (src/quant.cc:106-276); Q4_1 has no quantiser in the reference's library,
+// so it takes the generator's restatement of the reference test's
+// QuantizeToQ41ForTest. Norms are 1.0, the embedding fp32, biases (when
+// with_bias) fp32. Rows are generated and quantised in chunks on `threads`
+// threads, so no full fp32 copy of a large matrix is ever held. The bytes equal
+// what the GPU library's generator writes (the tests compare them).
+int ref_model_synthesize(void* h, int qtype, uint64_t seed, int with_bias, int threads) {
+  try {
+    MiniLlamaModel& m = static_cast<RefModel*>(h)->model;
+    const ModelConfig& c = m.config;
+    if (qtype < 1 || qtype > 3) throw std::runtime_error("ref_model_synthesize: quantised types only");
+    threads = threads < 1 ? 1 : threads;
+    auto key_of = [&](int kind, int layer) {
+      return mlb::synth::stream_key(seed, (uint64_t)kind * (1ull << 20) + (uint64_t)(layer < 0 ? 0 : layer));
+    };
+    auto par = [&](long long rows, const std::function<void(long long, long long)>& f) {
+      const long long chunk = 64;
+      const long long nchunks = (rows + chunk - 1) / chunk;
+      std::atomic<long long> next{0};
+      std::vector<std::thread> ts;
+      std::exception_ptr err;
+      std::mutex mu;
+      for (int t = 0; t < threads; ++t)
+        ts.emplace_back([&] {
+          try {
+            for (long long i; (i = next.fetch_add(1)) < nchunks;)
+              f(i * chunk, std::min(rows, (i + 1) * chunk));
+          } catch (...) {
+            std::lock_guard<std::mutex> g(mu);
+            err = std::current_exception();
+          }
+        });
+      for (auto& th : ts) th.join();
+      if (err) std::rethrow_exception(err);
+    };
+    auto f32 = [&](int kind, int layer, int rows, int cols, bool one_d) {
+      Tensor t(one_d ? std::vector<int>{rows * cols} : std::vector<int>{rows, cols}, 0.0f);
+      const uint64_t key = key_of(kind, layer);
+      par(rows, [&](long long a, long long b) {
+        for (long long r = a; r < b; ++r)
+          for (int j = 0; j < cols; ++j)
+            t.data[(size_t)r * cols + j] =
+                mlb::synth::fmul(mlb::synth::gauss(key, (uint64_t)(r * cols + j)), 0.02f);
+      });
+      return t;
+    };
+    auto ones = [&](int n) { return Tensor(std::vector<int>{n}, 1.0f); };
+    auto quant = [&](int kind, int layer, int rows, int cols) {
+      QuantizedTensor q;
+      q.shape = {rows, cols};
+      const int nb = (cols + 31) / 32;
+      const uint64_t key = key_of(kind, layer);
+      const size_t nblk = (size_t)rows * nb;
+      if (qtype == 1) { q.type = QuantType::kQ80; q.q8_0_data.resize(nblk); }
+      if (qtype == 2) { q.type = QuantType::kQ40; q.q4_0_data.resize(nblk); }
+      if (qtype == 3) { q.type = QuantType::kQ41; q.q4_1_data.resize(nblk); }
+      par(rows, [&](long long a, long long b) {
+        Tensor src(std::vector<int>{(int)(b - a), cols}, 0.0f);
+        for (long long r = a; r < b; ++r)
+          for (int j = 0; j < cols; ++j)
+            src.data[(size_t)(r - a) * cols + j] =
+                mlb::synth::fmul(mlb::synth::gauss(key, (uint64_t)(r * cols + j)), 0.02f);
+        const size_t off = (size_t)a * nb;
+        if (qtype == 1) {
+          auto blk = QuantizeToQ80(src);
+          std::memcpy(&q.q8_0_data[off], blk.data(), blk.size() * sizeof(BlockQ80));
+        } else if (qtype == 2) {
+          auto blk = QuantizeToQ40(src);
+          std::memcpy(&q.q4_0_data[off], blk.data(), blk.size() * sizeof(BlockQ40));
+        } else {
+          for (long long r = a; r < b; ++r)
+            for (int j = 0; j < nb; ++j) {
+              const int n = std::min(32, cols - 32 * j);
+              mlb::synth::quantize_q4_1(&src.data[(size_t)(r - a) * cols + 32 * j], n,
+                                        reinterpret_cast<uint8_t*>(&q.q4_1_data[(size_t)r * nb + j]));
+            }
+        }
+      });
+      return q;
+    };
+    const int D = c.head_dim, qd = c.n_heads * D, kvd = c.n_kv_heads * D;
+    for (int l = 0; l < c.n_layers; ++l) {
+      LayerWeights& lw = m.layers[l];
+      lw.attention_norm = ones(c.dim);
+      lw.wq = quant(4, l, qd, c.dim);
+      lw.wk = quant(5, l, kvd, c.dim);
+      lw.wv = quant(6, l, kvd, c.dim);
+      if (with_bias) {
+        lw.bq = f32(7, l, 1, qd, true);
+        lw.bk = f32(8, l, 1, kvd, true);
+        lw.bv = f32(9, l, 1, kvd, true);
+      }
+      lw.wo = quant(10, l, c.dim, qd);
+      lw.ffn_norm = ones(c.dim);
+      lw.w_gate = quant(12, l, c.hidden_dim, c.dim);
+      lw.w_up = quant(13, l, c.hidden_dim, c.dim);
+      lw.w_down = quant(14, l, c.dim, c.hidden_dim);
+    }
+    m.token_embedding = f32(0, -1, c.vocab_size, c.dim, false);
+    m.final_norm = ones(c.dim);
+    m.lm_head = quant(2, -1, c.vocab_size, c.dim);
+    return 0;
+  } catch (const std::exception& e) {
+    return Fail(e);
+  }
+}
+
 void* ref_ctx_create(void* h) {
   try {
     auto* c = new RefCtx();
@@ -270,6 +389,38 @@ void* ref_ctx_create(void* h) {
 }
 
 void ref_ctx_destroy(void* c) { delete static_cast<RefCtx*>(c); }
+
+// Positions [0, n_pos) of every layer's K and V rows from the seeded
+// generator, written through the reference's own KvCache::Write
+// (src/kv_cache.cc): element (pos, kv_head, d) of layer l is
+// gauss(key, (pos * n_kv_heads + kv_head) * head_dim + d) * scale with the keys
+// of streams 15 * 2^20 + l (K) and 16 * 2^20 + l (V). The GPU library's
+// mlb_context_fill_kv writes the same values, so both decode from the same
+// state at depth n_pos.
+int ref_ctx_fill_kv(void* ch, int n_pos, uint64_t seed, float scale) {
+  try {
+    auto* c = static_cast<RefCtx*>(ch);
+    const ModelConfig& cf = c->m->model.config;
+    if (n_pos < 0 || n_pos > cf.max_seq_len) throw std::out_of_range("ref_ctx_fill_kv: n_pos out of range");
+    const int KV = cf.n_kv_heads, D = cf.head_dim;
+    Tensor k(std::vector<int>{KV, D}, 0.0f), v(std::vector<int>{KV, D}, 0.0f);
+    for (int l = 0; l < cf.n_layers; ++l) {
+      const uint64_t kk = mlb::synth::stream_key(seed, 15ull * (1ull << 20) + (uint64_t)l);
+      const uint64_t kv = mlb::synth::stream_key(seed, 16ull * (1ull << 20) + (uint64_t)l);
+      for (int p = 0; p < n_pos; ++p) {
+        for (int i = 0; i < KV * D; ++i) {
+          const uint64_t idx = (uint64_t)p * KV * D + (uint64_t)i;
+          k.data[i] = mlb::synth::fmul(mlb::synth::gauss(kk, idx), scale);
+          v.data[i] = mlb::synth::fmul(mlb::synth::gauss(kv, idx), scale);
+        }
+        c->ctx->kv_cache.Write(l, p, k, v);
+      }
+    }
+    return 0;
+  } catch (const std::exception& e) {
+    return Fail(e);
+  }
+}
 
 // ForwardToken (CPU branch: the model has no cuda_weights).
 int ref_forward_token(void* ch, int token, int pos, float* logits) {

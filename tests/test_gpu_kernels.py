@@ -91,6 +91,55 @@ def test_qmatrix_gemv_vs_oracle(cuda, port, qtype, shape):
         np.testing.assert_array_equal(got, again)
 
 
+def random_blocks(qtype, n, k, seed):
+    """GGUF blocks with uniform random codes and random finite fp16 scales (and
+    Q4_1 mins), subnormals and negative values included."""
+    rng = np.random.default_rng(seed)
+    nb, bs = (k + 31) // 32, C.BLOCK_BYTES[qtype]
+    blk = rng.integers(0, 256, (n, nb, bs), dtype=np.uint8)
+    nhalf = 2 if qtype == C.Q4_1 else 1
+    h = rng.integers(0, 1 << 16, (n, nb, nhalf), dtype=np.uint32)
+    h = np.where((h & 0x7C00) == 0x7C00, h & 0x83FF, h).astype(np.uint16)  # no inf/nan
+    blk[:, :, :2 * nhalf] = h.view(np.uint8).reshape(n, nb, 2 * nhalf)
+    return blk.reshape(n, nb * bs)
+
+
+@pytest.mark.parametrize("qtype", [C.Q4_0, C.Q4_1, C.Q8_0])
+@pytest.mark.parametrize("shape", [(4096, 4096), (11008, 4096), (14336, 4096), (515, 160),
+                                   (100, 288), (33, 4128), (16, 32)])
+def test_qmatrix_dequant_bit_exact(cuda, port, qtype, shape):
+    """The repacked super-block layout decodes to exactly the reference's
+    DequantizeFromQ80/Q40/Q41 (src/quant.cc:170-361): raw float32 bits equal,
+    for the sweep shapes and ragged ones (K = 160, 288, 4128)."""
+    import oracle
+
+    n, k = shape
+    blocks = random_blocks(qtype, n, k, n * 7 + k)
+    qm = mlb.QMatrix.from_gguf(qtype, blocks, n, k)
+    got = qm.dequant().cpu().numpy()
+    want = port.dequant(qtype, blocks, n, k)
+    np.testing.assert_array_equal(got.view(np.uint32), want.view(np.uint32))
+    if oracle.ref_available():
+        ref = oracle.ref().dequant(qtype, blocks, n, k)
+        np.testing.assert_array_equal(got.view(np.uint32), ref.view(np.uint32))
+    # the same bits from a matrix the device generator filled (reference quantiser)
+    dev = mlb.QMatrix.synthesize(qtype, n, k, 13, 4321)
+    s = mlb._lib.synth_lib()
+    nb = (k + 31) // 32
+    hb = np.empty((n, nb * C.BLOCK_BYTES[qtype]), np.uint8)
+    s.mlbs_gguf(qtype, s.mlbs_stream_key(13, 4321), 0.02, 0, 0, n, 0, nb, k, hb.ctypes.data,
+                hb.shape[1], 8)
+    np.testing.assert_array_equal(dev.dequant().cpu().numpy().view(np.uint32),
+                                  port.dequant(qtype, hb, n, k).view(np.uint32))
+
+
+def test_qmatrix_dequant_rejects_f32(cuda):
+    w = np.ones((16, 32), np.float32)
+    qm = mlb.QMatrix.from_gguf(C.F32, w, 16, 32)
+    with pytest.raises(mlb.MlbError, match="F32"):
+        qm.dequant()
+
+
 @pytest.mark.parametrize("qtype", [C.Q4_0, C.Q4_1, C.Q8_0])
 def test_device_generator_matches_host_generator(cuda, qtype):
     """Weights synthesised on the GPU equal the CPU generator's bytes: the

@@ -192,3 +192,41 @@ def test_forward_errors_match_reference(port, ref):
             pm.forward_token(bad_tok, bad_pos)
         with pytest.raises(IndexError):
             rm.forward_token(bad_tok, bad_pos)
+
+
+# ------------------------------------------- reference arm inputs (no project .so)
+
+@pytest.mark.parametrize("qtype,bias", [(C.Q8_0, False), (C.Q4_0, False), (C.Q4_1, True)])
+def test_reference_model_synthesis_equals_generator_bytes(ref, qtype, bias):
+    """The reference arm builds its model inside oracle/_ref (the seeded
+    generator quantised with the reference's own QuantizeToQ80/Q40): its
+    logits equal, bit for bit, those of the same model loaded from the GPU
+    library's host generator, so both arms decode identical weights."""
+    cfg = dict(vocab_size=300, dim=96, hidden_dim=160, n_layers=2, n_heads=4, n_kv_heads=2,
+               head_dim=24, max_seq_len=16, rope_theta=10000.0, rms_norm_eps=1e-5,
+               rope_type=1 if bias else 0)
+    a = ref.model(cfg).synthesize(qtype, 77, bias, threads=3)
+    b = ref.model(cfg)
+    for kind, layer, qt, rows, cols, arr in C.host_weights(cfg, qtype, 77, bias):
+        b.set_weight(kind, layer, qt, rows, cols, arr)
+    tok = 5
+    for pos in range(4):
+        la, lb = a.forward_token(tok, pos), b.forward_token(tok, pos)
+        np.testing.assert_array_equal(la.view(np.uint32), lb.view(np.uint32))
+        tok = int(np.argmax(la))
+
+
+def test_reference_kv_fill_is_deterministic(ref):
+    cfg = dict(vocab_size=200, dim=64, hidden_dim=96, n_layers=2, n_heads=4, n_kv_heads=4,
+               head_dim=16, max_seq_len=32, rope_theta=10000.0, rms_norm_eps=1e-5, rope_type=0)
+    outs = []
+    for _ in range(2):
+        m = ref.model(cfg).synthesize(C.Q4_0, 3)
+        m.fill_kv(20, 11)
+        outs.append(m.forward_token(7, 20))
+    np.testing.assert_array_equal(outs[0], outs[1])
+    m = ref.model(cfg).synthesize(C.Q4_0, 3)
+    m.fill_kv(20, 12)  # another seed changes the attended context
+    assert not np.array_equal(outs[0], m.forward_token(7, 20))
+    with pytest.raises(IndexError):
+        m.fill_kv(33, 1)

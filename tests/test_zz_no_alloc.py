@@ -55,6 +55,57 @@ def test_noalloc_matches_allocating_entry_point(H, KV, D, S, mode):
         assert err.max() <= TOL, f"call {call}: max error {err.max():.2e}"
 
 
+@pytest.mark.parametrize("H,KV,D,S", [
+    (2048, 128, 128, 256),  # one split needs 266,240 floats: 3 splits fit where 4 are wanted
+    (32, 8, 128, 300),      # GQA 4:1, the 8B shape
+    (4, 2, 10, 40),         # head_dim not a multiple of 4: the generic kernel (no scratch)
+])
+def test_noalloc_matches_oracle(port, H, KV, D, S):
+    """Against the CPU oracle (oracle/port, the reference CPU attention with
+    its V-sum rule, src/forward.cc:463-545), not only against the allocating
+    entry point: a shape whose split count is cut to fit the fixed scratch, a
+    GQA shape, and a head_dim that takes the generic kernel. Two calls each."""
+    torch = pytest.importorskip("torch")
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    from mini_llama_b200 import _lib
+
+    lib = _lib.lib()
+    gen = torch.Generator(device="cuda").manual_seed(H + KV + D)
+    keys = torch.randn(2, S, KV, D, device="cuda", generator=gen)
+    values = torch.randn(2, S, KV, D, device="cuda", generator=gen)
+    kn, vn = keys.cpu().numpy(), values.cpu().numpy()
+    for mode in (0, 1):
+        for pos in (S - 1, S // 2):
+            q = torch.randn(H * D, device="cuda", generator=gen)
+            got = _attention(lib, "mlb_attention_decode_noalloc", q, keys, values, 1, pos, H, KV,
+                             D, mode)
+            want = port.attention(q.cpu().numpy(), kn, vn, 1, pos, H, KV, D,
+                                  include_current_v=bool(mode)).reshape(-1)
+            err = np.abs(got - want) / np.maximum(1.0, np.abs(want))
+            assert err.max() <= TOL, f"mode {mode} pos {pos}: max error {err.max():.2e}"
+            alloc = _attention(lib, "mlb_attention_decode", q, keys, values, 1, pos, H, KV, D,
+                               mode)
+            err = np.abs(got - alloc) / np.maximum(1.0, np.abs(alloc))
+            assert err.max() <= TOL
+
+
+def test_noalloc_rejects_a_split_beyond_its_scratch():
+    """KV = 256, 16 query heads per KV head, head_dim 256: one split alone needs
+    256 * 16 * 258 = 1,056,768 partial floats, above the 2^20 the array holds."""
+    torch = pytest.importorskip("torch")
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    from mini_llama_b200 import _lib
+
+    lib = _lib.lib()
+    buf = torch.zeros(16, device="cuda")
+    p = ctypes.c_void_p(buf.data_ptr())
+    rc = lib.mlb_attention_decode_noalloc(p, p, p, 1, 4, 0, 1, 4096, 256, 256, 0, p, 0, None)
+    assert rc == -1
+    assert b"scratch floats, above the fixed limit of 1048576" in lib.mlb_last_error()
+
+
 def test_noalloc_rejects_shapes_beyond_its_scratch():
     torch = pytest.importorskip("torch")
     if not torch.cuda.is_available():
