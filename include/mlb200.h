@@ -203,8 +203,18 @@ int mlb_qmatrix_create(int qtype, const void* w, int w_is_host,
 int mlb_qmatrix_synthesize(int qtype, int out_features, int in_features,
                            uint64_t seed, uint64_t stream_id, int raw,
                            int device_id, mlb_qmatrix** out);
-/* y[rows, out] = x[rows, in] * W^T, device pointers, on `stream`. */
+/* y[rows, out] = x[rows, in] * W^T, device pointers, on `stream`. Up to 4
+ * rows run the batch-1 GEMV (mma.sync over in-register dequantised codes);
+ * more rows run mlb_qmatrix_gemm. */
 int mlb_qmatrix_gemv(mlb_qmatrix* m, const float* x_dev, int rows, float* y_dev,
+                     void* stream);
+/* The same product on the tcgen05 tensor cores for any row count (64 rows per
+ * pass of the weights): codes dequantised to exact fp16 hi + lo pairs in
+ * tensor memory, activations as fp16 hi + lo, fp32 accumulation. Replaces the
+ * per-row loop a batch takes through LinearQ80/Q40/Q41 (src/quant.cc:365-471;
+ * ForwardBatch, src/batch.cc:35-50, runs one token at a time). Quantised types
+ * only. The first call on a matrix allocates its scratch. */
+int mlb_qmatrix_gemm(mlb_qmatrix* m, const float* x_dev, int rows, float* y_dev,
                      void* stream);
 /* The prepared weight dequantised back to fp32, out_dev[out_features *
  * in_features] row-major, decoded from the repacked layout the GEMV streams.
@@ -320,6 +330,48 @@ int mlb_context_kernels_per_step(const mlb_context* c);
 int mlb_context_set_step_kernel(mlb_context* c, int enable);
 /* 1 when this context's steps run as the persistent step kernel, else 0. */
 int mlb_context_step_kernel(const mlb_context* c);
+
+/* ------------------------------------------------------------------ batches
+ * Rows of (token, position) go through every layer together: the weights
+ * stream once per pass of up to 64 rows through the tcgen05 tensor-core GEMM
+ * (mlb_qmatrix_gemm) with the fused prologue/epilogues of the single-token
+ * step, and attention runs one CTA per (KV head, split, row). Tensor-parallel
+ * models all-reduce the wo and w_down partial sums with NCCL. */
+
+/* ForwardBatch (src/batch.cc:35-50) on one context: n_tokens tokens at their
+ * positions (strictly increasing: the reference feeds them one ForwardToken
+ * at a time, so each token sees the K/V of the ones before it), the KV cache
+ * written for every position, the logits of the last token to host. Prompt
+ * prefill in passes of 64 rows. Synchronous. */
+int mlb_forward_batch(mlb_context* c, int n_tokens, const int* tokens,
+                      const int* positions, float* logits_host);
+
+/* A batch of 1..64 independent sequences decoded together, each with its own
+ * fp32 KV cache laid out as CudaKvCache's [L][max_seq][KV][D]. The reference
+ * has no multi-sequence decode (one MiniLlamaContext per sequence); a batch
+ * replaces that many contexts stepping in lockstep. */
+typedef struct mlb_batch mlb_batch;
+int mlb_batch_create(mlb_model* m, int n_seqs, int attention_mode, mlb_batch** out);
+int mlb_batch_destroy(mlb_batch* b);
+/* Clears every sequence's KV cache. */
+int mlb_batch_reset(mlb_batch* b);
+/* mlb_context_fill_kv for sequence `seq` (the same seeded values). */
+int mlb_batch_fill_kv(mlb_batch* b, int seq, int n_pos, uint64_t seed, float scale);
+/* One pass of n_rows rows (seq_ids[i], tokens[i], positions[i]); rows of one
+ * sequence need strictly increasing positions. Writes each row's greedy
+ * token (ArgMax tie rule) to next_tokens_host[i] and, when logits_host is not
+ * NULL, its logits to logits_host[i * vocab]. Synchronous. */
+int mlb_batch_forward(mlb_batch* b, int n_rows, const int* seq_ids, const int* tokens,
+                      const int* positions, float* logits_host, int* next_tokens_host);
+/* Greedy decode of all n_seqs sequences in lockstep for n_steps steps:
+ * sequence s starts from tokens[s] at positions[s]; tokens_out[step * n_seqs
+ * + s] receives the argmax of each step. One CUDA graph launch per step, no
+ * host round trip between steps. */
+int mlb_batch_decode_greedy(mlb_batch* b, const int* tokens, const int* positions, int n_steps,
+                            int* tokens_out);
+/* The batch's stream (cudaStream_t) and the kernels one decode step launches. */
+void* mlb_batch_stream(mlb_batch* b);
+int mlb_batch_kernels_per_step(const mlb_batch* b);
 
 /* 128-byte NCCL unique id for building a tensor-parallel communicator. */
 int mlb_nccl_unique_id(void* out128);

@@ -32,7 +32,7 @@ __all__ = [
     "CudaRmsNormDeviceWeight", "CudaSiluDeviceInput", "CudaElementwiseMulDeviceInput",
     "CudaElementwiseAddDeviceInput", "CudaSoftmax", "CudaEmbeddingLookupDeviceWeight",
     "CudaRopeDeviceInput", "CudaArgMax", "CudaKvCache", "CudaAttentionDecodeDeviceInput",
-    "QMatrix", "CudaModel", "Context", "ForwardToken", "configs", "tp_plan", "nccl_unique_id",
+    "QMatrix", "CudaModel", "Context", "Batch", "ForwardToken", "configs", "tp_plan", "nccl_unique_id",
 ]
 
 
@@ -348,6 +348,16 @@ class QMatrix:
         check(lib().mlb_qmatrix_gemv(self.h, _ptr(x), rows, _ptr(y), _stream(stream)))
         return y
 
+    def gemm(self, x, y=None, stream=None):
+        """y = W x on the tensor cores (mlb_qmatrix_gemm), any row count."""
+        torch = _torch()
+        rows = 1 if x.dim() == 1 else x.shape[0]
+        if y is None:
+            y = torch.empty((rows, self.out_features) if x.dim() == 2 else (self.out_features,),
+                            dtype=torch.float32, device=x.device)
+        check(lib().mlb_qmatrix_gemm(self.h, _ptr(x), rows, _ptr(y), _stream(stream)))
+        return y
+
     def dequant(self, out=None, stream=None):
         """fp32 [out_features, in_features] on the device, decoded from the
         repacked layout (DequantizeFromQ80/Q40/Q41, src/quant.cc:170-361)."""
@@ -476,6 +486,16 @@ class Context:
         """Seeded K/V rows for positions [0, n_pos) (mlb_context_fill_kv)."""
         check(lib().mlb_context_fill_kv(self.h, int(n_pos), int(seed), float(scale)))
 
+    def forward_batch(self, tokens, positions) -> np.ndarray:
+        """ForwardBatch (src/batch.cc:35-50): every token at its position, the
+        last token's logits (mlb_forward_batch)."""
+        t = np.ascontiguousarray(tokens, np.int32)
+        p = np.ascontiguousarray(positions, np.int32)
+        out = np.empty(self.model.cfg["vocab_size"], np.float32)
+        check(lib().mlb_forward_batch(self.h, len(t), t.ctypes.data, p.ctypes.data,
+                                      out.ctypes.data))
+        return out
+
     def stream(self) -> int:
         return lib().mlb_context_stream(self.h) or 0
 
@@ -485,6 +505,60 @@ class Context:
     def close(self):
         if getattr(self, "h", None):
             lib().mlb_context_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class Batch:
+    """n_seqs sequences decoded together (mlb_batch_*), each with its own KV cache."""
+
+    def __init__(self, model: CudaModel, n_seqs: int, attention_mode=ATTN_CPU_COMPAT):
+        self.model = model
+        self.n_seqs = n_seqs
+        h = ctypes.c_void_p()
+        check(lib().mlb_batch_create(model.h, int(n_seqs), attention_mode, ctypes.byref(h)))
+        self.h = h
+
+    def reset(self):
+        check(lib().mlb_batch_reset(self.h))
+
+    def fill_kv(self, seq: int, n_pos: int, seed: int, scale: float = 1.25):
+        check(lib().mlb_batch_fill_kv(self.h, int(seq), int(n_pos), int(seed), float(scale)))
+
+    def forward(self, seqs, tokens, positions, logits=False):
+        """One pass of rows; returns (next greedy ids, logits [rows, vocab] or None)."""
+        s = np.ascontiguousarray(seqs, np.int32)
+        t = np.ascontiguousarray(tokens, np.int32)
+        p = np.ascontiguousarray(positions, np.int32)
+        nxt = np.empty(len(t), np.int32)
+        lg = np.empty((len(t), self.model.cfg["vocab_size"]), np.float32) if logits else None
+        check(lib().mlb_batch_forward(self.h, len(t), s.ctypes.data, t.ctypes.data, p.ctypes.data,
+                                      lg.ctypes.data if logits else None, nxt.ctypes.data))
+        return [int(v) for v in nxt], lg
+
+    def decode_greedy(self, tokens, positions, n_steps: int) -> np.ndarray:
+        """[n_steps, n_seqs] greedy ids, all sequences in lockstep."""
+        t = np.ascontiguousarray(tokens, np.int32)
+        p = np.ascontiguousarray(positions, np.int32)
+        out = np.empty((max(n_steps, 1), self.n_seqs), np.int32)
+        check(lib().mlb_batch_decode_greedy(self.h, t.ctypes.data, p.ctypes.data, int(n_steps),
+                                            out.ctypes.data))
+        return out[:n_steps]
+
+    def stream(self) -> int:
+        return lib().mlb_batch_stream(self.h) or 0
+
+    def kernels_per_step(self) -> int:
+        return lib().mlb_batch_kernels_per_step(self.h)
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().mlb_batch_destroy(self.h)
             self.h = None
 
     def __del__(self):

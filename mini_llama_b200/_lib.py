@@ -65,6 +65,7 @@ SIGNATURES = [
     ("mlb_qmatrix_synthesize", _c_int, [_c_int, _c_int, _c_int, _c_u64, _c_u64, _c_int, _c_int,
                                         ctypes.POINTER(_vp)]),
     ("mlb_qmatrix_gemv", _c_int, [_vp, _vp, _c_int, _vp, _vp]),
+    ("mlb_qmatrix_gemm", _c_int, [_vp, _vp, _c_int, _vp, _vp]),
     ("mlb_qmatrix_dequant", _c_int, [_vp, _vp, _vp]),
     ("mlb_qmatrix_bytes", _c_size_t, [_vp]),
     ("mlb_qmatrix_destroy", _c_int, [_vp]),
@@ -90,6 +91,15 @@ SIGNATURES = [
     ("mlb_context_set_step_kernel", _c_int, [_vp, _c_int]),
     ("mlb_context_step_kernel", _c_int, [_vp]),
     ("mlb_nccl_unique_id", _c_int, [_vp]),
+    ("mlb_forward_batch", _c_int, [_vp, _c_int, _vp, _vp, _vp]),
+    ("mlb_batch_create", _c_int, [_vp, _c_int, _c_int, ctypes.POINTER(_vp)]),
+    ("mlb_batch_destroy", _c_int, [_vp]),
+    ("mlb_batch_reset", _c_int, [_vp]),
+    ("mlb_batch_fill_kv", _c_int, [_vp, _c_int, _c_int, _c_u64, _c_float]),
+    ("mlb_batch_forward", _c_int, [_vp, _c_int, _vp, _vp, _vp, _vp, _vp]),
+    ("mlb_batch_decode_greedy", _c_int, [_vp, _vp, _vp, _c_int, _vp]),
+    ("mlb_batch_stream", _vp, [_vp]),
+    ("mlb_batch_kernels_per_step", _c_int, [_vp]),
 ]
 
 SYNTH_SIGNATURES = [

@@ -34,9 +34,16 @@ struct AttnKArgs {
   int H, KV, D, nsplit;
   float scale;
   int include_current_v;
-  float* ws;            // [KV][nsplit][G][D + 2]
-  int* counters;        // [KV]
-  float* out;           // [H][D]
+  float* ws;            // [KV][nsplit][G][D + 2] per row
+  int* counters;        // [KV] per row
+  float* out;           // [H][D] per row
+  // Batched form (grid.z = rows): row r reads q + r H D, writes out + r H D,
+  // attends positions [0, row_pos[r]] of sequence row_seq[r] (row r when
+  // null) whose cache starts seq_stride floats after the previous sequence's,
+  // and uses the r-th workspace and counter block.
+  const int* row_pos;
+  const int* row_seq;
+  long long seq_stride;
 };
 
 template <int N>
@@ -48,7 +55,14 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnKAr
   extern __shared__ __align__(16) float sm[];
   const int D = a.D, G = a.H / a.KV, KV = a.KV;
   const int pitch = D + 4;  // floats per staged row (no bank conflicts on 16-byte loads)
-  const int kvh = blockIdx.x, split = blockIdx.y;
+  const int kvh = blockIdx.x, split = blockIdx.y, row = blockIdx.z;
+  const int seq = a.row_seq ? a.row_seq[row] : row;
+  const float* keys = a.keys + (size_t)seq * a.seq_stride;
+  const float* values = a.values + (size_t)seq * a.seq_stride;
+  const float* qrow = a.q + (size_t)row * a.H * D;
+  float* outrow = a.out + (size_t)row * a.H * D;
+  float* wsrow = a.ws + (size_t)row * KV * a.nsplit * G * (D + 2);
+  int* cnt = a.counters + (size_t)row * KV;
   float* kt = sm;                              // [2][tile][pitch]
   float* vt = kt + 2 * kAttnTile * pitch;      // [2][tile][pitch]
   const int hstep_ = kAttnThreads / (D / 4);
@@ -62,7 +76,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnKAr
 
   pdl_launch_dependents();  // dependents still wait for this grid to complete
   pdl_wait();
-  const int pos = a.pos_dev ? *a.pos_dev : a.pos_host;
+  const int pos = a.row_pos ? a.row_pos[row] : (a.pos_dev ? *a.pos_dev : a.pos_host);
   const int n = pos + 1;
   // slice of positions, in whole tiles
   const int tiles = (n + kAttnTile - 1) / kAttnTile;
@@ -72,7 +86,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnKAr
   const int v_end = a.include_current_v ? n : pos;  // V rows < v_end are summed
 
   for (int i = threadIdx.x; i < G * D; i += kAttnThreads)
-    qs[i] = a.q[(size_t)(kvh * G) * D + i];
+    qs[i] = qrow[(size_t)(kvh * G) * D + i];
   for (int i = threadIdx.x; i < G; i += kAttnThreads) {
     mrun[i] = -INFINITY;
     lrun[i] = 0.0f;
@@ -87,8 +101,8 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnKAr
       float* vd = vt + (buf * kAttnTile + p) * pitch + c * 4;
       if (t < t_end) {
         const size_t off = (size_t)t * row_stride + (size_t)kvh * D + c * 4;
-        cp_async16(kd, a.keys + off);
-        cp_async16(vd, a.values + off);
+        cp_async16(kd, keys + off);
+        cp_async16(vd, values + off);
       } else {
         *reinterpret_cast<float4*>(kd) = make_float4(0.f, 0.f, 0.f, 0.f);
         *reinterpret_cast<float4*>(vd) = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -201,7 +215,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnKAr
   }
   __syncthreads();
   const int rec = D + 2;
-  float* wsk = a.ws + ((size_t)kvh * a.nsplit + split) * G * rec;
+  float* wsk = wsrow + ((size_t)kvh * a.nsplit + split) * G * rec;
   for (int i = threadIdx.x; i < G * D; i += kAttnThreads) {
     int h = i / D, d = i - h * D;
     float s = 0.0f;
@@ -214,7 +228,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnKAr
   }
   __threadfence();
   __syncthreads();
-  if (threadIdx.x == 0) last_flag = atomicAdd(&a.counters[kvh], 1) == a.nsplit - 1;
+  if (threadIdx.x == 0) last_flag = atomicAdd(&cnt[kvh], 1) == a.nsplit - 1;
   __syncthreads();
   if (!last_flag) return;
   __threadfence();
@@ -225,11 +239,11 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnKAr
   for (int h = warp; h < G; h += 4) {
     float m = -INFINITY;
     for (int s = lane; s < a.nsplit; s += 32)
-      m = fmaxf(m, __ldcg(a.ws + (((size_t)kvh * a.nsplit + s) * G + h) * rec));
+      m = fmaxf(m, __ldcg(wsrow + (((size_t)kvh * a.nsplit + s) * G + h) * rec));
     m = warp_max(m);
     float l = 0.0f;
     for (int s = lane; s < a.nsplit; s += 32) {
-      const float* r = a.ws + (((size_t)kvh * a.nsplit + s) * G + h) * rec;
+      const float* r = wsrow + (((size_t)kvh * a.nsplit + s) * G + h) * rec;
       const float ms = __ldcg(r);
       const float e = ms == -INFINITY ? 0.0f : expf(ms - m);
       wsl[h * a.nsplit + s] = e;
@@ -243,7 +257,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnKAr
   __syncthreads();
   for (int i = threadIdx.x; i < G * D; i += kAttnThreads) {
     const int h = i / D, d = i - h * D;
-    const float* base = a.ws + ((size_t)kvh * a.nsplit * G + h) * rec + 2 + d;
+    const float* base = wsrow + ((size_t)kvh * a.nsplit * G + h) * rec + 2 + d;
     const size_t step = (size_t)G * rec;
     float acc = 0.0f;
     int s = 0;
@@ -256,9 +270,9 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnKAr
       acc = fmaf(o3, wsl[h * a.nsplit + s + 3], acc);
     }
     for (; s < a.nsplit; ++s) acc = fmaf(__ldcg(base + s * step), wsl[h * a.nsplit + s], acc);
-    a.out[(size_t)(kvh * G + h) * D + d] = acc;
+    outrow[(size_t)(kvh * G + h) * D + d] = acc;
   }
-  if (threadIdx.x == 0) a.counters[kvh] = 0;
+  if (threadIdx.x == 0) cnt[kvh] = 0;
 }
 
 // Generic path for shapes the tiled kernel does not take (head_dim not a
@@ -364,9 +378,14 @@ void attn_launch(const AttnLaunch& l, cudaStream_t stream, bool pdl) {
   a.ws = l.ws;
   a.counters = l.counters;
   a.out = l.out;
+  a.row_pos = l.row_pos;
+  a.row_seq = l.row_seq;
+  a.seq_stride = l.seq_stride;
   int dev = 0;
   MLB_CUDA(cudaGetDevice(&dev));
+  if (l.rows < 1) invalid("attention: no rows");
   if (!attn_tiled_ok(l.H, l.KV, l.D)) {
+    if (l.rows != 1 || l.row_pos) invalid("attention: batched rows need the tiled kernel");
     const int pos = l.pos_host;
     if (l.pos_dev) invalid("attention: the generic path takes a host position");
     const size_t gsm = (size_t)(pos + 1) * sizeof(float);
@@ -390,7 +409,8 @@ void attn_launch(const AttnLaunch& l, cudaStream_t stream, bool pdl) {
                                   (int)smem));
     smem_set[dev] = smem;
   }
-  launch_pdl(attn_decode_kernel, dim3(l.KV, l.nsplit), dim3(kAttnThreads), smem, stream, pdl, a);
+  launch_pdl(attn_decode_kernel, dim3(l.KV, l.nsplit, l.rows), dim3(kAttnThreads), smem, stream,
+             pdl, a);
 }
 
 size_t attn_ws_floats(int H, int KV, int D, int nsplit) {

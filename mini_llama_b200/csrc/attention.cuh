@@ -18,6 +18,14 @@ struct AttnLaunch {
   float* ws = nullptr;            // attn_ws_floats(...)
   int* counters = nullptr;        // KV ints, zero between launches
   float* out = nullptr;           // [H][D]
+  // Batched rows (grid.z): row r of q/out at r * H * D, its own workspace
+  // (attn_ws_floats per row) and KV counters; positions row_pos[r] (device)
+  // and sequence row_seq[r] (device; null: row r) whose layer base is
+  // keys + row_seq[r] * seq_stride.
+  int rows = 1;
+  const int* row_pos = nullptr;
+  const int* row_seq = nullptr;
+  long long seq_stride = 0;
 };
 
 void attn_check(int H, int KV, int D);

@@ -11,6 +11,7 @@
 #include "attention.cuh"
 #include "gemv.cuh"
 #include "ops.cuh"
+#include "qgemm.cuh"
 #include "runtime.cuh"
 #include "synth.h"
 
@@ -92,6 +93,10 @@ struct QMatrixHandle {
   int device = 0;
   GemvWorkspace ws;
   DevBuf wsbuf, cnt, status;
+  // tensor-core GEMM (batches): staged activations and split-tile scratch,
+  // allocated on first use
+  TcWorkspace tcws;
+  DevBuf tc_staged, tc_parts, tc_cnt;
 };
 
 }  // namespace mlb
@@ -378,11 +383,18 @@ int mlb_qmatrix_synthesize(int qtype, int out_features, int in_features, uint64_
   });
 }
 
+static void qmatrix_tc_gemm(mlb_qmatrix& h, const float* x, int rows, float* y, cudaStream_t s);
+
 int mlb_qmatrix_gemv(mlb_qmatrix* m, const float* x, int rows, float* y, void* stream) {
   return guarded([&] {
     if (!m || !x || !y) invalid("mlb_qmatrix_gemv: null pointer");
     if (rows <= 0) invalid("mlb_qmatrix_gemv: rows must be positive");
     set_device(m->device);
+    if (rows > kMaxBatch && m->q.qtype != MLB_F32) {
+      // a batch: one pass of the weights through the tensor cores
+      qmatrix_tc_gemm(*m, x, rows, y, static_cast<cudaStream_t>(stream));
+      return;
+    }
     EpiParams e{};
     e.kind = kEpiStore;
     e.y = y;
@@ -390,6 +402,49 @@ int mlb_qmatrix_gemv(mlb_qmatrix* m, const float* x, int rows, float* y, void* s
     e.n_out = m->q.n;
     gemv_launch(m->q, x, rows, m->q.k, NormSpec{}, e, m->ws, static_cast<cudaStream_t>(stream),
                 false);
+  });
+}
+
+// Scratch of the tensor-core GEMM for up to kTcMaxMp rows per pass.
+static void qmatrix_tc_ws(mlb_qmatrix& h) {
+  if (h.tc_staged.p) return;
+  const int grid = sm_count(h.device);
+  h.tc_staged.alloc((size_t)h.q.nchunks * tc_chunk_bytes(kTcMaxMp));
+  const size_t pf = tc_partial_floats(h.q, kTcMaxMp, grid);
+  h.tc_parts.alloc(pf * 4);
+  const int nc = tc_counter_count(h.q);
+  h.tc_cnt.alloc((size_t)nc * 4);
+  MLB_CUDA(cudaMemset(h.tc_cnt.p, 0, h.tc_cnt.bytes));
+  h.tcws.partials = h.tc_parts.as<float>();
+  h.tcws.partial_floats = pf;
+  h.tcws.counters = h.tc_cnt.as<int>();
+  h.tcws.counter_count = nc;
+  h.tcws.status = h.ws.status;
+}
+
+// y = W x through the tensor-core GEMM, kTcMaxMp rows per pass.
+static void qmatrix_tc_gemm(mlb_qmatrix& h, const float* x, int rows, float* y, cudaStream_t s) {
+  if (h.q.qtype == MLB_F32) invalid("mlb_qmatrix_gemm: quantised types only");
+  qmatrix_tc_ws(h);
+  for (int r0 = 0; r0 < rows; r0 += kTcMaxMp) {
+    const int n = std::min(kTcMaxMp, rows - r0);
+    tc_stage_launch(x + (size_t)r0 * h.q.k, h.q.k, n, h.q.k, h.q.nchunks, nullptr, 0.0f, nullptr,
+                    h.tc_staged.as<uint8_t>(), s);
+    BEpi e{};
+    e.kind = kEpiStore;
+    e.y = y + (size_t)r0 * h.q.n;
+    e.ldy = h.q.n;
+    e.n_out = h.q.n;
+    tc_gemm_launch(h.q, h.tc_staged.as<uint8_t>(), n, e, h.tcws, s);
+  }
+}
+
+int mlb_qmatrix_gemm(mlb_qmatrix* m, const float* x, int rows, float* y, void* stream) {
+  return guarded([&] {
+    if (!m || !x || !y) invalid("mlb_qmatrix_gemm: null pointer");
+    if (rows <= 0) invalid("mlb_qmatrix_gemm: rows must be positive");
+    set_device(m->device);
+    qmatrix_tc_gemm(*m, x, rows, y, static_cast<cudaStream_t>(stream));
   });
 }
 
@@ -571,3 +626,85 @@ int mlb_nccl_unique_id(void* out128) {
 }
 
 }  // extern "C"
+
+// ----------------------------------------------------- batches (batch.cu)
+
+namespace mlb {
+struct BatchImpl;
+BatchImpl* batch_create(ModelImpl& m, int n_seqs, int mode);
+void batch_destroy(BatchImpl* b);
+void batch_reset(BatchImpl& b);
+void batch_fill_kv(BatchImpl& b, int seq, int n_pos, uint64_t seed, float scale);
+void batch_forward(BatchImpl& b, int n, const int* seqs, const int* toks, const int* poss,
+                   float* logits_host, int* next_host);
+void batch_decode_greedy(BatchImpl& b, const int* toks, const int* poss, int steps, int* out_host);
+void context_forward_batch(ContextImpl& c, int n, const int* toks, const int* poss,
+                           float* logits_host);
+int batch_kernels_per_step(const BatchImpl& b);
+cudaStream_t batch_stream(const BatchImpl& b);
+}  // namespace mlb
+
+struct mlb_batch {
+  BatchImpl* impl;
+};
+
+int mlb_forward_batch(mlb_context* c, int n_tokens, const int* tokens, const int* positions,
+                      float* logits_host) {
+  return guarded([&] {
+    if (!c || !tokens || !positions || !logits_host) invalid("ForwardBatch: null pointer");
+    context_forward_batch(*c->impl, n_tokens, tokens, positions, logits_host);
+  });
+}
+
+int mlb_batch_create(mlb_model* m, int n_seqs, int attention_mode, mlb_batch** out) {
+  return guarded([&] {
+    if (!m || !out) invalid("mlb_batch_create: null pointer");
+    BatchImpl* b = batch_create(*m->impl, n_seqs, attention_mode);
+    *out = new mlb_batch{b};
+  });
+}
+
+int mlb_batch_destroy(mlb_batch* b) {
+  return guarded([&] {
+    if (b) {
+      batch_destroy(b->impl);
+      delete b;
+    }
+  });
+}
+
+int mlb_batch_reset(mlb_batch* b) {
+  return guarded([&] {
+    if (!b) invalid("mlb_batch_reset: null batch");
+    batch_reset(*b->impl);
+  });
+}
+
+int mlb_batch_fill_kv(mlb_batch* b, int seq, int n_pos, uint64_t seed, float scale) {
+  return guarded([&] {
+    if (!b) invalid("mlb_batch_fill_kv: null batch");
+    batch_fill_kv(*b->impl, seq, n_pos, seed, scale);
+  });
+}
+
+int mlb_batch_forward(mlb_batch* b, int n_rows, const int* seq_ids, const int* tokens,
+                      const int* positions, float* logits_host, int* next_tokens_host) {
+  return guarded([&] {
+    if (!b || !seq_ids || !tokens || !positions) invalid("mlb_batch_forward: null pointer");
+    batch_forward(*b->impl, n_rows, seq_ids, tokens, positions, logits_host, next_tokens_host);
+  });
+}
+
+int mlb_batch_decode_greedy(mlb_batch* b, const int* tokens, const int* positions, int n_steps,
+                            int* tokens_out) {
+  return guarded([&] {
+    if (!b || !tokens || !positions || !tokens_out) invalid("mlb_batch_decode_greedy: null pointer");
+    batch_decode_greedy(*b->impl, tokens, positions, n_steps, tokens_out);
+  });
+}
+
+void* mlb_batch_stream(mlb_batch* b) { return b ? (void*)batch_stream(*b->impl) : nullptr; }
+
+int mlb_batch_kernels_per_step(const mlb_batch* b) {
+  return b ? batch_kernels_per_step(*b->impl) : 0;
+}

@@ -63,12 +63,6 @@ void qmatrix_geometry(QMatrix& m, int qtype, int n, int k, int max_batch) {
   m.bytes = (size_t)m.nsb * sb_bytes(qtype);
 }
 
-__host__ __device__ inline long long sb_index(int t, int c, int ntiles, int nchunks, int gc) {
-  int grp = c / gc;
-  int cc = c - grp * gc;
-  int geff = min(gc, nchunks - grp * gc);
-  return (long long)grp * ntiles * gc + (long long)t * geff + cc;
-}
 
 // ------------------------------------------------------------------- repack
 

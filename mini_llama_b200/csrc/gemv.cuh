@@ -125,6 +125,18 @@ __device__ __forceinline__ unsigned long long warp_max_u64(unsigned long long v)
 }
 #endif
 
+// Index of the super-block of tile t, chunk c in the (chunk group, tile,
+// chunk) order.
+#if defined(__CUDACC__)
+__host__ __device__
+#endif
+inline long long sb_index(int t, int c, int ntiles, int nchunks, int gc) {
+  const int grp = c / gc;
+  const int cc = c - grp * gc;
+  const int geff = gc < nchunks - grp * gc ? gc : nchunks - grp * gc;
+  return (long long)grp * ntiles * gc + (long long)t * geff + cc;
+}
+
 struct QMatrix {
   int qtype = 0;
   int n = 0, k = 0;          // logical shape [n, k]

@@ -605,12 +605,13 @@ __device__ __forceinline__ void load_b(const uint32_t* fsrc_lane, uint32_t (&B)[
 // += the super-block in shared memory times the staged chunk in B.
 // side_chunk: the chunk's side data (side_per_chunk).
 //
-// The codes enter the MMA with the magic-exponent bias left in: a 4-bit code
-// ORed into the mantissa of 1024.0h is exactly 1024 + q (low nibble) or
-// 1024 + 16 q (high nibble, whose activations were staged divided by 16); an
-// int8 code through prmt is 1024 + 128 + q. One fp32 MMA chain per block then
-// yields sum (q - 8) x (Q4_0) / sum q x (Q4_1, Q8_0) plus bias * sum x, and the
-// staged correction removes the bias term: no per-code subtraction.
+// The codes are decoded through the magic exponent: a 4-bit code ORed into
+// the mantissa of 1024.0h is exactly 1024 + q (low nibble) or 1024 + 16 q
+// (high nibble, whose activations were staged divided by 16); an int8 code
+// through prmt is 1024 + 128 + q. One half2 subtraction per register then
+// leaves the exact small integers q - 8 (Q4_0), q (Q4_1) or the int8 value
+// (Q8_0), so each block's fp32 MMA chain is the block dot itself (its
+// rounding relative to that dot, as in the reference's sequential fp32 sum).
 template <int QT, int M>
 __device__ __forceinline__ void sb_accumulate(const uint8_t* sb, int lane,
                                               const uint32_t (&B)[16][2],
@@ -667,13 +668,26 @@ __device__ __forceinline__ void sb_accumulate(const uint8_t* sb, int lane,
       A2[2] = lop3_and_or(w0s, M2, E);
       A2[3] = lop3_and_or(w1s, M2, E);
     }
+    // remove the magic bias in fp16 (exact: small integers), so the MMA sums
+    // the codes' own products and its fp32 rounding is relative to the block
+    // dot itself rather than to ~1000 times the block sum of x
+    {
+      const __half2 b1 = __float2half2_rn(QT == MLB_Q4_0 ? 1032.0f
+                                                        : (QT == MLB_Q4_1 ? 1024.0f : 1152.0f));
+      const __half2 b2 = __float2half2_rn(QT == MLB_Q4_0 ? 1152.0f
+                                                        : (QT == MLB_Q4_1 ? 1024.0f : 1152.0f));
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        A1[i] = h2_as_u32(__hsub2(u32_as_h2(A1[i]), b1));
+        A2[i] = h2_as_u32(__hsub2(u32_as_h2(A2[i]), b2));
+      }
+    }
     float d[4];
     mma_16816_z(d, A1, B[2 * b][0], B[2 * b][1]);
     mma_16816(d, A2, B[2 * b + 1][0], B[2 * b + 1][1]);
-    const float corr = side_chunk[b * M + rr];
     const float2 sc = __half22float2(u32_as_h2(scw[b]));
-    acc0 = fmaf(sc.x, (d[0] + d[1]) - corr, acc0);
-    acc1 = fmaf(sc.y, (d[2] + d[3]) - corr, acc1);
+    acc0 = fmaf(sc.x, d[0] + d[1], acc0);
+    acc1 = fmaf(sc.y, d[2] + d[3], acc1);
     if (QT == MLB_Q4_1) {
       const float2 mn = __half22float2(u32_as_h2(mnw[b]));
       const float sx = side_chunk[8 * M + b * M + rr];

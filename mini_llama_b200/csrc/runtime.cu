@@ -474,6 +474,7 @@ ContextImpl::~ContextImpl() {
   if (stream) cudaStreamSynchronize(stream);
   for (void* p : tp_opened) cudaIpcCloseMemHandle(p);
   release_graphs();
+  if (batch) batch_engine_free(batch);
   if (h_scalars) cudaFreeHost(h_scalars);
   if (h_logits) cudaFreeHost(h_logits);
   if (h_tokens) cudaFreeHost(h_tokens);
@@ -1128,16 +1129,21 @@ __global__ void fill_kv_kernel(float* keys, float* values, int L, int S, int KVl
   }
 }
 
+void fill_kv_rows(float* keys, float* values, const ModelImpl& m, int n_pos, uint64_t seed,
+                  float scale, cudaStream_t s) {
+  const mlb_config& cf = m.cfg;
+  if (n_pos <= 0) return;
+  fill_kv_kernel<<<sm_count(m.device) * 8, 256, 0, s>>>(keys, values, cf.n_layers,
+                                                       cf.max_seq_len, m.kv_heads, cf.n_kv_heads,
+                                                       m.kv_head0, cf.head_dim, n_pos, seed, scale);
+  MLB_CUDA(cudaGetLastError());
+}
+
 void context_fill_kv(ContextImpl& c, int n_pos, uint64_t seed, float scale) {
   const mlb_config& cf = c.m->cfg;
   if (n_pos < 0 || n_pos > cf.max_seq_len) out_of_range("mlb_context_fill_kv: n_pos out of range");
   set_device(c.m->device);
-  if (n_pos > 0) {
-    fill_kv_kernel<<<sm_count(c.m->device) * 8, 256, 0, c.stream>>>(
-        c.keys.as<float>(), c.values.as<float>(), cf.n_layers, cf.max_seq_len, c.m->kv_heads,
-        cf.n_kv_heads, c.m->kv_head0, cf.head_dim, n_pos, seed, scale);
-    MLB_CUDA(cudaGetLastError());
-  }
+  fill_kv_rows(c.keys.as<float>(), c.values.as<float>(), *c.m, n_pos, seed, scale, c.stream);
   MLB_CUDA(cudaStreamSynchronize(c.stream));
 }
 

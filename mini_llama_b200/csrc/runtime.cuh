@@ -69,7 +69,13 @@ struct ModelImpl {
   size_t step_weight_bytes() const;
 };
 
+struct BatchEngine;  // batch.cu: scratch of one batched pass
+void batch_engine_free(BatchEngine* e);
+
 struct ContextImpl {
+  // ForwardBatch on this context (prompt prefill through the tensor-core
+  // GEMM), created on first use
+  BatchEngine* batch = nullptr;
   ModelImpl* m = nullptr;
   int attention_mode = MLB_ATTN_CPU_COMPAT;
   cudaStream_t stream = nullptr;

@@ -296,6 +296,12 @@ class RefModel:
                 raise RuntimeError(self.ref.lib.ref_last_error().decode())
         return self.ctx
 
+    def new_context(self):
+        """Drops the current MiniLlamaContext; the next call makes a fresh one."""
+        if self.ctx:
+            self.ref.lib.ref_ctx_destroy(self.ctx)
+        self.ctx = None
+
     def fill_kv(self, n_pos, seed, scale=1.25):
         """Seeded K/V rows for positions [0, n_pos) of every layer, written with
         KvCache::Write (the values mlb_context_fill_kv writes on the GPU)."""

@@ -30,6 +30,20 @@ def pattern(shape, scale, shift, mult=19, add=7, mod=31):
     return ((((i * mult + add) % mod) - (mod // 2)) * scale + shift).astype(np.float32).reshape(shape)
 
 
+def cpu_linear(port, qtype, x, blocks, n):
+    """The reference CPU linear (oracle/_ref, all host threads) where built,
+    else the C restatement (bit-identical, one thread)."""
+    import os
+
+    import oracle
+
+    if oracle.ref_available():
+        r = oracle.ref()
+        r.set_threads(len(os.sched_getaffinity(0)))
+        return r.linear(qtype, x, blocks, n)
+    return port.linear(qtype, x, blocks, n)
+
+
 def quantize(port, qtype, w):
     return port.quantize(qtype, w) if qtype != C.F32 else np.ascontiguousarray(w)
 
@@ -89,6 +103,31 @@ def test_qmatrix_gemv_vs_oracle(cuda, port, qtype, shape):
         # deterministic: a second run is bit-identical
         again = qm.gemv(torch.from_numpy(x).cuda()).cpu().numpy()
         np.testing.assert_array_equal(got, again)
+
+
+@pytest.mark.parametrize("qtype", [C.Q4_0, C.Q4_1, C.Q8_0])
+@pytest.mark.parametrize("shape", [(4096, 4096), (11008, 4096), (1024, 4096), (515, 160),
+                                   (300, 29568 // 8 + 32), (2048, 14336)])
+def test_tensor_core_gemm_vs_oracle(cuda, port, qtype, shape):
+    """The tcgen05 GEMM (batches: dequantised fp16 hi + lo weights in TMEM,
+    fp16 hi + lo activations) against the reference CPU linear
+    (LinearQ80/Q40/Q41, src/quant.cc:365-471) for batch widths 1..64 and a
+    ragged 70-row batch (two passes), within the linear tolerance; reruns are
+    bit-identical (split tiles are summed in chunk order)."""
+    torch = cuda
+    n, k = shape
+    blocks = C.synth_tensor(5, C.W_WQ, n % 97, qtype, n, k)
+    qm = mlb.QMatrix.from_gguf(qtype, blocks, n, k)
+    rng = np.random.default_rng(n + 7 * k)
+    for rows in (1, 5, 16, 17, 32, 48, 64, 70):
+        x = rng.normal(0, 1, (rows, k)).astype(np.float32)
+        want = cpu_linear(port, qtype, x, blocks, n).reshape(rows, n)
+        xd = torch.from_numpy(x).cuda()
+        got = qm.gemm(xd).cpu().numpy()
+        close(got, want, 1e-3)
+        np.testing.assert_array_equal(got, qm.gemm(xd).cpu().numpy())
+        if rows > 4:  # the auto-routed entry point takes the same path
+            np.testing.assert_array_equal(got, qm.gemv(xd).cpu().numpy())
 
 
 def random_blocks(qtype, n, k, seed):
