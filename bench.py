@@ -60,8 +60,11 @@ def parse_args():
     p.add_argument("--impl", choices=["b200", "reference"], default="b200")
     p.add_argument("--workload", choices=sorted(C.WORKLOADS) + ["gemv-sweep"],
                    default="llama2-7b-q4_0")
-    p.add_argument("--also", type=str, default="qwen2-72b-q4_1",
-                   help="second workload timed in the same run (comma list; 'none' for none)")
+    p.add_argument("--also", type=str, default="llama3-8b-q8_0@32,qwen2-72b-q4_1@32",
+                   help="more workloads timed in the same run: NAME or NAME@BATCH, comma "
+                        "separated ('none' for none)")
+    p.add_argument("--batch-ctx", type=int, default=4096,
+                   help="K/V depth of every sequence of the batched workloads")
     p.add_argument("--sweep-n", type=str, default="4096,11008,14336")
     p.add_argument("--sweep-m", type=str, default="1,4,16,64")
     p.add_argument("--sweep-q", type=str, default="q4_0,q4_1,q8_0")
@@ -107,7 +110,7 @@ class Clocks:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
-                 "-i", ",".join(str(g) for g in self.gpus), "-lms", "200"],
+                 "-i", ",".join(str(g) for g in self.gpus), "-lms", "50"],
                 stdout=self.f, stderr=subprocess.DEVNULL)
         except Exception:
             self.proc = None
@@ -413,7 +416,7 @@ def measure_workload(torch, mlb, dist, args, name, cfg, qtype, bias, rank, world
         h1 = time.time()
         barrier()
     ms = max_over_ranks(ev0.elapsed_time(ev1))
-    clocks = clk.summary([(h0, h1)])
+    clocks = clk.summary([(h0 - 0.1, h1 + 0.1)])
     pos += steps
     ctx_end = pos
     tok = ids[-1]
@@ -482,6 +485,91 @@ def measure_workload(torch, mlb, dist, args, name, cfg, qtype, bias, rank, world
     }
 
 
+def measure_batch(torch, mlb, dist, args, name, cfg, qtype, bias, B, ctx0, rank, world, local,
+                  steps, warmup, peak):
+    """B sequences decoded in lockstep (mlb_batch_decode_greedy: the tcgen05
+    GEMM for every projection, batched attention), each from its own seeded
+    K/V state at depth ctx0. Time: CUDA events on the batch stream around the
+    timed steps, max over ranks; tokens/s counts B tokens per step. Rank 0
+    checks the greedy ids of the first and last sequence against one GPU's
+    single-sequence step kernel from the same state."""
+    barrier = lambda: (torch.cuda.synchronize(), dist.barrier() if dist else None)  # noqa: E731
+
+    def max_over_ranks(v):
+        if not dist:
+            return v
+        t = torch.tensor([v], dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    cfg = dict(cfg, max_seq_len=min(cfg["max_seq_len"], ctx0 + warmup + steps + 64))
+    nccl_id = None
+    if world > 1:
+        obj = [mlb.nccl_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        nccl_id = obj[0]
+    model = mlb.CudaModel(cfg, device_id=local, tp_rank=rank, tp_size=world, nccl_id=nccl_id)
+    model.synthesize(qtype, SEED, with_bias=bias)
+    _, step_weights = model.bytes()
+    b = mlb.Batch(model, B)
+    for s in range(B):
+        b.fill_kv(s, ctx0, KV_SEED + s, KV_SCALE)
+    toks = C.prompt_ids(SEED + 7, B, cfg["vocab_size"])
+    ids_w = b.decode_greedy(toks, [ctx0] * B, warmup)
+    stream = torch.cuda.ExternalStream(b.stream())
+    barrier()
+    with Clocks([local]) as clk:
+        barrier()
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        h0 = time.time()
+        ev0.record(stream)
+        ids_t = b.decode_greedy(ids_w[-1], [ctx0 + warmup] * B, steps)
+        ev1.record(stream)
+        torch.cuda.synchronize()
+        h1 = time.time()
+        barrier()
+    ms = max_over_ranks(ev0.elapsed_time(ev1))
+    clocks = clk.summary([(h0 - 0.1, h1 + 0.1)])
+    kps = b.kernels_per_step()
+    ids = np.concatenate([ids_w, ids_t])
+    b.close()
+    model.close()
+    check = None
+    if rank == 0:
+        n = min(N_CHECK, len(ids))
+        one = (mlb.CudaModel(cfg, device_id=local).synthesize(qtype, SEED, with_bias=bias))
+        c1 = one.context(mlb.ATTN_CPU_COMPAT)
+        ok = True
+        for s in (0, B - 1):
+            c1.reset()
+            c1.fill_kv(ctx0, KV_SEED + s, KV_SCALE)
+            ok = ok and c1.decode_greedy(toks[s], ctx0, n) == [int(v) for v in ids[:n, s]]
+        c1.close()
+        one.close()
+        check = {"seq_ids_match": ok, "sequences": [0, B - 1], "n": n,
+                 "against": "one GPU's single-sequence step kernel from the same seeded state"}
+    barrier()
+    kv_per_pos = 2 * cfg["n_layers"] * (cfg["n_kv_heads"] // world) * cfg["head_dim"] * 4
+    mid_ctx = ctx0 + warmup + steps / 2
+    step_bytes = step_weights + B * kv_per_pos * mid_ctx
+    step_s = ms / 1e3 / steps
+    return {
+        "name": name, "value": B * steps / (ms / 1e3), "unit": "tok/s",
+        "ms_per_step": ms / steps, "steps": steps, "warmup": warmup, "batch": B, "ctx": ctx0,
+        "parallelism": f"tp{world}" if world > 1 else "single gpu",
+        "roofline": {"bound": "hbm", "achieved": step_bytes / step_s / 1e9, "peak": peak[0],
+                     "unit": "GB/s", "frac": step_bytes / step_s / 1e9 / peak[0],
+                     "bytes_per_step": step_bytes, "weight_bytes": step_weights,
+                     "kv_bytes": B * kv_per_pos * mid_ctx,
+                     "note": "algorithmic bytes: GGUF weights of this rank once per step + every "
+                             "sequence's fp32 K and V at the mean timed context",
+                     "peak_source": peak[1] + " (MEASURED_PEAKS.json hbm_gbs, burst)"},
+        "clocks": clocks, "parity": check, "greedy_ids_seq0": [int(v) for v in ids[:N_CHECK, 0]],
+        "kernels_per_step": kps, "gpu_launches": kps * steps,
+        "data": "seeded weights; each sequence's K/V rows seeded to depth ctx; seeded tokens",
+    }
+
+
 def run_gpu(args, cfg, qtype, bias, rank, world, local):
     import torch
 
@@ -499,16 +587,26 @@ def run_gpu(args, cfg, qtype, bias, rank, world, local):
     head = measure_workload(torch, mlb, dist, args, args.workload, cfg, qtype, bias, rank, world,
                             local, args.steps, args.warmup, peak, check_single=True)
     extras = []
-    for name in [] if args.also in ("", "none") or args.layers else args.also.split(","):
-        if name == args.workload:
+    for spec in [] if args.also in ("", "none") or args.layers else args.also.split(","):
+        name, _, bsz = spec.partition("@")
+        B = int(bsz) if bsz else 1
+        if name == args.workload and B == 1:
             continue
         ecfg, eq, eb = C.WORKLOADS[name]
         try:
-            extras.append(measure_workload(torch, mlb, dist, args, name, ecfg, eq, eb, rank,
-                                           world, local, min(args.steps, 24),
-                                           max(3, min(args.warmup, 4)), peak, check_single=True))
+            if B > 1:
+                r = measure_batch(torch, mlb, dist, args, name, ecfg, eq, eb, B, args.batch_ctx,
+                                  rank, world, local, min(args.steps, 16),
+                                  max(3, min(args.warmup, 4)), peak)
+                r["name"] = f"{name}_b{B}"
+                extras.append(r)
+            else:
+                extras.append(measure_workload(torch, mlb, dist, args, name, ecfg, eq, eb, rank,
+                                               world, local, min(args.steps, 24),
+                                               max(3, min(args.warmup, 4)), peak,
+                                               check_single=True))
         except Exception as e:  # reported, not fatal
-            extras.append({"name": name, "error": str(e)[:300]})
+            extras.append({"name": spec, "error": str(e)[:300]})
 
     gemv_roof = sweep = sweep_cpu = None
     cpu = None
@@ -579,6 +677,9 @@ def run_gpu(args, cfg, qtype, bias, rank, world, local):
             key = e["name"].replace("-", "_")
             if "error" in e:
                 line[key] = {"error": e["error"]}
+                continue
+            if "batch" in e:
+                line[key] = e
                 continue
             line[key] = {"value": e["value"], "unit": "tok/s", "ms_per_step": e["ms_per_step"],
                          "steps": e["steps"], "warmup": e["warmup"], "batch": 1,

@@ -213,7 +213,8 @@ int mlb_qmatrix_gemv(mlb_qmatrix* m, const float* x_dev, int rows, float* y_dev,
  * tensor memory, activations as fp16 hi + lo, fp32 accumulation. Replaces the
  * per-row loop a batch takes through LinearQ80/Q40/Q41 (src/quant.cc:365-471;
  * ForwardBatch, src/batch.cc:35-50, runs one token at a time). Quantised types
- * only. The first call on a matrix allocates its scratch. */
+ * only. Its scratch is allocated with the matrix, so calls can be captured in a
+ * CUDA graph. */
 int mlb_qmatrix_gemm(mlb_qmatrix* m, const float* x_dev, int rows, float* y_dev,
                      void* stream);
 /* The prepared weight dequantised back to fp32, out_dev[out_features *

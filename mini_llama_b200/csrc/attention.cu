@@ -275,6 +275,225 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnKAr
   if (threadIdx.x == 0) cnt[kvh] = 0;
 }
 
+// ------------------------------------------------------------ batched rows
+
+constexpr int kRowsWarps = 8;
+constexpr int kRowsThreads = kRowsWarps * 32;
+
+// Sums NV values across the warp: afterwards v[0] of lane L holds the total of
+// value index L / (32 / NV) (NV a power of two <= 32); each round keeps half
+// of the remaining values and adds the partner lane's copy of that half.
+template <int NV>
+__device__ __forceinline__ void rows_multi_sum(float (&v)[NV], int lane) {
+#pragma unroll
+  for (int r = 0; r < 5; ++r) {
+    const int off = 16 >> r;
+    const int cnt = NV >> r;
+    if (cnt > 1) {
+      const int half = cnt >> 1;
+      const bool upper = (lane & off) != 0;
+#pragma unroll
+      for (int i = 0; i < half; ++i) {
+        const float send = upper ? v[i] : v[i + half];
+        const float keep = upper ? v[i + half] : v[i];
+        v[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+      }
+    } else {
+      v[0] += __shfl_xor_sync(0xffffffffu, v[0], off);
+    }
+  }
+}
+
+// Decode attention for batched rows: CTA (KV head, split, row) with 8 warps.
+// Each warp streams blocks of PB positions of the split round robin, every
+// lane holding 4 of the head_dim values of the K and V rows and of each
+// query head of the GQA group (G heads, registers), and keeps an online
+// softmax (m, l, o) per query head; the next block's rows are loaded before
+// the current one is computed. The CTA then combines its 8 warps in warp
+// order and, as in the tiled kernel, the last split of a head combines the
+// splits in split order. head_dim is a multiple of 4 and at most 128.
+template <int G, int PB>
+__global__ void __launch_bounds__(kRowsThreads, 2) attn_rows_kernel(const AttnKArgs a) {
+  constexpr int NV = G * PB;
+  static_assert(NV <= 32, "GQA group too large for one pass");
+  constexpr unsigned kNvMask = NV >= 32 ? 0xffffffffu : ((1u << NV) - 1u);
+  __shared__ float scw[kRowsWarps][NV];
+  __shared__ float alw[kRowsWarps][G];
+  __shared__ float wm[kRowsWarps][G], wl[kRowsWarps][G];
+  __shared__ __align__(16) float wo[kRowsWarps][G][128];
+  __shared__ float cw[G][kRowsWarps];
+  __shared__ int last_flag;
+  const int D = a.D, KV = a.KV;
+  const int kvh = blockIdx.x, split = blockIdx.y, row = blockIdx.z;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  pdl_launch_dependents();  // dependents still wait for this grid to complete
+  pdl_wait();
+  const int seq = a.row_seq ? a.row_seq[row] : row;
+  const float* keys = a.keys + (size_t)seq * a.seq_stride;
+  const float* values = a.values + (size_t)seq * a.seq_stride;
+  const float* qrow = a.q + (size_t)row * a.H * D;
+  float* outrow = a.out + (size_t)row * a.H * D;
+  float* wsrow = a.ws + (size_t)row * KV * a.nsplit * G * (D + 2);
+  int* cnt = a.counters + (size_t)row * KV;
+  const int pos = a.row_pos ? a.row_pos[row] : (a.pos_dev ? *a.pos_dev : a.pos_host);
+  const int n = pos + 1;
+  const int v_end = a.include_current_v ? n : pos;
+  // this split's positions, in whole warp blocks
+  const int blocks = (n + PB - 1) / PB;
+  const int per = (blocks + a.nsplit - 1) / a.nsplit;
+  const int t_begin = min(n, split * per * PB), t_end = min(n, (split + 1) * per * PB);
+  const bool dl = lane < (D >> 2);
+  const size_t rstride = (size_t)KV * D;
+  const float* kb = keys + (size_t)kvh * D + 4 * lane;
+  const float* vb = values + (size_t)kvh * D + 4 * lane;
+  float4 q[G], o[G];
+#pragma unroll
+  for (int h = 0; h < G; ++h) {
+    q[h] = dl ? __ldg(reinterpret_cast<const float4*>(qrow + (size_t)(kvh * G + h) * D) + lane)
+              : make_float4(0.f, 0.f, 0.f, 0.f);
+    o[h] = make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  float m_run = -INFINITY, l_run = 0.0f;  // lane i < NV: head i / PB
+  auto load_block = [&](int tb, float4 (&kx)[PB], float4 (&vx)[PB]) {
+#pragma unroll
+    for (int j = 0; j < PB; ++j) {
+      const int t = tb + j;
+      kx[j] = (dl && t < t_end) ? __ldcs(reinterpret_cast<const float4*>(kb + (size_t)t * rstride))
+                                : make_float4(0.f, 0.f, 0.f, 0.f);
+      vx[j] = (dl && t < t_end && t < v_end)
+                  ? __ldcs(reinterpret_cast<const float4*>(vb + (size_t)t * rstride))
+                  : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+  };
+  float4 kn[PB], vn[PB];
+  const int tb0 = t_begin + warp * PB;
+  if (tb0 < t_end) load_block(tb0, kn, vn);
+  for (int tb = tb0; tb < t_end; tb += kRowsWarps * PB) {
+    float4 kx[PB], vx[PB];
+#pragma unroll
+    for (int j = 0; j < PB; ++j) {
+      kx[j] = kn[j];
+      vx[j] = vn[j];
+    }
+    if (tb + kRowsWarps * PB < t_end) load_block(tb + kRowsWarps * PB, kn, vn);
+    float dv[NV];
+#pragma unroll
+    for (int h = 0; h < G; ++h)
+#pragma unroll
+      for (int j = 0; j < PB; ++j) {
+        float d = q[h].x * kx[j].x;
+        d = fmaf(q[h].y, kx[j].y, d);
+        d = fmaf(q[h].z, kx[j].z, d);
+        d = fmaf(q[h].w, kx[j].w, d);
+        dv[h * PB + j] = d;
+      }
+    rows_multi_sum<NV>(dv, lane);
+    if ((lane & (32 / NV - 1)) == 0) scw[warp][lane / (32 / NV)] = dv[0];
+    __syncwarp();
+    if (lane < NV) {
+      const int j = lane % PB;
+      const int t = tb + j;
+      const float sc = t < t_end ? __fmul_rn(scw[warp][lane], a.scale) : -INFINITY;
+      float bmax = sc;
+#pragma unroll
+      for (int off = 1; off < PB; off <<= 1) bmax = fmaxf(bmax, __shfl_xor_sync(kNvMask, bmax, off));
+      const float mnew = fmaxf(m_run, bmax);
+      const float p = t < t_end ? expf(sc - mnew) : 0.0f;
+      float psum = p;
+#pragma unroll
+      for (int off = 1; off < PB; off <<= 1) psum += __shfl_xor_sync(kNvMask, psum, off);
+      const float al = m_run == -INFINITY ? 0.0f : expf(m_run - mnew);
+      l_run = fmaf(l_run, al, psum);
+      m_run = mnew;
+      scw[warp][lane] = t < v_end ? p : 0.0f;  // counted in the softmax, V row summed below v_end
+      if (j == 0) alw[warp][lane / PB] = al;
+    }
+    __syncwarp();
+#pragma unroll
+    for (int h = 0; h < G; ++h) {
+      const float al = alw[warp][h];
+      float4 acc = make_float4(o[h].x * al, o[h].y * al, o[h].z * al, o[h].w * al);
+#pragma unroll
+      for (int j = 0; j < PB; ++j) {
+        const float p = scw[warp][h * PB + j];
+        acc.x = fmaf(p, vx[j].x, acc.x);
+        acc.y = fmaf(p, vx[j].y, acc.y);
+        acc.z = fmaf(p, vx[j].z, acc.z);
+        acc.w = fmaf(p, vx[j].w, acc.w);
+      }
+      o[h] = acc;
+    }
+    __syncwarp();
+  }
+  // this warp's (m, l, o) per query head
+  if (lane < NV && lane % PB == 0) {
+    wm[warp][lane / PB] = m_run;
+    wl[warp][lane / PB] = l_run;
+  }
+  if (dl) {
+#pragma unroll
+    for (int h = 0; h < G; ++h) *reinterpret_cast<float4*>(&wo[warp][h][4 * lane]) = o[h];
+  }
+  __syncthreads();
+  // the CTA's record: warps combined in warp order
+  if (threadIdx.x < G) {
+    const int h = threadIdx.x;
+    float m = -INFINITY;
+    for (int w = 0; w < kRowsWarps; ++w) m = fmaxf(m, wm[w][h]);
+    float l = 0.0f;
+    for (int w = 0; w < kRowsWarps; ++w) {
+      const float e = wm[w][h] == -INFINITY ? 0.0f : expf(wm[w][h] - m);
+      cw[h][w] = e;
+      l = fmaf(wl[w][h], e, l);
+    }
+    float* r = wsrow + (((size_t)kvh * a.nsplit + split) * G + h) * (D + 2);
+    r[0] = m;
+    r[1] = l;
+  }
+  __syncthreads();
+  const int rec = D + 2;
+  for (int i = threadIdx.x; i < G * D; i += kRowsThreads) {
+    const int h = i / D, d = i - h * D;
+    float acc = 0.0f;
+    for (int w = 0; w < kRowsWarps; ++w) acc = fmaf(wo[w][h][d], cw[h][w], acc);
+    wsrow[(((size_t)kvh * a.nsplit + split) * G + h) * rec + 2 + d] = acc;
+  }
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) last_flag = atomicAdd(&cnt[kvh], 1) == a.nsplit - 1;
+  __syncthreads();
+  if (!last_flag) return;
+  __threadfence();
+  // the last split of the head combines the splits in split order
+  float* wsl = &wo[0][0][0];  // [G][nsplit] weights (nsplit <= 8 * 128 / G)
+  if (threadIdx.x < G) {
+    const int h = threadIdx.x;
+    float m = -INFINITY;
+    for (int s = 0; s < a.nsplit; ++s)
+      m = fmaxf(m, __ldcg(wsrow + (((size_t)kvh * a.nsplit + s) * G + h) * rec));
+    float l = 0.0f;
+    for (int s = 0; s < a.nsplit; ++s) {
+      const float* r = wsrow + (((size_t)kvh * a.nsplit + s) * G + h) * rec;
+      const float ms = __ldcg(r);
+      const float e = ms == -INFINITY ? 0.0f : expf(ms - m);
+      wsl[h * a.nsplit + s] = e;
+      l = fmaf(__ldcg(r + 1), e, l);
+    }
+    const float inv = 1.0f / l;
+    for (int s = 0; s < a.nsplit; ++s) wsl[h * a.nsplit + s] *= inv;
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < G * D; i += kRowsThreads) {
+    const int h = i / D, d = i - h * D;
+    float acc = 0.0f;
+    for (int s = 0; s < a.nsplit; ++s)
+      acc = fmaf(__ldcg(wsrow + (((size_t)kvh * a.nsplit + s) * G + h) * rec + 2 + d),
+                 wsl[h * a.nsplit + s], acc);
+    outrow[(size_t)(kvh * G + h) * D + d] = acc;
+  }
+  if (threadIdx.x == 0) cnt[kvh] = 0;
+}
+
 // Generic path for shapes the tiled kernel does not take (head_dim not a
 // multiple of 4, or more than 16 query heads per KV head): one CTA per query
 // head, scores in shared memory, one pass per output element.
@@ -396,9 +615,23 @@ void attn_launch(const AttnLaunch& l, cudaStream_t stream, bool pdl) {
     launch_pdl(attn_decode_generic_kernel, dim3(l.H), dim3(kAttnThreads), gsm, stream, pdl, a);
     return;
   }
+  const int G = l.H / l.KV;
+  if (l.row_pos && l.D % 4 == 0 && l.D <= 128 && (G == 1 || G == 2 || G == 4 || G == 8)) {
+    // batched rows: the register-streaming kernel (its combine keeps G x
+    // nsplit split weights in 8 x G x 128 floats)
+    a.nsplit = std::max(1, std::min(l.nsplit, kRowsWarps * 128));
+    const dim3 grid(l.KV, a.nsplit, l.rows);
+    switch (G) {
+      case 1: launch_pdl(attn_rows_kernel<1, 4>, grid, dim3(kRowsThreads), 0, stream, pdl, a); break;
+      case 2: launch_pdl(attn_rows_kernel<2, 4>, grid, dim3(kRowsThreads), 0, stream, pdl, a); break;
+      case 4: launch_pdl(attn_rows_kernel<4, 4>, grid, dim3(kRowsThreads), 0, stream, pdl, a); break;
+      default: launch_pdl(attn_rows_kernel<8, 2>, grid, dim3(kRowsThreads), 0, stream, pdl, a); break;
+    }
+    return;
+  }
   {
     // the combine keeps G x nsplit slice weights in the K/V tile region
-    const int G = l.H / l.KV, pitch = l.D + 4, hstep = kAttnThreads / (l.D / 4);
+    const int pitch = l.D + 4, hstep = kAttnThreads / (l.D / 4);
     const int region = std::max(4 * kAttnTile * pitch, hstep * G * l.D);
     a.nsplit = std::max(1, std::min(l.nsplit, region / G));
   }
@@ -409,7 +642,7 @@ void attn_launch(const AttnLaunch& l, cudaStream_t stream, bool pdl) {
                                   (int)smem));
     smem_set[dev] = smem;
   }
-  launch_pdl(attn_decode_kernel, dim3(l.KV, l.nsplit, l.rows), dim3(kAttnThreads), smem, stream,
+  launch_pdl(attn_decode_kernel, dim3(l.KV, a.nsplit, l.rows), dim3(kAttnThreads), smem, stream,
              pdl, a);
 }
 

@@ -133,9 +133,10 @@ struct BatchEngine {
     tcws.counter_count = cnt;
     tcws.status = status.as<DeviceStatus>();
     attn_check_tiled(m->q_heads, m->kv_heads, D);
-    // enough (KV head, split, row) CTAs for two waves, whole 32-position tiles
-    attn_nsplit = std::max(1, std::min((2 * grid + rows * m->kv_heads - 1) / (rows * m->kv_heads),
-                                       (c.max_seq_len + 31) / 32));
+    // (KV head, split, row) CTAs for about four waves of two per SM at the
+    // longest context, at least 64 positions per split
+    attn_nsplit = std::max(1, std::min((8 * grid + rows * m->kv_heads - 1) / (rows * m->kv_heads),
+                                       (c.max_seq_len + 63) / 64));
     attn_ws.alloc(attn_ws_floats(m->q_heads, m->kv_heads, D, attn_nsplit) * rows * 4);
     attn_cnt.alloc((size_t)rows * m->kv_heads * 4);
     MLB_CUDA(cudaMemset(attn_cnt.p, 0, attn_cnt.bytes));
@@ -158,11 +159,11 @@ struct BatchEngine {
     int launches = 0;
     auto stage = [&](const float* src, int ld, int k, int chunks, const float* norm) {
       tc_stage_launch(src, ld, rows, k, chunks, norm, c.rms_norm_eps, nullptr,
-                      staged.as<uint8_t>(), s);
+                      staged.as<uint8_t>(), s, true);
       ++launches;
     };
     auto gemm = [&](const QMatrix& w, const BEpi& e) {
-      tc_gemm_launch(w, staged.as<uint8_t>(), rows, e, tcws, s);
+      tc_gemm_launch(w, staged.as<uint8_t>(), rows, e, tcws, s, 0, true);
       ++launches;
     };
     gather_rows_kernel<<<dim3((c.dim + 255) / 256, rows), 256, 0, s>>>(
@@ -207,7 +208,7 @@ struct BatchEngine {
       al.row_pos = pos();
       al.row_seq = seq();
       al.seq_stride = seq_stride;
-      attn_launch(al, s, false);
+      attn_launch(al, s, true);
       ++launches;
 
       const int qd = m->q_heads * D;
@@ -289,6 +290,8 @@ struct BatchEngine {
     }
   }
 };
+
+constexpr int kDecodeChunk = 1024;  // decode steps per token record
 
 struct BatchImpl {
   ModelImpl* m = nullptr;
@@ -457,19 +460,13 @@ void batch_decode_greedy(BatchImpl& b, const int* toks, const int* poss, int ste
   }
   MLB_CUDA(cudaMemcpyAsync(e.rows_dev.p, b.h_rows, (size_t)3 * R * 4, cudaMemcpyHostToDevice,
                            b.stream));
-  if ((size_t)steps * n > b.h_out_cap) {
-    if (b.h_out) cudaFreeHost(b.h_out);
-    b.h_out = nullptr;
-    MLB_CUDA(cudaStreamSynchronize(b.stream));
-    if (b.exec) {
-      cudaGraphExecDestroy(b.exec);
-      b.exec = nullptr;
-    }
-    b.h_out_cap = (size_t)steps * n;
+  if (!b.h_out) {
+    // a fixed token record of kDecodeChunk steps: the graph captures its
+    // address once, longer decodes run in chunks of it
+    b.h_out_cap = (size_t)kDecodeChunk * n;
     MLB_CUDA(cudaMallocHost(&b.h_out, b.h_out_cap * 4));
     b.out_dev.alloc(b.h_out_cap * 4);
   }
-  MLB_CUDA(cudaMemsetAsync(e.step_dev.p, 0, 4, b.stream));
   if (!b.exec) {
     cudaGraph_t g = nullptr;
     MLB_CUDA(cudaStreamBeginCapture(b.stream, cudaStreamCaptureModeThreadLocal));
@@ -490,12 +487,16 @@ void batch_decode_greedy(BatchImpl& b, const int* toks, const int* poss, int ste
     MLB_CUDA(err);
     b.kernels_per_step = k + 1;
   }
-  for (int i = 0; i < steps; ++i) MLB_CUDA(cudaGraphLaunch(b.exec, b.stream));
-  MLB_CUDA(cudaMemcpyAsync(b.h_out, b.out_dev.p, (size_t)steps * n * 4, cudaMemcpyDeviceToHost,
-                           b.stream));
-  MLB_CUDA(cudaStreamSynchronize(b.stream));
-  e.check_status();
-  std::memcpy(out_host, b.h_out, (size_t)steps * n * 4);
+  for (int s0 = 0; s0 < steps; s0 += kDecodeChunk) {
+    const int k = std::min(kDecodeChunk, steps - s0);
+    MLB_CUDA(cudaMemsetAsync(e.step_dev.p, 0, 4, b.stream));
+    for (int i = 0; i < k; ++i) MLB_CUDA(cudaGraphLaunch(b.exec, b.stream));
+    MLB_CUDA(cudaMemcpyAsync(b.h_out, b.out_dev.p, (size_t)k * n * 4, cudaMemcpyDeviceToHost,
+                             b.stream));
+    MLB_CUDA(cudaStreamSynchronize(b.stream));
+    e.check_status();
+    std::memcpy(out_host + (size_t)s0 * n, b.h_out, (size_t)k * n * 4);
+  }
 }
 
 // ForwardBatch on a single context: its tokens at their positions in passes

@@ -325,6 +325,8 @@ int mlb_attention_decode(const float* q, const float* keys, const float* values,
 
 // ---------------------------------------------------------- prepared weights
 
+static void qmatrix_tc_ws(mlb_qmatrix& h);
+
 static void qmatrix_ws(mlb_qmatrix& h) {
   size_t pf = (size_t)h.q.ntiles * std::max(h.q.nchunks, 1) * 16 * kMaxBatch;
   h.wsbuf.alloc(pf * 4);
@@ -337,6 +339,9 @@ static void qmatrix_ws(mlb_qmatrix& h) {
   h.ws.counters = h.cnt.as<int>();
   h.ws.counter_count = h.q.ntiles;
   h.ws.status = h.status.as<DeviceStatus>();
+  // the tensor-core GEMM's scratch too, so that no call allocates (calls may
+  // be captured in a CUDA graph)
+  if (h.q.qtype != MLB_F32) qmatrix_tc_ws(h);
 }
 
 int mlb_qmatrix_create(int qtype, const void* w, int w_is_host, int out_features, int in_features,
@@ -429,13 +434,13 @@ static void qmatrix_tc_gemm(mlb_qmatrix& h, const float* x, int rows, float* y, 
   for (int r0 = 0; r0 < rows; r0 += kTcMaxMp) {
     const int n = std::min(kTcMaxMp, rows - r0);
     tc_stage_launch(x + (size_t)r0 * h.q.k, h.q.k, n, h.q.k, h.q.nchunks, nullptr, 0.0f, nullptr,
-                    h.tc_staged.as<uint8_t>(), s);
+                    h.tc_staged.as<uint8_t>(), s, r0 > 0);
     BEpi e{};
     e.kind = kEpiStore;
     e.y = y + (size_t)r0 * h.q.n;
     e.ldy = h.q.n;
     e.n_out = h.q.n;
-    tc_gemm_launch(h.q, h.tc_staged.as<uint8_t>(), n, e, h.tcws, s);
+    tc_gemm_launch(h.q, h.tc_staged.as<uint8_t>(), n, e, h.tcws, s, 0, true);
   }
 }
 

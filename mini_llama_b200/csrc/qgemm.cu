@@ -131,85 +131,106 @@ __device__ __forceinline__ size_t staged_off(int n, int k, size_t chunk_bytes) {
          (size_t)(n & 7) * 16 + (size_t)(kk & 7) * 2;
 }
 
-// One CTA per padded row r < Mp: x row (RMS-normalised when norm_w, with the
-// statistic of src/ops.cc:55-61 summed in a fixed tree order) as fp16 hi
-// (row r) and lo (row Mp + r) over `chunks` chunks; rows >= rows are zero.
-__global__ void tc_stage_kernel(const float* x, int ldx, int rows, int k, int chunks,
-                                const float* norm_w, float eps, const int* gather,
-                                uint8_t* staged) {
-  const int r = blockIdx.x, mp = gridDim.x;
+constexpr int kStageThreads = 128;
+constexpr int kStageChunks = 4;  // chunks per CTA (128 threads x 8 inputs)
+
+// Eight consecutive inputs from k0 of a row of length k (zeros past the end).
+__device__ __forceinline__ void load8(const float* row, int k0, int k, float (&e)[8]) {
+  if (k0 + 7 < k && ((((uintptr_t)(row + k0)) & 15) == 0)) {
+    const float4 a = __ldcg(reinterpret_cast<const float4*>(row + k0));
+    const float4 b = __ldcg(reinterpret_cast<const float4*>(row + k0 + 4));
+    e[0] = a.x; e[1] = a.y; e[2] = a.z; e[3] = a.w;
+    e[4] = b.x; e[5] = b.y; e[6] = b.z; e[7] = b.w;
+  } else {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) e[i] = k0 + i < k ? __ldcg(row + k0 + i) : 0.0f;
+  }
+}
+
+// CTA (r, g): row r < Mp of x (RMS-normalised when norm_w, with the
+// statistic of src/ops.cc:55-61 summed in a fixed tree order that every CTA
+// of the row repeats identically) over chunks [4 g, 4 g + 4), as fp16 hi (row
+// r) and lo (row Mp + r) of the B layout, and the half-block sums (16 inputs,
+// the thread's 8 then its lane pair's 8) as the Q4_1 min term's K operand.
+// Rows >= rows stage as zero. Each thread takes 8 consecutive inputs.
+__global__ void __launch_bounds__(kStageThreads) tc_stage_kernel(const float* x, int ldx, int rows,
+                                                                 int k, int chunks,
+                                                                 const float* norm_w, float eps,
+                                                                 const int* gather, int mp,
+                                                                 uint8_t* staged) {
+  const int r = blockIdx.x;
   const size_t cb = tc_chunk_bytes(mp);
-  __shared__ float part[32];
+  __shared__ float part[kStageThreads / 32];
   __shared__ float inv_s;
+  pdl_launch_dependents();  // the GEMM after it starts streaming its weights now
+  pdl_wait();
   const bool live = r < rows;
   const float* xr = live ? (gather ? x + (size_t)gather[r] * ldx : x + (size_t)r * ldx) : nullptr;
   float inv = 1.0f;
   if (live && norm_w) {
     float ss = 0.0f;
-    for (int i = threadIdx.x; i < k; i += blockDim.x) {
-      const float v = __ldcg(xr + i);
-      ss = fmaf(v, v, ss);
+    for (int i = threadIdx.x * 4; i < k; i += kStageThreads * 4) {
+      if (i + 3 < k && ((((uintptr_t)(xr + i)) & 15) == 0)) {
+        const float4 v = __ldcg(reinterpret_cast<const float4*>(xr + i));
+        ss = fmaf(v.x, v.x, ss);
+        ss = fmaf(v.y, v.y, ss);
+        ss = fmaf(v.z, v.z, ss);
+        ss = fmaf(v.w, v.w, ss);
+      } else {
+        for (int j = i; j < i + 4 && j < k; ++j) ss = fmaf(xr[j], xr[j], ss);
+      }
     }
     ss = warp_sum(ss);
     if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = ss;
     __syncthreads();
     if (threadIdx.x == 0) {
       float t = 0.0f;
-      for (int w = 0; w < (int)(blockDim.x >> 5); ++w) t += part[w];  // fixed order
+      for (int w = 0; w < kStageThreads / 32; ++w) t += part[w];  // fixed order
       t = __fdiv_rn(t, (float)k);
       inv_s = __fdiv_rn(1.0f, sqrtf(__fadd_rn(t, eps)));
     }
     __syncthreads();
     inv = inv_s;
   }
-  const int units = chunks * 32;  // 8 inputs each
-  for (int u = threadIdx.x; u < units; u += blockDim.x) {
-    const int k0 = u * 8;
-    uint32_t hw[4], lw[4];
+  const int u = blockIdx.y * kStageChunks * 32 + threadIdx.x;  // unit of 8 inputs
+  if (u >= chunks * 32) return;  // whole lane pairs leave together
+  const int k0 = u * 8;
+  float e[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  if (live) {
+    load8(xr, k0, k, e);
+    if (norm_w) {
+      float w[8];
+      load8(norm_w, k0, k, w);
 #pragma unroll
-    for (int p = 0; p < 4; ++p) {
-      float e[2];
-#pragma unroll
-      for (int q = 0; q < 2; ++q) {
-        const int kk = k0 + 2 * p + q;
-        float v = 0.0f;
-        if (live && kk < k) {
-          v = __ldcg(xr + kk);
-          if (norm_w) v = __fmul_rn(__fmul_rn(v, inv), norm_w[kk]);
-        }
-        e[q] = v;
-      }
-      const __half h0 = __float2half_rn(e[0]), h1 = __float2half_rn(e[1]);
-      const __half l0 = __float2half_rn(e[0] - __half2float(h0));
-      const __half l1 = __float2half_rn(e[1] - __half2float(h1));
-      hw[p] = h2_as_u32(__halves2half2(h0, h1));
-      lw[p] = h2_as_u32(__halves2half2(l0, l1));
+      for (int i = 0; i < 8; ++i) e[i] = __fmul_rn(__fmul_rn(e[i], inv), w[i]);
     }
-    *reinterpret_cast<uint4*>(staged + staged_off(r, k0, cb)) =
-        make_uint4(hw[0], hw[1], hw[2], hw[3]);
-    *reinterpret_cast<uint4*>(staged + staged_off(mp + r, k0, cb)) =
-        make_uint4(lw[0], lw[1], lw[2], lw[3]);
   }
-  // half-block sums (16 inputs each, sequential fp32) as fp16 hi / lo: the K
-  // operand of the Q4_1 min term, 16 per chunk
-  for (int hb = threadIdx.x; hb < chunks * 16; hb += blockDim.x) {
-    float s = 0.0f;
-    if (live) {
-      for (int i = 0; i < 16; ++i) {
-        const int kk = hb * 16 + i;
-        if (kk >= k) break;
-        float v = __ldcg(xr + kk);
-        if (norm_w) v = __fmul_rn(__fmul_rn(v, inv), norm_w[kk]);
-        s = __fadd_rn(s, v);
-      }
-    }
-    const __half h = __float2half_rn(s);
-    const __half l = __float2half_rn(s - __half2float(h));
-    const int c = hb >> 4, kk = hb & 15;
+  uint32_t hw[4], lw[4];
+  float s = 0.0f;
+#pragma unroll
+  for (int p = 0; p < 4; ++p) {
+    const __half h0 = __float2half_rn(e[2 * p]), h1 = __float2half_rn(e[2 * p + 1]);
+    const __half l0 = __float2half_rn(e[2 * p] - __half2float(h0));
+    const __half l1 = __float2half_rn(e[2 * p + 1] - __half2float(h1));
+    hw[p] = h2_as_u32(__halves2half2(h0, h1));
+    lw[p] = h2_as_u32(__halves2half2(l0, l1));
+    s = __fadd_rn(__fadd_rn(s, e[2 * p]), e[2 * p + 1]);
+  }
+  *reinterpret_cast<uint4*>(staged + staged_off(r, k0, cb)) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+  *reinterpret_cast<uint4*>(staged + staged_off(mp + r, k0, cb)) =
+      make_uint4(lw[0], lw[1], lw[2], lw[3]);
+  // half-block sum: the even unit's 8 then the odd unit's 8
+  const float s2 = __shfl_xor_sync(0xffffffffu, s, 1);
+  if ((u & 1) == 0) {
+    const float hs = __fadd_rn(s, s2);
+    const __half h = __float2half_rn(hs);
+    const __half l = __float2half_rn(hs - __half2float(h));
+    const int hb = u >> 1, c = hb >> 4, kk = hb & 15;
     uint8_t* base = staged + (size_t)c * cb + (size_t)mp * 1024 + (size_t)(kk >> 3) * 128 +
                     (size_t)(kk & 7) * 2;
     *reinterpret_cast<__half*>(base + (size_t)(r >> 3) * 256 + (size_t)(r & 7) * 16) = h;
-    *reinterpret_cast<__half*>(base + (size_t)((mp + r) >> 3) * 256 + (size_t)((mp + r) & 7) * 16) = l;
+    *reinterpret_cast<__half*>(base + (size_t)((mp + r) >> 3) * 256 + (size_t)((mp + r) & 7) * 16) =
+        l;
   }
 }
 
@@ -472,17 +493,15 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const TcArgs a) 
   tc_fence_after();
   const uint32_t tbase = sh.tmem_base;
 
+  pdl_launch_dependents();  // dependents still wait for this grid to complete
   if (warp == 0) {
     // ------------------------------------------------------ producer
     if (lane == 0) {
       long long it = 0;
       long long last_it[kMaxRingStages];
       for (int s = 0; s < kMaxRingStages; ++s) last_it[s] = -1;
-      for (long long u = u_begin; u < u_end; ++u, ++it) {
+      auto issue_weights = [&](long long u, int s) {
         const int rt = (int)(u / C), c = (int)(u - (long long)rt * C);
-        const int s = (int)(it % a.stages);
-        const uint32_t par = (uint32_t)((it / a.stages) & 1);
-        if (!tc_wait(&sh.empty[s], par ^ 1u, sh, a.status, 700)) break;
         uint8_t* st = ring + (size_t)s * a.stage_bytes;
         const int nt = min(8, a.ntiles - rt * 8);
         mbar_arrive_expect_tx(&sh.full[s], (uint32_t)(nt * a.sbb) + kChunkBytes);
@@ -490,7 +509,29 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const TcArgs a) 
           const long long sbi = sb_index(rt * 8 + j, c, a.ntiles, a.nchunks, a.gc);
           bulk_g2s(st + j * a.sbb, a.w + sbi * a.sbb, a.sbb, &sh.full[s]);
         }
+      };
+      auto issue_acts = [&](long long u, int s) {
+        const int c = (int)(u % C);
+        uint8_t* st = ring + (size_t)s * a.stage_bytes;
         bulk_g2s(st + a.sb_region, a.staged + (size_t)c * kChunkStride, kChunkBytes, &sh.full[s]);
+      };
+      // the first stages' weights do not depend on the previous kernel:
+      // stream them while it finishes (programmatic dependent launch), then
+      // wait for it before copying the activations it staged
+      const long long pre = min((long long)a.stages, u_end - u_begin);
+      for (long long i = 0; i < pre; ++i) issue_weights(u_begin + i, (int)i);
+      pdl_wait();
+      for (long long i = 0; i < pre; ++i) {
+        issue_acts(u_begin + i, (int)i);
+        last_it[i] = i;
+      }
+      it = pre;
+      for (long long u = u_begin + pre; u < u_end; ++u, ++it) {
+        const int s = (int)(it % a.stages);
+        const uint32_t par = (uint32_t)((it / a.stages) & 1);
+        if (!tc_wait(&sh.empty[s], par ^ 1u, sh, a.status, 700)) break;
+        issue_weights(u, s);
+        issue_acts(u, s);
         last_it[s] = it;
       }
       if (*(volatile int*)&sh.abort_flag) {
@@ -561,6 +602,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const TcArgs a) 
     }
   } else {
     // ------------------------------------------- dequantise + epilogue
+    pdl_wait();  // the epilogue reads and writes the previous kernels' data
     const int q = warp & 3, half = (warp - 2) >> 2;
     const int slice = warp - 2;
     const int lr = 32 * q + lane;  // weight row within the CTA tile (TMEM lane)
@@ -637,11 +679,13 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const TcArgs a) 
       if (!whole) {
         // this warp slice's partial into its run slot; the last of the
         // tile's runs to finish this slice sums the slots in chunk order
+        // slot layout [run][column][row]: a warp's 32 rows of one column are
+        // one coalesced 128-byte line
         const long long k0 = first_boundary_after(rt * C, U, G);
         const int jr = run_start == rt * C ? 0 : (int)(blockIdx.x - k0 + 1);
-        float* slot = a.ws + (((size_t)rt * a.maxruns + jr) * kTcRows + lr) * MP + cbase;
+        float* slot = a.ws + (((size_t)rt * a.maxruns + jr) * MP + cbase) * kTcRows + lr;
 #pragma unroll
-        for (int i = 0; i < NC; ++i) slot[i] = v[i];
+        for (int i = 0; i < NC; ++i) slot[(size_t)i * kTcRows] = v[i];
         __threadfence();
         __syncwarp();
         int last = 0;
@@ -656,9 +700,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const TcArgs a) 
 #pragma unroll
         for (int i = 0; i < NC; ++i) v[i] = 0.0f;
         for (int jj = 0; jj < nr; ++jj) {
-          const float* sl = a.ws + (((size_t)rt * a.maxruns + jj) * kTcRows + lr) * MP + cbase;
+          const float* sl = a.ws + (((size_t)rt * a.maxruns + jj) * MP + cbase) * kTcRows + lr;
 #pragma unroll
-          for (int i = 0; i < NC; ++i) v[i] += __ldcg(sl + i);
+          for (int i = 0; i < NC; ++i) v[i] += __ldcg(sl + (size_t)i * kTcRows);
         }
         if (lane == 0) a.counters[rt * 8 + slice] = 0;
       }
@@ -687,11 +731,13 @@ void* tc_kernel_for(int mp) {
 }  // namespace
 
 void tc_stage_launch(const float* x, int ldx, int rows, int k, int chunks, const float* norm_w,
-                     float eps, const int* gather, uint8_t* staged, cudaStream_t stream) {
+                     float eps, const int* gather, uint8_t* staged, cudaStream_t stream,
+                     bool pdl) {
   const int mp = tc_mp(rows);
   if (mp > kTcMaxMp) invalid("tensor-core GEMM: more than 64 activation rows per pass");
-  tc_stage_kernel<<<mp, 256, 0, stream>>>(x, ldx, rows, k, chunks, norm_w, eps, gather, staged);
-  MLB_CUDA(cudaGetLastError());
+  const dim3 grid(mp, (chunks + kStageChunks - 1) / kStageChunks);
+  launch_pdl(tc_stage_kernel, grid, dim3(kStageThreads), 0, stream, pdl, x, ldx, rows, k, chunks,
+             norm_w, eps, gather, mp, staged);
 }
 
 // CTAs of a launch: at most one per (tile, chunk) unit, so that every CTA
@@ -716,7 +762,7 @@ bool tc_gemm_ok(const QMatrix& m, int rows) {
 }
 
 void tc_gemm_launch(const QMatrix& m, const uint8_t* staged, int rows, const BEpi& epi,
-                    const TcWorkspace& ws, cudaStream_t stream, int grid_ctas) {
+                    const TcWorkspace& ws, cudaStream_t stream, int grid_ctas, bool pdl) {
   if (!tc_gemm_ok(m, rows)) invalid("tensor-core GEMM: unsupported matrix or batch");
   int dev = 0;
   MLB_CUDA(cudaGetDevice(&dev));
@@ -750,8 +796,18 @@ void tc_gemm_launch(const QMatrix& m, const uint8_t* staged, int rows, const BEp
                                  : (m.qtype == MLB_Q4_1 ? tc_kernel_for<MLB_Q4_1>(mp)
                                                         : tc_kernel_for<MLB_Q8_0>(mp));
   MLB_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kTcThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
   void* params[] = {&a};
-  MLB_CUDA(cudaLaunchKernel(fn, dim3(grid), dim3(kTcThreads), params, smem, stream));
+  MLB_CUDA(cudaLaunchKernelExC(&cfg, fn, params));
 }
 
 }  // namespace mlb

@@ -81,8 +81,11 @@ struct TcWorkspace {
 // row by row) -> fp16 hi/lo in the B layout of `chunks` 256-input chunks.
 // Rows >= rows and inputs >= k stage as zero. gather (optional): row r of x is
 // table + gather[r] * ldx (the embedding rows of the step's tokens).
+// pdl: launch with programmatic dependent launch (the kernel waits for the
+// previous one before reading its data).
 void tc_stage_launch(const float* x, int ldx, int rows, int k, int chunks, const float* norm_w,
-                     float eps, const int* gather, uint8_t* staged, cudaStream_t stream);
+                     float eps, const int* gather, uint8_t* staged, cudaStream_t stream,
+                     bool pdl = false);
 
 // Scratch sizes for a matrix at `rows` activation rows on `grid` CTAs.
 size_t tc_partial_floats(const QMatrix& m, int rows, int grid);
@@ -90,8 +93,11 @@ int tc_counter_count(const QMatrix& m);
 
 // y = W x for the staged activations (rows <= kTcMaxMp), epilogue `epi`.
 // grid_ctas 0 = one CTA per SM.
+// pdl: programmatic dependent launch; the first stages' weight copies are
+// issued before the kernel waits for the previous one.
 void tc_gemm_launch(const QMatrix& m, const uint8_t* staged, int rows, const BEpi& epi,
-                    const TcWorkspace& ws, cudaStream_t stream, int grid_ctas = 0);
+                    const TcWorkspace& ws, cudaStream_t stream, int grid_ctas = 0,
+                    bool pdl = false);
 
 // Whether the tensor-core GEMM takes this matrix (quantised, k <= 2^20).
 bool tc_gemm_ok(const QMatrix& m, int rows);
