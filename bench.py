@@ -368,6 +368,41 @@ def gemv_sweep(torch, mlb, args, peak, with_cpu=True):
     return rows, windows, cpu
 
 
+PHASE_KINDS = ("qkv", "attention", "wo", "gate_up", "down")
+
+
+def step_phase_summary(ctx, tok, pos, n_layers, n=5):
+    """Per-phase times of the step kernel (mlb_context_step_trace), after the
+    timed region: n single steps, each read on its own, medians over steps,
+    summed over layers by phase kind. span: from the latest CTA end of the
+    phase before to the latest CTA end of this one (grid barriers and
+    cross-rank waits count in the phase after them); work_mean / work_max:
+    the mean / largest CTA time from the phase's start (after its barrier) to
+    its end."""
+    ctx.step_trace(True)
+    spans, wmean, wmax = [], [], []
+    for _ in range(n):
+        tok = ctx.decode_greedy(tok, pos, 1)[-1]
+        pos += 1
+        st = ctx.step_trace_read().astype(np.int64)
+        start, end = st[:, :, 0], st[:, :, 1]
+        ends = end.max(axis=1)
+        spans.append(np.diff(np.concatenate([[start[0].min()], ends])) / 1e3)
+        work = (end - start) / 1e3
+        wmean.append(work.mean(axis=1))
+        wmax.append(work.max(axis=1))
+    ctx.step_trace(False)
+    out = {}
+    for key, rows in (("span", spans), ("work_mean", wmean), ("work_max", wmax)):
+        med = np.median(np.stack(rows), axis=0)
+        d = {k: round(float(med[i:5 * n_layers:5].sum()), 1) for i, k in enumerate(PHASE_KINDS)}
+        d["lm_head"] = round(float(med[5 * n_layers:].sum()), 1)
+        d["total"] = round(float(med.sum()), 1)
+        out[key] = d
+    out["unit"] = "us per step, summed over layers (median of single traced steps, this rank)"
+    return out
+
+
 def measure_workload(torch, mlb, dist, args, name, cfg, qtype, bias, rank, world, local,
                      steps, warmup, peak, check_single):
     """One decode workload on this rank: seeded model and K/V state at depth
@@ -437,6 +472,7 @@ def measure_workload(torch, mlb, dist, args, name, cfg, qtype, bias, rank, world
     barrier()
     e2e_ms = max_over_ranks(e0.elapsed_time(e1))
     kpl = ctx.kernels_per_step()
+    phases = step_phase_summary(ctx, tok, pos, cfg["n_layers"]) if step_kernel else None
     ctx.close()
     model.close()
 
@@ -481,7 +517,7 @@ def measure_workload(torch, mlb, dist, args, name, cfg, qtype, bias, rank, world
                 "api": "mlb_forward_token (host logits)"},
         "roofline": roof, "kernels_per_step": kpl, "step_kernel": step_kernel,
         "resident_bytes": resident, "step_weight_bytes": step_weights, "tp_check": tp_check,
-        "gpu_launches": kpl * steps,
+        "gpu_launches": kpl * steps, "step_phases": phases,
     }
 
 
@@ -664,6 +700,7 @@ def run_gpu(args, cfg, qtype, bias, rank, world, local):
             "gpu_launches": head["gpu_launches"],
             "kernels_per_step": head["kernels_per_step"],
             "resident_bytes": head["resident_bytes"],
+            "step_phases": head["step_phases"],
         }
         if gemv_roof:
             line["gemv_roofline"] = gemv_roof

@@ -323,14 +323,29 @@ int mlb_context_kernels_per_step(const mlb_context* c);
 /* Selects how a single-GPU decode step runs: 1 = the persistent step kernel
  * (one cooperative launch computes the whole step; the default wherever the
  * model allows it), 0 = one kernel per op in a CUDA graph. Asking for 1 on a
- * model the step kernel does not take (tensor parallel, F32 or mixed quant
- * types, head_dim > 128 or not a multiple of 4, very large GQA groups)
+ * model the step kernel does not take (F32 or mixed quant types, head_dim >
+ * 128 or not a multiple of 4, very large GQA groups, tensor parallel with dim
+ * above 8192)
  * returns MLB_ERR_INVALID and mlb_last_error() gives the reason. No reference
  * counterpart: the reference always launches one kernel per op
  * (src/forward.cc:700-794). */
 int mlb_context_set_step_kernel(mlb_context* c, int enable);
 /* 1 when this context's steps run as the persistent step kernel, else 0. */
 int mlb_context_step_kernel(const mlb_context* c);
+
+/* Phase trace of the step kernel (a diagnostic; no reference counterpart).
+ * enable = 1 makes every later step record, per phase and CTA, two global-
+ * timer stamps (ns): the start of the phase's work after the grid barrier
+ * ahead of it, and its end before the next one; the context must be on the
+ * step kernel. mlb_context_step_trace_read sets *nphases and *grid; when
+ * stamps is non-null and cap >= nphases * grid * 2 it syncs the context's
+ * stream, copies the stamps of the last traced step there ([phase][cta][2])
+ * and clears the record (a read with no whole traced step since the last one
+ * fails); otherwise it only reports the sizes. Phases in order: per layer
+ * QKV projection, attention, wo, gate/up, w_down; then lm_head. */
+int mlb_context_step_trace(mlb_context* c, int enable);
+int mlb_context_step_trace_read(mlb_context* c, uint64_t* stamps, size_t cap, int* nphases,
+                                int* grid);
 
 /* ------------------------------------------------------------------ batches
  * Rows of (token, position) go through every layer together: the weights

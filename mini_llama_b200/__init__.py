@@ -457,6 +457,22 @@ class Context:
     def step_kernel(self) -> bool:
         return bool(lib().mlb_context_step_kernel(self.h))
 
+    def step_trace(self, enable: bool):
+        """Records per-phase times of later step-kernel steps (diagnostic)."""
+        check(lib().mlb_context_step_trace(self.h, 1 if enable else 0))
+
+    def step_trace_read(self) -> np.ndarray:
+        """Global-timer stamps (ns) of the last traced step, [phase][cta][2]:
+        start of each phase's work after its barrier, end before the next.
+        Phases: per layer QKV, attention, wo, gate/up, w_down; then lm_head."""
+        n, g = ctypes.c_int(0), ctypes.c_int(0)
+        check(lib().mlb_context_step_trace_read(self.h, None, 0, ctypes.byref(n),
+                                                ctypes.byref(g)))
+        out = np.zeros((n.value, g.value, 2), np.uint64)
+        check(lib().mlb_context_step_trace_read(self.h, out.ctypes.data, out.size,
+                                                ctypes.byref(n), ctypes.byref(g)))
+        return out
+
     def forward_token(self, token: int, pos: int) -> np.ndarray:
         """ForwardToken's device branch (src/forward.cc:776-794): host logits."""
         out = np.empty(self.model.cfg["vocab_size"], np.float32)

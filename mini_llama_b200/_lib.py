@@ -90,6 +90,9 @@ SIGNATURES = [
     ("mlb_context_kernels_per_step", _c_int, [_vp]),
     ("mlb_context_set_step_kernel", _c_int, [_vp, _c_int]),
     ("mlb_context_step_kernel", _c_int, [_vp]),
+    ("mlb_context_step_trace", _c_int, [_vp, _c_int]),
+    ("mlb_context_step_trace_read", _c_int,
+     [_vp, _vp, _c_size_t, ctypes.POINTER(_c_int), ctypes.POINTER(_c_int)]),
     ("mlb_nccl_unique_id", _c_int, [_vp]),
     ("mlb_forward_batch", _c_int, [_vp, _c_int, _vp, _vp, _vp]),
     ("mlb_batch_create", _c_int, [_vp, _c_int, _c_int, ctypes.POINTER(_vp)]),

@@ -605,6 +605,21 @@ int mlb_context_set_step_kernel(mlb_context* c, int enable) {
 
 int mlb_context_step_kernel(const mlb_context* c) { return c && c->impl->use_step ? 1 : 0; }
 
+int mlb_context_step_trace(mlb_context* c, int enable) {
+  return guarded([&] {
+    if (!c) invalid("mlb_context_step_trace: null context");
+    c->impl->set_step_trace(enable != 0);
+  });
+}
+
+int mlb_context_step_trace_read(mlb_context* c, uint64_t* stamps, size_t cap, int* nphases,
+                                int* grid) {
+  return guarded([&] {
+    if (!c || !nphases || !grid) invalid("mlb_context_step_trace_read: null argument");
+    c->impl->read_step_trace(reinterpret_cast<unsigned long long*>(stamps), cap, nphases, grid);
+  });
+}
+
 int mlb_wait_selftest(int device, int which, double limit_ms, int* code, int* where) {
   return guarded([&] {
     if (!code || !where) invalid("mlb_wait_selftest: null output");

@@ -97,10 +97,12 @@ struct EpiParams {
   float* ss_out;
   // Step kernel (set on the device): resid_s, when set, holds the residual
   // rows of tiles resid_t0.. (batch row 0) in shared memory; pos_set marks
-  // pos_now as the position (else *pos is read)
+  // pos_now as the position (else *pos is read); rope_s, when set, holds the
+  // position's rope row (head_dim / 2 float2) in shared memory
   const float* resid_s;
   int resid_t0;
   int pos_set, pos_now;
+  const float2* rope_s;
 };
 
 #if defined(__CUDACC__)

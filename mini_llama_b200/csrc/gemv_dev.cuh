@@ -199,7 +199,8 @@ __device__ __forceinline__ void cursor_step16(SbCursor& c, int ntiles, int nchun
 // --------------------------------------------------------------- epilogues
 
 template <int M>
-__device__ void epilogue_row(const EpiParams& p, int tile, int row, int r, const float* vals) {
+// Returns the value stored for a residual row (0 for other kinds).
+__device__ float epilogue_row(const EpiParams& p, int tile, int row, int r, const float* vals) {
   float v = vals[row * M + r];
   int grow = tile * 16 + row;
   switch (p.kind) {
@@ -218,9 +219,10 @@ __device__ void epilogue_row(const EpiParams& p, int tile, int row, int r, const
         const TpXchg* x = p.tp;
         const long long o =
             x->parts_off + ((long long)(p.tp_slot * x->n + x->me) * x->dim + grow) * 8;
-        for (int rr = 0; rr < x->n; ++rr)
-          asm volatile("st.relaxed.sys.global.v2.u32 [%0], {%1, %2};" ::"l"(x->peers[rr] + o),
-                       "r"(__float_as_uint(v)), "r"(p.tp_tag)
+        const unsigned long long word =
+            ((unsigned long long)p.tp_tag << 32) | (unsigned long long)__float_as_uint(v);
+        for (int rr = 0; rr < x->n; ++rr)  // one whole 8-byte word per rank
+          asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(x->peers[rr] + o), "l"(word)
                        : "memory");
       }
       break;
@@ -228,7 +230,9 @@ __device__ void epilogue_row(const EpiParams& p, int tile, int row, int r, const
       if (grow < p.n_out) {
         const float rv = p.resid_s ? p.resid_s[grow - p.resid_t0 * 16]
                                    : __ldcg(p.resid + (size_t)r * p.ldr + grow);
-        p.y[(size_t)r * p.ldy + grow] = __fadd_rn(rv, v);
+        const float y = __fadd_rn(rv, v);
+        p.y[(size_t)r * p.ldy + grow] = y;
+        return y;
       }
       break;
     case kEpiSwiglu: {
@@ -277,7 +281,7 @@ __device__ void epilogue_row(const EpiParams& p, int tile, int row, int r, const
         first = (in_head & 1) == 0;
         j = in_head >> 1;
       }
-      float2 cs = p.rope[(size_t)pos * (D / 2) + j];
+      float2 cs = p.rope_s ? p.rope_s[j] : p.rope[(size_t)pos * (D / 2) + j];
       float out;
       if (first)  // a*c - b*s with a = this, b = partner (src/ops.cc:155, 174)
         out = __fsub_rn(__fmul_rn(v, cs.x), __fmul_rn(w, cs.y));
@@ -290,6 +294,7 @@ __device__ void epilogue_row(const EpiParams& p, int tile, int row, int r, const
       break;
     }
   }
+  return 0.0f;
 }
 
 // ------------------------------------------------------ activation staging
@@ -461,30 +466,53 @@ struct TpSum {
   int* failed;  // shared flag, set to 1 on timeout
 };
 
-// Adds rank rr's tagged partial sums of inputs k0 .. k0 + 3 to v, waiting
-// (bounded) until all four words carry the tag.
-__device__ __forceinline__ void tp_add_quad(const TpSum& t, int rr, int k0, int k, float4& v) {
-  const uint2* w = t.parts + (size_t)rr * t.ldp + k0;
-  float e[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+// Two tagged words {fp32 bits (low half), tag (high half)} from a 16-byte
+// aligned address, each 8-byte word read whole (single-copy atomic u64).
+__device__ __forceinline__ void ld_tagged_pair(const void* p, unsigned long long& a,
+                                               unsigned long long& b) {
+  asm volatile("ld.relaxed.sys.global.v2.u64 {%0, %1}, [%2];"
+               : "=l"(a), "=l"(b)
+               : "l"(p)
+               : "memory");
+}
+
+// Adds every rank's tagged partial sums of inputs k0 .. k0 + 3 (k0 a multiple
+// of 4) to v in rank order: per rank two 16-byte loads of two tagged words
+// each, re-loading only a pair whose tags are not yet this exchange step's
+// (bounded; on timeout the status records it and *failed is set). Words past
+// k count as zero. Out of line and one rank at a time: the callers keep
+// several staged quads per thread in registers, and holding every rank's
+// words at once (or inlining this into each caller) spills them.
+static __device__ __noinline__ void tp_add_all(const TpSum& t, int k0, int k, float4& v) {
+  const unsigned long long tag = t.tag;
   const long long t0 = clock64();
-  for (int i = 0; i < 4; ++i) {
-    if (k0 + i >= k) break;
-    uint32_t val, tg;
-    while (true) {
-      asm volatile("ld.relaxed.sys.global.v2.u32 {%0, %1}, [%2];"
-                   : "=r"(val), "=r"(tg) : "l"(w + i) : "memory");
-      if (tg == t.tag) break;
-      if (clock64() - t0 > 4000000000LL || *(volatile int*)t.failed) {
-        if (t.status && atomicCAS(&t.status->code, 0, MLB_ERR_TIMEOUT) == 0)
-          atomicExch(&t.status->where, 400);
-        *(volatile int*)t.failed = 1;
-        val = 0u;
-        break;
+#pragma unroll 1
+  for (int rr = 0; rr < t.nparts; ++rr) {
+    const uint2* p = t.parts + (size_t)rr * t.ldp + k0;
+    unsigned long long w[4];
+    ld_tagged_pair(p, w[0], w[1]);
+    ld_tagged_pair(p + 2, w[2], w[3]);
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh) {
+      const bool need0 = k0 + 2 * hh < k, need1 = k0 + 2 * hh + 1 < k;
+      while ((need0 && (w[2 * hh] >> 32) != tag) || (need1 && (w[2 * hh + 1] >> 32) != tag)) {
+        if (clock64() - t0 > 4000000000LL || *(volatile int*)t.failed) {
+          if (t.status && atomicCAS(&t.status->code, 0, MLB_ERR_TIMEOUT) == 0)
+            atomicExch(&t.status->where, 400);
+          *(volatile int*)t.failed = 1;
+          w[2 * hh] = w[2 * hh + 1] = tag << 32;
+          break;
+        }
+        ld_tagged_pair(p + 2 * hh, w[2 * hh], w[2 * hh + 1]);
       }
+      if (!need0) w[2 * hh] = 0ull;
+      if (!need1) w[2 * hh + 1] = 0ull;
     }
-    e[i] = __uint_as_float(val);
+    v.x += __uint_as_float((unsigned int)w[0]);
+    v.y += __uint_as_float((unsigned int)w[1]);
+    v.z += __uint_as_float((unsigned int)w[2]);
+    v.w += __uint_as_float((unsigned int)w[3]);
   }
-  v.x += e[0]; v.y += e[1]; v.z += e[2]; v.w += e[3];
 }
 
 template <int QT>
@@ -509,7 +537,7 @@ __device__ __forceinline__ void stage_x_m1(const float* x, int k, const float* n
       if (idx < nq) {
         v[j] = load_quad(x, kbase + idx * 4, k, false);
         if (tps) {
-          for (int rr = 0; rr < tps->nparts; ++rr) tp_add_quad(*tps, rr, kbase + idx * 4, k, v[j]);
+          tp_add_all(*tps, kbase + idx * 4, k, v[j]);
           if (tps->store) {  // this CTA's slice of the summed row
             const int lo = (int)((long long)nq * blockIdx.x / gridDim.x);
             const int hi = (int)((long long)nq * (blockIdx.x + 1) / gridDim.x);
@@ -580,7 +608,7 @@ __device__ __forceinline__ void tp_store_slice(const float* x, int k, const TpSu
   const int hi = (int)((long long)nq * (blockIdx.x + 1) / gridDim.x);
   for (int idx = lo + threadIdx.x; idx < hi; idx += blockDim.x) {
     float4 v = load_quad(x, idx * 4, k, false);
-    for (int rr = 0; rr < tps.nparts; ++rr) tp_add_quad(tps, rr, idx * 4, k, v);
+    tp_add_all(tps, idx * 4, k, v);
     const float e4[4] = {v.x, v.y, v.z, v.w};
     for (int i = 0; i < 4; ++i)
       if (idx * 4 + i < k) tps.store[idx * 4 + i] = e4[i];
@@ -805,18 +833,16 @@ __device__ __forceinline__ void finish_runs(const float* parts, float* red, cons
       }
     }
     if (finish) {
+      float stored = 0.0f;  // M == 1: row `lane` (< 16) of the tile
       for (int i = lane; i < 16 * M; i += 32) {
         int row = i / M, rb = i - row * M;
-        if (rb < fg.rows) epilogue_row<M>(epi, t, row, rb, myred);
+        if (rb < fg.rows) stored = epilogue_row<M>(epi, t, row, rb, myred);
       }
       if (M == 1 && epi.ss_out && epi.kind == kEpiResidual) {
-        // lane r < 16 wrote row r above; its square, summed over the 16 rows
+        // lane r < 16 stored row r above; its square, summed over the 16 rows
         // by a fixed tree (lanes 16.. add zeros and are not read)
         float sq = 0.0f;
-        if (lane < 16 && t * 16 + lane < epi.n_out) {
-          const float yv = epi.y[t * 16 + lane];
-          sq = yv * yv;
-        }
+        if (lane < 16 && t * 16 + lane < epi.n_out) sq = stored * stored;
         sq += __shfl_xor_sync(0xffffffffu, sq, 8);
         sq += __shfl_xor_sync(0xffffffffu, sq, 4);
         sq += __shfl_xor_sync(0xffffffffu, sq, 2);

@@ -774,6 +774,7 @@ void ContextImpl::launch_step(cudaStream_t s) {
     a.tp_gen = tp_gen.as<unsigned int>();
     a.tp_steps = 2 * m->cfg.n_layers;
   }
+  a.trace = trace_on ? step_trace.as<unsigned long long>() : nullptr;
   step_launch(step, a, s);
 }
 
@@ -1032,7 +1033,34 @@ void ContextImpl::set_use_step(bool on) {
   set_device(m->device);
   MLB_CUDA(cudaStreamSynchronize(stream));
   use_step = on;
+  if (!on) trace_on = false;
   build_graph();
+}
+
+void ContextImpl::set_step_trace(bool on) {
+  if (on && !use_step) invalid("mlb_context_step_trace: the context is not on the step kernel");
+  set_device(m->device);
+  MLB_CUDA(cudaStreamSynchronize(stream));
+  if (on && !step_trace.p) step_trace.alloc((size_t)step.nphases * step.grid * 2 * 8);
+  if (on) MLB_CUDA(cudaMemset(step_trace.p, 0, step_trace.bytes));
+  trace_on = on;
+  build_graph();
+}
+
+void ContextImpl::read_step_trace(unsigned long long* stamps, size_t cap, int* nphases,
+                                  int* grid) {
+  if (!trace_on) invalid("mlb_context_step_trace_read: tracing is off");
+  *nphases = step.nphases;
+  *grid = step.grid;
+  const size_t n = step_trace.bytes / 8;
+  if (!stamps || cap < n) return;  // a size query
+  set_device(m->device);
+  MLB_CUDA(cudaStreamSynchronize(stream));
+  MLB_CUDA(cudaMemcpy(stamps, step_trace.p, step_trace.bytes, cudaMemcpyDeviceToHost));
+  MLB_CUDA(cudaMemset(step_trace.p, 0, step_trace.bytes));
+  for (size_t i = 0; i < n; ++i)
+    if (stamps[i] == 0ull)
+      invalid("mlb_context_step_trace_read: no whole traced step since the last read");
 }
 
 void ContextImpl::check_status() {

@@ -98,6 +98,8 @@ struct ContextImpl {
   // words and attention workspace. use_step selects it over the per-op graph.
   StepPlan step;
   DevBuf step_phases, step_cta, step_sync, step_attn_ws, step_attn_cnt;
+  DevBuf step_trace;      // [nphases][grid][2] u64 (StepArgs::trace) while tracing
+  bool trace_on = false;
   // tensor-parallel step kernel: this rank's exchange buffer, the other
   // ranks' buffers mapped here, the exchange descriptor and step counter
   DevBuf xchg, tp_desc, tp_gen;
@@ -114,6 +116,8 @@ struct ContextImpl {
   void release_graphs();
   void replay(bool greedy);  // one step from the graph (or a direct launch)
   void set_use_step(bool on);
+  void set_step_trace(bool on);
+  void read_step_trace(unsigned long long* stamps, size_t cap, int* nphases, int* grid);
   void check_status();
   ~ContextImpl();
 };

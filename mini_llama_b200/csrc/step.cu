@@ -60,6 +60,12 @@ struct AttnShape {
   static constexpr int NV = HG * PB;          // scores per block (<= 16)
 };
 
+// A softmax record (m, l, o[D]) is kRec(D) floats with o at offset kRecO, so
+// that o starts on a 16-byte boundary (D is a multiple of 4).
+constexpr int kRecO = 4;
+__host__ __device__ constexpr int attn_rec(int D) { return D + kRecO; }
+
+
 // Residual rows a CTA prefetches into shared memory for its residual epilogue
 // (16 tiles; larger ranges read the residual from L2 in the epilogue).
 constexpr int kResidPre = 256;
@@ -84,6 +90,9 @@ struct ProducerRun {
 // Shared state of one CTA besides the ring and the scratch region.
 struct StepShared {
   StepPhase cur[2];  // this phase's descriptor and the next one's (prefetched)
+  // the launch arguments, copied once: the phases read them from here rather
+  // than through a generic pointer to the parameter space
+  StepArgs args;
   float inv_rms[4];
   float part[kStepWarps];
   int run_u0[kWinRuns + 1];
@@ -96,7 +105,14 @@ struct StepShared {
   int pos, token;        // the step's position and input token (read once)
   Producer prod[kStepWarps];  // each warp's producer (lane 0 reads and writes it)
   alignas(16) float resid_pre[kResidPre];  // residual rows of this CTA's tiles (epilogue)
+  alignas(16) float2 rope_pre[64];         // the position's rope row (QKV epilogue, D <= 128)
 };
+
+__device__ __forceinline__ unsigned long long global_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
 
 __device__ __forceinline__ unsigned int ld_acquire_u32(const unsigned int* p) {
   unsigned int v;
@@ -313,6 +329,10 @@ __device__ __forceinline__ GemvScratch gemv_scratch(uint8_t* scratch, const Step
 // phase's n per-tile sums of squares, summed in one fixed order and broadcast
 // from lane 0, so every warp of every CTA gets the same bits. Eight
 // independent loads per lane per round (one L2 round trip up to 256 tiles).
+// Plain (L1-cached) loads: every warp of every CTA reads the same n values,
+// written by other CTAs before the grid barrier whose acquire orders these
+// reads, so the CTA's warps share its L1 lines instead of each sending the
+// same requests to the few L2 lines that hold them.
 __device__ __forceinline__ float warp_inv_rms(const float* ss, int n, int k, float eps) {
   const int lane = threadIdx.x & 31;
   float v = 0.0f;
@@ -321,7 +341,7 @@ __device__ __forceinline__ float warp_inv_rms(const float* ss, int n, int k, flo
 #pragma unroll
     for (int q = 0; q < 8; ++q) {
       const int i = i0 + lane + 32 * q;
-      t[q] = i < n ? __ldcg(ss + i) : 0.0f;
+      t[q] = i < n ? ss[i] : 0.0f;
     }
 #pragma unroll
     for (int q = 0; q < 8; ++q) v += t[q];
@@ -380,6 +400,7 @@ __device__ __forceinline__ void stage_chunks_warp(const float* x, int k, const f
     }
   }
 }
+
 
 // One warp, one chunk-major window of Tw tiles: chunk c = warp, warp + 16, ...
 // of every tile, from the ring in the producer's order; each super-block's
@@ -487,9 +508,18 @@ __device__ bool gemv_phase(StepShared& sh, StepPhase& cur, const StepCta& ct, ui
       }
     }
   }
-  if (threadIdx.x == 0 && g.epi.kind == kEpiQkv) {
-    cur.g.epi.pos_set = 1;
-    cur.g.epi.pos_now = sh.pos;
+  if (g.epi.kind == kEpiQkv) {
+    // the rope row of this position, fetched now for the epilogue
+    const int D = g.epi.head_dim;
+    const float2* src = g.epi.rope + (size_t)sh.pos * (D / 2);
+    for (int i = threadIdx.x; i < D / 4; i += blockDim.x)
+      cp_async16(reinterpret_cast<float4*>(sh.rope_pre) + i, reinterpret_cast<const float4*>(src) + i);
+    cp_async_commit();
+    if (threadIdx.x == 0) {
+      cur.g.epi.pos_set = 1;
+      cur.g.epi.pos_now = sh.pos;
+      cur.g.epi.rope_s = sh.rope_pre;
+    }
   }
   const EpiParams& epi = cur.g.epi;
   RunTable rt{sh.run_u0, sh.run_t, sh.run_grp, sh.run_cc0};
@@ -558,10 +588,6 @@ __device__ __forceinline__ void warp_multi_sum(float (&v)[NV], int lane) {
   }
 }
 
-// A softmax record (m, l, o[D]) is kRec(D) floats with o at offset kRecO, so
-// that o starts on a 16-byte boundary (D is a multiple of 4).
-constexpr int kRecO = 4;
-__host__ __device__ constexpr int attn_rec(int D) { return D + kRecO; }
 
 struct AttnScratch {
   float* wpart;   // [warps][gq][attn_rec(D)]: m, l, -, -, o
@@ -797,23 +823,40 @@ __device__ __noinline__ bool attn_phase(StepShared& sh, const StepPhase& cur, ui
         acc = fmaf(s.wpart[((size_t)i * gq + h) * rec + kRecO + d], s.ew[h * kMaxGrid + i], acc);
       dst[h * rec + kRecO + d] = acc;
     }
-    // thread 0 publishes the CTA's record (bar.sync, then its fence: the
-    // pattern of a grid barrier) and, as the head's last slice, acquires the
-    // others' before the block reads them
+    // thread 0 publishes the CTA's record and, as the head's last slice,
+    // acquires the others' before the block reads them: one acq_rel add
+    // after bar.sync (the pattern of a grid barrier)
     __syncthreads();
     if (threadIdx.x == 0) {
-      __threadfence();
-      const bool last = atomicAdd(&a.attn_counters[kvh], 1) == pph - 1;
-      if (last) __threadfence();
-      sh.flag = last;
+      unsigned int prev;
+      asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;"
+                   : "=r"(prev)
+                   : "l"(a.attn_counters + kvh)
+                   : "memory");
+      sh.flag = (int)prev == pph - 1;
     }
     __syncthreads();
     if (sh.flag) {
-      // the last slice of the head to finish combines all slices, in order
-      attn_combine(
-          s, D, gq, pph,
-          [&](int h, int i) { return a.attn_ws + ((size_t)(kvh * pph + i) * gq + h) * rec; },
-          true, out);
+      // The last slice of the head to finish combines all slices, in order:
+      // their records are copied into the scratch past the attention's own
+      // (one round trip for all of them) when they fit, else read in place.
+      const float* src = a.attn_ws + (size_t)kvh * pph * gq * rec;
+      const size_t own = ((size_t)((s.ew + gq * kMaxGrid) - reinterpret_cast<float*>(scratch)) *
+                              4 + 127) / 128 * 128;
+      const size_t need = (size_t)pph * gq * rec * 4;
+      if (own + need <= (size_t)a.scratch_bytes) {
+        float* rs = reinterpret_cast<float*>(scratch + own);
+        for (int i = threadIdx.x; i < (int)(need / 16); i += kStepThreads)
+          cp_async16(reinterpret_cast<float4*>(rs) + i, reinterpret_cast<const float4*>(src) + i);
+        cp_async_commit();
+        cp_async_wait_all();
+        __syncthreads();
+        attn_combine(s, D, gq, pph,
+                     [&](int h, int i) { return rs + ((size_t)i * gq + h) * rec; }, false, out);
+      } else {
+        attn_combine(s, D, gq, pph,
+                     [&](int h, int i) { return src + ((size_t)i * gq + h) * rec; }, true, out);
+      }
       if (threadIdx.x == 0) a.attn_counters[kvh] = 0;
     }
     __syncthreads();
@@ -824,14 +867,17 @@ __device__ __noinline__ bool attn_phase(StepShared& sh, const StepPhase& cur, ui
 // ---------------------------------------------------------------- kernel
 
 template <int QT, int HG>
-__global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const StepArgs a) {
+__global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const StepArgs args) {
   extern __shared__ __align__(128) uint8_t smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   uint8_t* ring_base = smem;
   uint64_t* bars =
-      reinterpret_cast<uint64_t*>(smem + (size_t)kStepWarps * a.stages * a.sb_stride);
+      reinterpret_cast<uint64_t*>(smem + (size_t)kStepWarps * args.stages * args.sb_stride);
   uint8_t* scratch = reinterpret_cast<uint8_t*>(bars + kStepWarps * kMaxStages);
-  StepShared& sh = *reinterpret_cast<StepShared*>(scratch + a.scratch_bytes);
+  StepShared& sh = *reinterpret_cast<StepShared*>(scratch + args.scratch_bytes);
+  if (threadIdx.x == 0) sh.args = args;
+  __syncthreads();
+  const StepArgs& a = sh.args;
   StepCta* tab = reinterpret_cast<StepCta*>(reinterpret_cast<uint8_t*>(&sh) +
                                             (sizeof(StepShared) + 15) / 16 * 16);
   // this CTA's column of the phase table
@@ -887,6 +933,8 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
     StepPhase& cur = sh.cur[p & 1];
     if (threadIdx.x == 0) sh.flag = 1;
     __syncthreads();
+    if (a.trace && threadIdx.x == 0)
+      a.trace[((size_t)p * gridDim.x + blockIdx.x) * 2] = global_ns();
     if (p + 1 < a.nphases) {
       const int4* src = reinterpret_cast<const int4*>(a.phases + p + 1);
       int4* dst = reinterpret_cast<int4*>(&sh.cur[(p + 1) & 1]);
@@ -898,6 +946,8 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
     else
       ok = attn_phase<HG>(sh, cur, scratch, a);
     cp_async_wait_all();
+    if (a.trace && threadIdx.x == 0)
+      a.trace[((size_t)p * gridDim.x + blockIdx.x) * 2 + 1] = global_ns();
     if (cur.kind == kPhaseGemv && cur.g.tp_ar >= 0) {
       // tensor parallel: the next phase reads this one's partial sums as
       // tagged words and waits for the tags itself; no barrier

@@ -97,6 +97,10 @@ struct StepArgs {
   const TpXchg* tp;
   unsigned int* tp_gen;
   int tp_steps;
+  // optional phase trace (null: none): global-timer nanoseconds per phase p
+  // and CTA c at [(p * grid + c) * 2]: the start of the phase's work (after
+  // the barrier ahead of it) and, at + 1, its end (before the next barrier)
+  unsigned long long* trace;
 };
 
 // Launch plan of the step kernel for one context.

@@ -208,6 +208,36 @@ def test_step_kernel_selection(cuda):
         f32.set_step_kernel(True)
 
 
+def test_step_trace(cuda):
+    """The step kernel's phase trace: one traced step gives stamps for 5 phases
+    per layer plus lm_head on every CTA, in order; the traced steps decode the
+    same ids; a read
+    with no step since the last one, tracing on the per-op path, and reading
+    with tracing off are refused."""
+    mt = meta()["small_q4_0_gqa"]
+    model = mlb.CudaModel(mt["config"]).synthesize(C.Q4_0, 3)
+    plain = make_ctx(model, "step").decode_greedy(5, 0, 4)
+    ctx = make_ctx(model, "step")
+    with pytest.raises(mlb.MlbError, match="tracing is off"):
+        ctx.step_trace_read()
+    ctx.step_trace(True)
+    ids, tok = [], 5
+    for pos in range(4):
+        tok = ctx.decode_greedy(tok, pos, 1)[-1]
+        ids.append(tok)
+        t = ctx.step_trace_read().astype(np.int64)
+        assert t.shape[0] == 5 * mt["config"]["n_layers"] + 1 and t.shape[2] == 2
+        assert (t[:, :, 1] >= t[:, :, 0]).all()          # each phase ends after it starts
+        assert (t[1:, :, 0] >= t[:-1, :, 1]).all()       # and each CTA's phases in order
+    assert ids == plain
+    with pytest.raises(mlb.MlbError, match="no whole traced step"):
+        ctx.step_trace_read()
+    ctx.step_trace(False)
+    per_op = make_ctx(model, "per_op")
+    with pytest.raises(mlb.MlbError, match="not on the step kernel"):
+        per_op.step_trace(True)
+
+
 def test_step_kernel_decode_greedy_matches_forward(cuda):
     """The on-device greedy loop of the step kernel (position, token and step
     advanced by the kernel itself) against step-by-step host decoding."""

@@ -49,10 +49,13 @@ def test_two_rank_decode_matches_reference(name, path, tmp_path):
     assert res["device_greedy"] == res["gold"][n - 1:]     # free-running on the device
 
 
-@pytest.mark.parametrize("path", ["step", "per_op"])
-def test_tp_greedy_ids_match_one_gpu(path, tmp_path):
-    """Every available rank count (2, 4, 8): a 7B-shaped model (4 layers)
-    decoded greedily at TP=N gives the single-GPU ids; logits within the bar."""
+@pytest.mark.parametrize("path", ["step", "per_op", "batch"])
+@pytest.mark.parametrize("model", ["synth7b", "synth72b"])
+def test_tp_greedy_ids_match_one_gpu(model, path, tmp_path):
+    """Every available rank count (2, 4, 8): a 7B-shaped model (4 layers) and a
+    Qwen2-72B-shaped one (2 layers: Q4_1, bias, NeoX, GQA 8) decoded greedily
+    at TP=N give the single-GPU ids; logits within the bar. "batch": 8
+    sequences through the batched engine (tensor-core GEMMs)."""
     n = gpus()
     if n < 2:
         pytest.skip("needs 2 GPUs")
@@ -61,7 +64,7 @@ def test_tp_greedy_ids_match_one_gpu(path, tmp_path):
     cmd = ["timeout", "-k", "30", "400", sys.executable, "-m", "torch.distributed.run",
            "--nnodes=1", "--nproc-per-node", str(world), "--master-addr", "127.0.0.1",
            "--master-port", str(free_port()), os.path.join(ROOT, "tests", "tp_worker.py"),
-           "synth7b", str(out), path]
+           model, str(out), path]
     r = subprocess.run(cmd, cwd=ROOT, capture_output=True, text=True)
     assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-4000:]
     res = json.loads(out.read_text())

@@ -21,14 +21,23 @@ import mini_llama_b200 as mlb  # noqa: E402
 from mini_llama_b200 import configs as C  # noqa: E402
 
 
-def synth_vs_single(out, step_kernel, rank, world, local, nccl_id):
-    """A Llama-2-7B-shaped model cut to 4 layers (seeded on the device, so every
-    rank and the single-GPU copy hold the same weights): greedy ids at TP=world
-    against one GPU."""
-    cfg = dict(C.LLAMA2_7B, n_layers=4, max_seq_len=256)
+# Full-width shapes cut to a few layers, seeded on the device so every rank and
+# the single-GPU copy hold the same weights: (config, format, q/k/v bias).
+SYNTH = {
+    "synth7b": (dict(C.LLAMA2_7B, n_layers=4), C.Q4_0, False),
+    # Qwen2-72B width: NeoX RoPE, q/k/v bias, GQA 64/8, hidden 29568 (not a
+    # multiple of 256 per rank)
+    "synth72b": (dict(C.QWEN2_72B, n_layers=2), C.Q4_1, True),
+}
+
+
+def synth_vs_single(name, out, step_kernel, rank, world, local, nccl_id):
+    """Greedy ids of a SYNTH model at TP=world against one GPU."""
+    base, qt, bias = SYNTH[name]
+    cfg = dict(base, max_seq_len=256)
     steps = 48
     model = mlb.CudaModel(cfg, device_id=local, tp_rank=rank, tp_size=world, nccl_id=nccl_id)
-    model.synthesize(C.Q4_0, 77)
+    model.synthesize(qt, 77, with_bias=bias)
     ctx = model.context(step_kernel=step_kernel)
     tp_ids = ctx.decode_greedy(11, 0, steps)
     lg = ctx.forward_token(tp_ids[-1], steps)
@@ -37,7 +46,7 @@ def synth_vs_single(out, step_kernel, rank, world, local, nccl_id):
     model.close()
     dist.barrier()
     if rank == 0:
-        one = mlb.CudaModel(cfg, device_id=local).synthesize(C.Q4_0, 77)
+        one = mlb.CudaModel(cfg, device_id=local).synthesize(qt, 77, with_bias=bias)
         c1 = one.context()
         ids = c1.decode_greedy(11, 0, steps)
         l1 = c1.forward_token(ids[-1], steps)
@@ -46,6 +55,40 @@ def synth_vs_single(out, step_kernel, rank, world, local, nccl_id):
                        "max_err": float(np.abs(lg - l1).max())}, f)
         c1.close()
         one.close()
+    dist.barrier()
+
+
+def synth_batch_vs_single(name, out, rank, world, local, nccl_id):
+    """The batched engine at TP=world (tensor-core GEMMs on each rank's shard,
+    NCCL all-reduce after wo and w_down, vocab-sharded greedy keys) against one
+    GPU: 8 sequences of different seeded K/V lengths decoded in lockstep."""
+    base, qt, bias = SYNTH[name]
+    cfg = dict(base, max_seq_len=512)
+    n_seqs, steps = 8, 12
+    starts = [40 + 37 * s for s in range(n_seqs)]
+    toks = [11 + 101 * s for s in range(n_seqs)]
+
+    def run(model):
+        b = mlb.Batch(model, n_seqs)
+        for s in range(n_seqs):
+            b.fill_kv(s, starts[s], 5 + s)
+        ids = b.decode_greedy(toks, starts, steps)
+        _, lg = b.forward(list(range(n_seqs)), ids[-1], [p + steps for p in starts], logits=True)
+        b.close()
+        return ids, lg
+
+    model = mlb.CudaModel(cfg, device_id=local, tp_rank=rank, tp_size=world, nccl_id=nccl_id)
+    model.synthesize(qt, 77, with_bias=bias)
+    tp_ids, tp_lg = run(model)
+    model.close()
+    dist.barrier()
+    if rank == 0:
+        one = mlb.CudaModel(cfg, device_id=local).synthesize(qt, 77, with_bias=bias)
+        ids, lg = run(one)
+        one.close()
+        with open(out, "w") as f:
+            json.dump({"tp_ids": tp_ids.tolist(), "ids": ids.tolist(), "step_kernel": False,
+                       "max_err": float(np.abs(tp_lg - lg).max())}, f)
     dist.barrier()
 
 
@@ -58,8 +101,12 @@ def main():
     dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=120))
     obj = [mlb.nccl_unique_id() if rank == 0 else None]
     dist.broadcast_object_list(obj, src=0)
-    if name == "synth7b":
-        synth_vs_single(out, step_kernel, rank, world, local, obj[0])
+    if name in SYNTH and path == "batch":
+        synth_batch_vs_single(name, out, rank, world, local, obj[0])
+        dist.destroy_process_group()
+        return
+    if name in SYNTH:
+        synth_vs_single(name, out, step_kernel, rank, world, local, obj[0])
         dist.destroy_process_group()
         return
     golden = os.path.join(ROOT, "tests", "golden")
