@@ -316,6 +316,36 @@ int mlb_context_sync(mlb_context* c);
  * per step, no host round trip between steps. */
 int mlb_decode_greedy(mlb_context* c, int token, int pos, int n_steps,
                       int* tokens_host);
+
+/* -------------------------------------------------------------- sampling
+ * A sampler is MiniSampler (include/mini_llama/sampler.h): a std::mt19937
+ * seeded with `seed` (0 = a random seed, as the reference), its state
+ * resident on device_id. mlb_sample is MiniSampler::Sample
+ * (src/sampler.cc:172-183) over n logits in device memory: temperature <
+ * 1e-6 or top_k == 1 is greedy (first index of the maximum, no draw); top_k
+ * > 1 samples among the top_k largest logits (ties: lower index first);
+ * top_k == 0 among all. The generator's draws equal the reference's word for
+ * word; the softmax sums run on the device in a fixed order, so a sample
+ * differs from the reference's only when the uniform draw falls within
+ * rounding distance of a candidate boundary. Errors, with the reference's
+ * messages: empty logits, negative top_k, negative or non-finite temperature
+ * (before any device work), non-finite logits (after the sample, MLB_ERR_INVALID).
+ * top_k above 4096 (after clamping to n) is rejected: the device sorts at
+ * most 4096 candidates. mlb_sample syncs the sampler's own stream. */
+typedef struct mlb_sampler mlb_sampler;
+int mlb_sampler_create(int device_id, unsigned int seed, mlb_sampler** out);
+int mlb_sampler_destroy(mlb_sampler* s);
+int mlb_sample(mlb_sampler* s, const float* logits_dev, int n, float temperature, int top_k,
+               int* out_id);
+/* mlb_decode_greedy with the sampler's choice in place of the argmax at every
+ * step (RunGenerate's decode loop, src/main.cc:883-912, without the per-step logits
+ * download): one full-logits step and one sampling kernel per step, on the
+ * context's stream, with no host round trip between steps. Tensor-parallel
+ * ranks each pass a sampler seeded alike: every rank holds the whole logits
+ * row, so all draw and pick the same ids. The sampler must be on the
+ * context's device. */
+int mlb_decode_sample(mlb_context* c, mlb_sampler* s, float temperature, int top_k, int token,
+                      int pos, int n_steps, int* tokens_host);
 /* The context's stream (cudaStream_t), for timing with events. */
 void* mlb_context_stream(mlb_context* c);
 /* Number of kernels one decode step launches on this rank. */

@@ -26,7 +26,7 @@ ERR_TIMEOUT = -5  # MLB_ERR_TIMEOUT: a bounded device wait gave up
 
 __all__ = [
     "F32", "Q8_0", "Q4_0", "Q4_1", "ROPE_NORMAL", "ROPE_NEOX", "ATTN_CPU_COMPAT",
-    "ATTN_STANDARD", "MlbError", "MlbRangeError", "CudaQuantBuilt", "CudaDeviceCount",
+    "ATTN_STANDARD", "Sampler", "MlbError", "MlbRangeError", "CudaQuantBuilt", "CudaDeviceCount",
     "CudaQ80LinearDeviceInput", "CudaQ40LinearDeviceInput", "CudaQ41LinearDeviceInput",
     "CudaLinearDeviceInput", "CudaQ80Linear", "CudaQ40Linear", "CudaQ41Linear", "CudaLinear",
     "CudaRmsNormDeviceWeight", "CudaSiluDeviceInput", "CudaElementwiseMulDeviceInput",
@@ -457,6 +457,14 @@ class Context:
     def step_kernel(self) -> bool:
         return bool(lib().mlb_context_step_kernel(self.h))
 
+    def decode_sample(self, sampler: "Sampler", token: int, pos: int, n_steps: int,
+                      temperature: float = 0.0, top_k: int = 0) -> list:
+        """decode_greedy with the sampler's choice at every step (mlb_decode_sample)."""
+        out = np.empty(max(n_steps, 1), np.int32)
+        check(lib().mlb_decode_sample(self.h, sampler.h, float(temperature), int(top_k),
+                                      int(token), int(pos), int(n_steps), out.ctypes.data))
+        return [int(t) for t in out[:n_steps]]
+
     def step_trace(self, enable: bool):
         """Records per-phase times of later step-kernel steps (diagnostic)."""
         check(lib().mlb_context_step_trace(self.h, 1 if enable else 0))
@@ -521,6 +529,35 @@ class Context:
     def close(self):
         if getattr(self, "h", None):
             lib().mlb_context_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class Sampler:
+    """MiniSampler (include/mini_llama/sampler.h) on the device: a std::mt19937
+    seeded with `seed` (0: a random seed) whose state stays on device_id."""
+
+    def __init__(self, seed: int = 0, device_id: int = 0):
+        h = ctypes.c_void_p()
+        check(lib().mlb_sampler_create(int(device_id), int(seed), ctypes.byref(h)))
+        self.h = h
+        self.device_id = device_id
+
+    def sample(self, logits_ptr: int, n: int, temperature: float = 0.0, top_k: int = 0) -> int:
+        """MiniSampler::Sample over n fp32 logits at device address logits_ptr."""
+        out = ctypes.c_int(-1)
+        check(lib().mlb_sample(self.h, ctypes.c_void_p(logits_ptr), int(n), float(temperature),
+                               int(top_k), ctypes.byref(out)))
+        return out.value
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().mlb_sampler_destroy(self.h)
             self.h = None
 
     def __del__(self):

@@ -94,6 +94,10 @@ SIGNATURES = [
     ("mlb_context_step_trace_read", _c_int,
      [_vp, _vp, _c_size_t, ctypes.POINTER(_c_int), ctypes.POINTER(_c_int)]),
     ("mlb_nccl_unique_id", _c_int, [_vp]),
+    ("mlb_sampler_create", _c_int, [_c_int, ctypes.c_uint, ctypes.POINTER(_vp)]),
+    ("mlb_sampler_destroy", _c_int, [_vp]),
+    ("mlb_sample", _c_int, [_vp, _vp, _c_int, _c_float, _c_int, ctypes.POINTER(_c_int)]),
+    ("mlb_decode_sample", _c_int, [_vp, _vp, _c_float, _c_int, _c_int, _c_int, _c_int, _vp]),
     ("mlb_forward_batch", _c_int, [_vp, _c_int, _vp, _vp, _vp]),
     ("mlb_batch_create", _c_int, [_vp, _c_int, _c_int, ctypes.POINTER(_vp)]),
     ("mlb_batch_destroy", _c_int, [_vp]),

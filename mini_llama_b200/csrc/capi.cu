@@ -4,7 +4,10 @@
 // replaces (messages follow the reference's wording where its tests grep
 // them), turns exceptions into a status code plus a thread-local message, and
 // never falls back to a CPU implementation.
+#include <cmath>
 #include <cstring>
+#include <memory>
+#include <random>
 #include <string>
 #include <vector>
 
@@ -13,6 +16,7 @@
 #include "ops.cuh"
 #include "qgemm.cuh"
 #include "runtime.cuh"
+#include "sample.cuh"
 #include "synth.h"
 
 namespace mlb {
@@ -54,6 +58,9 @@ ContextImpl* context_create(ModelImpl& m, int mode);
 void context_step_async(ContextImpl& c, int token, int pos);
 void context_forward_token(ContextImpl& c, int token, int pos, float* logits_host);
 void context_decode_greedy(ContextImpl& c, int token, int pos, int n, int* tokens_host);
+void context_decode_sample(ContextImpl& c, MtState* st, int* st_out, DeviceStatus* st_status,
+                           float temperature, int top_k, int token, int pos, int n,
+                           int* tokens_host);
 void context_reset(ContextImpl& c);
 void context_fill_kv(ContextImpl& c, int n_pos, uint64_t seed, float scale);
 
@@ -580,6 +587,99 @@ int mlb_context_sync(mlb_context* c) {
     set_device(c->impl->m->device);
     MLB_CUDA(cudaStreamSynchronize(c->impl->stream));
     c->impl->check_status();
+  });
+}
+
+// ------------------------------------------------------------------ sampling
+
+struct mlb_sampler {
+  int device = 0;
+  mlb::DevBuf state;   // MtState
+  mlb::DevBuf out;     // int: the last sample
+  mlb::DevBuf status;  // DeviceStatus: a non-finite logit
+  cudaStream_t stream = nullptr;
+};
+
+namespace {
+
+// MiniSampler::Sample's parameter checks (src/sampler.cc:28-41, 175-178), on
+// the host; the finiteness of the logits is checked on the device.
+void validate_sampling(int n, float temperature, int top_k) {
+  if (n <= 0) mlb::invalid("sampler: cannot sample from empty logits");
+  if (top_k < 0) mlb::invalid("sampler: top_k must be non-negative");
+  if (!std::isfinite(temperature) || temperature < 0.0f)
+    mlb::invalid("Sampler: temperature must be finite and non-negative");
+  const bool greedy = temperature < 1e-6f || top_k == 1;
+  if (!greedy && top_k > 1 && std::min(top_k, n) > mlb::kSampleMaxTopK)
+    mlb::invalid("sampler: top_k above " + std::to_string(mlb::kSampleMaxTopK) +
+                 " is not sampled on the device");
+}
+
+void check_sampler_status(mlb_sampler* s) {
+  mlb::DeviceStatus st{};
+  MLB_CUDA(cudaMemcpy(&st, s->status.p, sizeof(st), cudaMemcpyDeviceToHost));
+  if (st.code != 0) {
+    MLB_CUDA(cudaMemset(s->status.p, 0, sizeof(st)));
+    mlb::invalid("sampler: logits must be finite");
+  }
+}
+
+}  // namespace
+
+int mlb_sampler_create(int device_id, unsigned int seed, mlb_sampler** out) {
+  return guarded([&] {
+    if (!out) invalid("mlb_sampler_create: null output");
+    *out = nullptr;
+    set_device(device_id);
+    auto s = std::make_unique<mlb_sampler>();
+    s->device = device_id;
+    if (seed == 0) seed = std::random_device{}();  // MiniSampler(0): a random seed
+    MtState h;
+    mt_seed(seed, &h);
+    s->state.alloc(sizeof(MtState));
+    MLB_CUDA(cudaMemcpy(s->state.p, &h, sizeof(MtState), cudaMemcpyHostToDevice));
+    s->out.alloc(sizeof(int));
+    s->status.alloc(sizeof(DeviceStatus));
+    MLB_CUDA(cudaMemset(s->status.p, 0, sizeof(DeviceStatus)));
+    MLB_CUDA(cudaStreamCreateWithFlags(&s->stream, cudaStreamNonBlocking));
+    *out = s.release();
+  });
+}
+
+int mlb_sampler_destroy(mlb_sampler* s) {
+  return guarded([&] {
+    if (!s) return;
+    set_device(s->device);
+    if (s->stream) cudaStreamDestroy(s->stream);
+    delete s;
+  });
+}
+
+int mlb_sample(mlb_sampler* s, const float* logits_dev, int n, float temperature, int top_k,
+               int* out_id) {
+  return guarded([&] {
+    if (!s || !out_id || (n > 0 && !logits_dev)) invalid("mlb_sample: null pointer");
+    validate_sampling(n, temperature, top_k);
+    set_device(s->device);
+    sample_launch(logits_dev, n, temperature, top_k, s->state.as<MtState>(), s->out.as<int>(),
+                  s->status.as<DeviceStatus>(), nullptr, nullptr, nullptr, s->stream);
+    MLB_CUDA(cudaMemcpyAsync(out_id, s->out.p, sizeof(int), cudaMemcpyDeviceToHost, s->stream));
+    MLB_CUDA(cudaStreamSynchronize(s->stream));
+    check_sampler_status(s);
+  });
+}
+
+int mlb_decode_sample(mlb_context* c, mlb_sampler* s, float temperature, int top_k, int token,
+                      int pos, int n_steps, int* tokens_host) {
+  return guarded([&] {
+    if (!c || !s || (n_steps > 0 && !tokens_host)) invalid("mlb_decode_sample: null pointer");
+    if (s->device != c->impl->m->device)
+      invalid("mlb_decode_sample: the sampler is on another device than the context");
+    validate_sampling(c->impl->m->cfg.vocab_size, temperature, top_k);
+    context_decode_sample(*c->impl, s->state.as<MtState>(), s->out.as<int>(),
+                          s->status.as<DeviceStatus>(), temperature, top_k, token, pos, n_steps,
+                          tokens_host);
+    check_sampler_status(s);
   });
 }
 

@@ -18,6 +18,7 @@
 // all-reduce combines before the residual add, and the vocabulary-sharded
 // lm_head logits are all-gathered.
 #include "runtime.cuh"
+#include "sample.cuh"
 
 #include <algorithm>
 #include <cstring>
@@ -1114,6 +1115,35 @@ void context_decode_greedy(ContextImpl& c, int token, int pos, int n, int* token
   c.h_scalars[2] = 0;
   MLB_CUDA(cudaMemcpyAsync(c.scalars.p, c.h_scalars, 3 * sizeof(int), cudaMemcpyHostToDevice, c.stream));
   for (int i = 0; i < n; ++i) c.replay(true);
+  MLB_CUDA(cudaMemcpyAsync(c.h_tokens, c.scalars.as<int>() + 4, (size_t)n * 4,
+                           cudaMemcpyDeviceToHost, c.stream));
+  MLB_CUDA(cudaStreamSynchronize(c.stream));
+  c.check_status();
+  std::memcpy(tokens_host, c.h_tokens, (size_t)n * 4);
+}
+
+// The step loop of context_decode_greedy with a device sample after each
+// step in place of the greedy id (the full-logits step, then sample_launch
+// over this rank's complete logits row, which rewrites the next input token
+// and the step's entry of the token record).
+void context_decode_sample(ContextImpl& c, MtState* st, int* st_out, DeviceStatus* st_status,
+                           float temperature, int top_k, int token, int pos, int n,
+                           int* tokens_host) {
+  if (n < 0) invalid("mlb_decode_sample: negative step count");
+  if (n == 0) return;
+  validate_step(c, token, pos);
+  if (pos + n > c.m->cfg.max_seq_len) out_of_range("ForwardToken position out of range");
+  set_device(c.m->device);
+  c.h_scalars[0] = token;
+  c.h_scalars[1] = pos;
+  c.h_scalars[2] = 0;
+  MLB_CUDA(cudaMemcpyAsync(c.scalars.p, c.h_scalars, 3 * sizeof(int), cudaMemcpyHostToDevice, c.stream));
+  int* d_token = c.scalars.as<int>();
+  for (int i = 0; i < n; ++i) {
+    c.replay(false);
+    sample_launch(c.logits_dev(), c.m->cfg.vocab_size, temperature, top_k, st, st_out, st_status,
+                  d_token, d_token + 4, d_token + 2, c.stream);
+  }
   MLB_CUDA(cudaMemcpyAsync(c.h_tokens, c.scalars.as<int>() + 4, (size_t)n * 4,
                            cudaMemcpyDeviceToHost, c.stream));
   MLB_CUDA(cudaStreamSynchronize(c.stream));

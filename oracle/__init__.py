@@ -245,6 +245,11 @@ class Ref(_Lib):
         L.ref_model_synthesize.argtypes = [_vp, ctypes.c_int, ctypes.c_uint64, ctypes.c_int,
                                            ctypes.c_int]
         L.ref_ctx_fill_kv.argtypes = [_vp, ctypes.c_int, ctypes.c_uint64, ctypes.c_float]
+        L.ref_sampler_create.argtypes = [ctypes.c_uint]
+        L.ref_sampler_create.restype = _vp
+        L.ref_sampler_destroy.argtypes = [_vp]
+        L.ref_sample.argtypes = [_vp, _f, ctypes.c_int, ctypes.c_float, ctypes.c_int,
+                                 ctypes.POINTER(ctypes.c_int)]
 
     def set_threads(self, n):
         self.lib.ref_set_threads(n)
@@ -254,6 +259,31 @@ class Ref(_Lib):
 
     def model(self, cfg):
         return RefModel(self, cfg)
+
+    def sampler(self, seed):
+        return RefSampler(self, seed)
+
+
+class RefSampler:
+    """A MiniSampler (src/sampler.cc) in the reference's own code."""
+
+    def __init__(self, ref: Ref, seed: int):
+        self.ref = ref
+        self.h = ref.lib.ref_sampler_create(int(seed))
+        if not self.h:
+            raise RuntimeError(ref.lib.ref_last_error().decode())
+
+    def sample(self, logits, temperature, top_k):
+        x = np.ascontiguousarray(logits, np.float32)
+        out = ctypes.c_int(-1)
+        self.ref._check(self.ref.lib.ref_sample(self.h, _fptr(x), x.size, float(temperature),
+                                                int(top_k), ctypes.byref(out)))
+        return out.value
+
+    def __del__(self):
+        if getattr(self, "h", None):
+            self.ref.lib.ref_sampler_destroy(self.h)
+            self.h = None
 
 
 class RefModel:

@@ -8,13 +8,14 @@
 // here calls the reference's public C++ API: LinearQ80/Q40/Q41 and Linear
 // (include/mini_llama/ops.h, quant.h), Dequantize*/Quantize* (quant.h),
 // RmsNorm/Softmax/SwiGlu/Rope/ArgMax (ops.h), and ForwardToken on a
-// MiniLlamaModel with cuda_weights == nullptr (forward.h:11) and SetThreadCount
-// (thread_pool.h:10).
+// MiniLlamaModel with cuda_weights == nullptr (forward.h:11), SetThreadCount
+// (thread_pool.h:10) and MiniSampler (sampler.h).
 #include "mini_llama/context.h"
 #include "mini_llama/forward.h"
 #include "mini_llama/model.h"
 #include "mini_llama/ops.h"
 #include "mini_llama/quant.h"
+#include "mini_llama/sampler.h"
 #include "mini_llama/thread_pool.h"
 
 #include <algorithm>
@@ -429,6 +430,32 @@ int ref_forward_token(void* ch, int token, int pos, float* logits) {
     c->ctx->pos = pos;
     Tensor out = ForwardToken(*c->ctx, c->m->model, token);
     std::memcpy(logits, out.data.data(), out.data.size() * sizeof(float));
+    return 0;
+  } catch (const std::exception& e) {
+    return Fail(e);
+  }
+}
+
+// MiniSampler(seed) and MiniSampler::Sample (src/sampler.cc:89-183).
+void* ref_sampler_create(unsigned int seed) {
+  try {
+    return new MiniSampler(seed);
+  } catch (const std::exception& e) {
+    Fail(e);
+    return nullptr;
+  }
+}
+
+void ref_sampler_destroy(void* s) { delete static_cast<MiniSampler*>(s); }
+
+int ref_sample(void* s, const float* logits, int n, float temperature, int top_k, int* out) {
+  try {
+    Tensor t(std::vector<int>{n});
+    std::memcpy(t.data.data(), logits, (size_t)n * sizeof(float));
+    SamplingParams p;
+    p.temperature = temperature;
+    p.top_k = top_k;
+    *out = static_cast<MiniSampler*>(s)->Sample(t, p);
     return 0;
   } catch (const std::exception& e) {
     return Fail(e);

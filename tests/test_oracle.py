@@ -230,3 +230,51 @@ def test_reference_kv_fill_is_deterministic(ref):
     assert not np.array_equal(outs[0], m.forward_token(7, 20))
     with pytest.raises(IndexError):
         m.fill_kv(33, 1)
+
+
+def test_reference_sampler_reproduces_golden(ref):
+    """oracle/_ref's MiniSampler (src/sampler.cc) gives the recorded ids."""
+    import json
+    import os
+    import sys
+
+    here = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+    sys.path.insert(0, here)
+    from sampler_cases import CASES, logits_rows
+
+    with open(os.path.join(here, "sampler.json")) as f:
+        want = json.load(f)
+    for case in CASES:
+        s = ref.sampler(case["seed"])
+        got = [s.sample(r, case["temperature"], case["top_k"]) for r in logits_rows(case)]
+        assert got == want[case["name"]], case["name"]
+
+
+def test_reference_sampler_uniform_draws(ref):
+    """The draw the device sampler restates: uniform_real_distribution<float>
+    over std::mt19937 is float(u) / 2^32 of one 32-bit word (numpy's legacy
+    RandomState is the same generator). Two equal logits at temperature 1 pick
+    index 0 exactly when that draw is below 0.5."""
+    import numpy as np
+
+    seed, n = 12345, 2000
+    u = np.random.RandomState(seed).randint(0, 2**32, size=n, dtype=np.uint32)
+    r = u.astype(np.float32) * np.float32(2.0**-32)
+    s = ref.sampler(seed)
+    zeros = np.zeros(2, np.float32)
+    got = [s.sample(zeros, 1.0, 0) for _ in range(n)]
+    assert got == [0 if x < 0.5 else 1 for x in r]
+
+
+def test_reference_sampler_errors(ref):
+    import numpy as np
+
+    s = ref.sampler(1)
+    x = np.zeros(8, np.float32)
+    for t, k, msg in ((-1.0, 0, "temperature"), (1.0, -2, "top_k"),
+                      (float("inf"), 0, "temperature")):
+        with pytest.raises(RuntimeError, match=msg):
+            s.sample(x, t, k)
+    x[3] = np.nan
+    with pytest.raises(RuntimeError, match="finite"):
+        s.sample(x, 1.0, 0)
