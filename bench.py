@@ -432,7 +432,7 @@ def measure_workload(torch, mlb, dist, args, name, cfg, qtype, bias, rank, world
     stream = torch.cuda.ExternalStream(ctx.stream())
     tok0 = C.prompt_ids(SEED, 1, cfg["vocab_size"])[0]
     ctx0 = args.ctx
-    if ctx0 + warmup + 2 * steps + 2 > cfg["max_seq_len"]:
+    if ctx0 + warmup + 3 * steps + 12 > cfg["max_seq_len"]:
         raise SystemExit("context too long for max_seq_len")
     ctx.fill_kv(ctx0, KV_SEED, KV_SCALE)
     ids = ctx.decode_greedy(tok0, ctx0, warmup) if warmup else []
@@ -471,6 +471,21 @@ def measure_workload(torch, mlb, dist, args, name, cfg, qtype, bias, rank, world
     torch.cuda.synchronize()
     barrier()
     e2e_ms = max_over_ranks(e0.elapsed_time(e1))
+    # the on-device sampling loop (mlb_decode_sample, temperature 0.8, top-k
+    # 40): the same step plus one sampling kernel per step, same clock rules
+    sampler = mlb.Sampler(SEED, device_id=local)
+    ctx.decode_sample(sampler, tok, pos, 2, 0.8, 40)
+    pos += 2
+    barrier()
+    s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s0.record(stream)
+    tok = ctx.decode_sample(sampler, tok, pos, steps, 0.8, 40)[-1]
+    s1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    pos += steps
+    sample_ms = max_over_ranks(s0.elapsed_time(s1))
+    sampler.close()
     kpl = ctx.kernels_per_step()
     phases = step_phase_summary(ctx, tok, pos, cfg["n_layers"]) if step_kernel else None
     ctx.close()
@@ -518,6 +533,9 @@ def measure_workload(torch, mlb, dist, args, name, cfg, qtype, bias, rank, world
         "roofline": roof, "kernels_per_step": kpl, "step_kernel": step_kernel,
         "resident_bytes": resident, "step_weight_bytes": step_weights, "tp_check": tp_check,
         "gpu_launches": kpl * steps, "step_phases": phases,
+        "decode_sample": {"value": steps / (sample_ms / 1e3), "unit": "tok/s",
+                          "temperature": 0.8, "top_k": 40,
+                          "api": "mlb_decode_sample (device sampling, ids to host at the end)"},
     }
 
 
@@ -572,18 +590,31 @@ def measure_batch(torch, mlb, dist, args, name, cfg, qtype, bias, B, ctx0, rank,
     model.close()
     check = None
     if rank == 0:
+        # Teacher-forced: one GPU's single-sequence step kernel is fed the
+        # batch's own ids, and its argmax at every step must be the batch's
+        # next id. Where it is not, the step kernel's top-2 margin there is
+        # recorded (two GPU paths summing in different orders can part on a
+        # near tie without either leaving the logits bar).
         n = min(N_CHECK, len(ids))
         one = (mlb.CudaModel(cfg, device_id=local).synthesize(qtype, SEED, with_bias=bias))
         c1 = one.context(mlb.ATTN_CPU_COMPAT)
-        ok = True
+        mism = []
         for s in (0, B - 1):
             c1.reset()
             c1.fill_kv(ctx0, KV_SEED + s, KV_SCALE)
-            ok = ok and c1.decode_greedy(toks[s], ctx0, n) == [int(v) for v in ids[:n, s]]
+            tok = toks[s]
+            for t in range(n):
+                lg = c1.forward_token(tok, ctx0 + t)
+                top = np.argsort(lg)[-2:]
+                if int(top[-1]) != int(ids[t, s]):
+                    mism.append({"seq": s, "step": t, "margin": float(lg[top[-1]] - lg[top[-2]])})
+                tok = int(ids[t, s])
         c1.close()
         one.close()
-        check = {"seq_ids_match": ok, "sequences": [0, B - 1], "n": n,
-                 "against": "one GPU's single-sequence step kernel from the same seeded state"}
+        check = {"seq_ids_match": not mism, "sequences": [0, B - 1], "n": n,
+                 "mismatches": mism,
+                 "against": "one GPU's single-sequence step kernel, teacher-forced on the "
+                            "batch's ids from the same seeded state"}
     barrier()
     kv_per_pos = 2 * cfg["n_layers"] * (cfg["n_kv_heads"] // world) * cfg["head_dim"] * 4
     mid_ctx = ctx0 + warmup + steps / 2
@@ -701,6 +732,7 @@ def run_gpu(args, cfg, qtype, bias, rank, world, local):
             "kernels_per_step": head["kernels_per_step"],
             "resident_bytes": head["resident_bytes"],
             "step_phases": head["step_phases"],
+            "decode_sample": head["decode_sample"],
         }
         if gemv_roof:
             line["gemv_roofline"] = gemv_roof

@@ -124,9 +124,9 @@ struct BatchEngine {
     staged.alloc((size_t)chunks * tc_chunk_bytes(tc_mp(rows)));
     tc_parts.alloc(parts * 4);
     tc_cnt.alloc((size_t)cnt * 4);
-    MLB_CUDA(cudaMemset(tc_cnt.p, 0, tc_cnt.bytes));
+    zero_now(tc_cnt.p, tc_cnt.bytes);
     status.alloc(sizeof(DeviceStatus));
-    MLB_CUDA(cudaMemset(status.p, 0, status.bytes));
+    zero_now(status.p, status.bytes);
     tcws.partials = tc_parts.as<float>();
     tcws.partial_floats = parts;
     tcws.counters = tc_cnt.as<int>();
@@ -139,13 +139,13 @@ struct BatchEngine {
                                        (c.max_seq_len + 63) / 64));
     attn_ws.alloc(attn_ws_floats(m->q_heads, m->kv_heads, D, attn_nsplit) * rows * 4);
     attn_cnt.alloc((size_t)rows * m->kv_heads * 4);
-    MLB_CUDA(cudaMemset(attn_cnt.p, 0, attn_cnt.bytes));
+    zero_now(attn_cnt.p, attn_cnt.bytes);
     rows_dev.alloc((size_t)3 * rows * 4);
-    MLB_CUDA(cudaMemset(rows_dev.p, 0, rows_dev.bytes));
+    zero_now(rows_dev.p, rows_dev.bytes);
     keys_dev.alloc((size_t)rows * 8);
-    MLB_CUDA(cudaMemset(keys_dev.p, 0, keys_dev.bytes));
+    zero_now(keys_dev.p, keys_dev.bytes);
     step_dev.alloc(4);
-    MLB_CUDA(cudaMemset(step_dev.p, 0, 4));
+    zero_now(step_dev.p, 4);
   }
 
   // The kernels of one pass of `rows` rows on stream s (rows_dev filled).
@@ -281,10 +281,10 @@ struct BatchEngine {
     DeviceStatus st{};
     MLB_CUDA(cudaMemcpy(&st, status.p, sizeof(st), cudaMemcpyDeviceToHost));
     if (st.code != 0) {
-      MLB_CUDA(cudaMemset(tc_cnt.p, 0, tc_cnt.bytes));
-      MLB_CUDA(cudaMemset(attn_cnt.p, 0, attn_cnt.bytes));
-      MLB_CUDA(cudaMemset(keys_dev.p, 0, keys_dev.bytes));
-      MLB_CUDA(cudaMemset(status.p, 0, sizeof(st)));
+      zero_now(tc_cnt.p, tc_cnt.bytes);
+      zero_now(attn_cnt.p, attn_cnt.bytes);
+      zero_now(keys_dev.p, keys_dev.bytes);
+      zero_now(status.p, sizeof(st));
       fail(st.code, "batched step: a device-side check failed (site " + std::to_string(st.where) +
                         ")");
     }
@@ -350,8 +350,8 @@ BatchImpl* batch_create(ModelImpl& m, int n_seqs, int mode) {
   const size_t kv = (size_t)n_seqs * b->seq_stride * 4;
   b->keys.alloc(kv);
   b->values.alloc(kv);
-  MLB_CUDA(cudaMemset(b->keys.p, 0, kv));
-  MLB_CUDA(cudaMemset(b->values.p, 0, kv));
+  zero_now(b->keys.p, kv);
+  zero_now(b->values.p, kv);
   b->eng.init(&m, n_seqs, mode);
   MLB_CUDA(cudaMallocHost(&b->h_rows, 3 * kTcMaxMp * sizeof(int)));
   return b.release();

@@ -37,6 +37,16 @@ void set_device(int device_id) {
   MLB_CUDA(cudaSetDevice(device_id));
 }
 
+void zero_now(void* p, size_t bytes) {
+  MLB_CUDA(cudaMemset(p, 0, bytes));
+  MLB_CUDA(cudaStreamSynchronize(cudaStreamLegacy));
+}
+
+void copy_to_device_now(void* dst, const void* src, size_t bytes) {
+  MLB_CUDA(cudaMemcpy(dst, src, bytes, cudaMemcpyHostToDevice));
+  MLB_CUDA(cudaStreamSynchronize(cudaStreamLegacy));
+}
+
 int sm_count(int device_id) {
   static int cache[64] = {};
   if (device_id >= 0 && device_id < 64 && cache[device_id]) return cache[device_id];
@@ -169,7 +179,7 @@ int mlb_linear_host(int qtype, const float* x, int rows, int in_features, const 
     if (!x || !w || !y) invalid(std::string(linear_caller(qtype)) + ": null host pointer");
     set_device(device_id);
     DevBuf wd(weight_bytes(qtype, out_features, in_features));
-    MLB_CUDA(cudaMemcpy(wd.p, w, wd.bytes, cudaMemcpyHostToDevice));
+    copy_to_device_now(wd.p, w, wd.bytes);
     linear_host_common(qtype, x, rows, in_features, wd.p, out_features, bias, y, nullptr);
   });
 }
@@ -338,9 +348,9 @@ static void qmatrix_ws(mlb_qmatrix& h) {
   size_t pf = (size_t)h.q.ntiles * std::max(h.q.nchunks, 1) * 16 * kMaxBatch;
   h.wsbuf.alloc(pf * 4);
   h.cnt.alloc((size_t)h.q.ntiles * 4);
-  MLB_CUDA(cudaMemset(h.cnt.p, 0, h.cnt.bytes));
+  zero_now(h.cnt.p, h.cnt.bytes);
   h.status.alloc(sizeof(DeviceStatus));
-  MLB_CUDA(cudaMemset(h.status.p, 0, h.status.bytes));
+  zero_now(h.status.p, h.status.bytes);
   h.ws.partials = h.wsbuf.as<float>();
   h.ws.partial_floats = pf;
   h.ws.counters = h.cnt.as<int>();
@@ -366,7 +376,7 @@ int mlb_qmatrix_create(int qtype, const void* w, int w_is_host, int out_features
     DevBuf tmp;
     if (w_is_host) {
       tmp.alloc(pitch * (size_t)out_features);
-      MLB_CUDA(cudaMemcpy(tmp.p, w, tmp.bytes, cudaMemcpyHostToDevice));
+      copy_to_device_now(tmp.p, w, tmp.bytes);
       src = tmp.as<uint8_t>();
     }
     qmatrix_repack(h->q, src, pitch, nullptr, 0, nullptr);
@@ -426,7 +436,7 @@ static void qmatrix_tc_ws(mlb_qmatrix& h) {
   h.tc_parts.alloc(pf * 4);
   const int nc = tc_counter_count(h.q);
   h.tc_cnt.alloc((size_t)nc * 4);
-  MLB_CUDA(cudaMemset(h.tc_cnt.p, 0, h.tc_cnt.bytes));
+  zero_now(h.tc_cnt.p, h.tc_cnt.bytes);
   h.tcws.partials = h.tc_parts.as<float>();
   h.tcws.partial_floats = pf;
   h.tcws.counters = h.tc_cnt.as<int>();
@@ -619,7 +629,7 @@ void check_sampler_status(mlb_sampler* s) {
   mlb::DeviceStatus st{};
   MLB_CUDA(cudaMemcpy(&st, s->status.p, sizeof(st), cudaMemcpyDeviceToHost));
   if (st.code != 0) {
-    MLB_CUDA(cudaMemset(s->status.p, 0, sizeof(st)));
+    zero_now(s->status.p, sizeof(st));
     mlb::invalid("sampler: logits must be finite");
   }
 }
@@ -637,10 +647,10 @@ int mlb_sampler_create(int device_id, unsigned int seed, mlb_sampler** out) {
     MtState h;
     mt_seed(seed, &h);
     s->state.alloc(sizeof(MtState));
-    MLB_CUDA(cudaMemcpy(s->state.p, &h, sizeof(MtState), cudaMemcpyHostToDevice));
+    copy_to_device_now(s->state.p, &h, sizeof(MtState));
     s->out.alloc(sizeof(int));
     s->status.alloc(sizeof(DeviceStatus));
-    MLB_CUDA(cudaMemset(s->status.p, 0, sizeof(DeviceStatus)));
+    zero_now(s->status.p, sizeof(DeviceStatus));
     MLB_CUDA(cudaStreamCreateWithFlags(&s->stream, cudaStreamNonBlocking));
     *out = s.release();
   });

@@ -54,6 +54,17 @@ int guarded(F&& f) {
 // Selects `device_id` for the calling thread (CudaSetDevice, src/cuda_runtime.cc).
 void set_device(int device_id);
 
+// Zeroes `bytes` of device memory and waits until it is done. cudaMemset runs
+// on the legacy default stream, which the library's non-blocking streams are
+// not ordered against: without the wait a large clear (a KV cache) can still
+// be running when a kernel on another stream writes the same bytes.
+void zero_now(void* p, size_t bytes);
+
+// Copies host memory to the device and waits until the bytes have landed
+// (cudaMemcpy from pageable memory may return before its DMA has finished, on
+// the legacy stream that the library's streams are not ordered against).
+void copy_to_device_now(void* dst, const void* src, size_t bytes);
+
 // Device-side error word: kernels that give up a bounded wait record where.
 struct DeviceStatus {
   int code;  // 0 = ok, else MLB_ERR_TIMEOUT

@@ -199,7 +199,7 @@ ModelImpl* model_create(const mlb_config* cfg, int device, int rank, int size,
   std::vector<float2> tab((size_t)c.max_seq_len * (c.head_dim / 2));
   rope_table_host(c.rope_theta, c.head_dim, 0, c.max_seq_len, tab.data());
   m->rope.alloc(tab.size() * sizeof(float2));
-  MLB_CUDA(cudaMemcpy(m->rope.p, tab.data(), tab.size() * sizeof(float2), cudaMemcpyHostToDevice));
+  copy_to_device_now(m->rope.p, tab.data(), tab.size() * sizeof(float2));
   if (size > 1) {
     if (!nccl_id) invalid("mlb_model_create: tensor parallelism needs an NCCL id");
     ncclUniqueId id;
@@ -250,15 +250,15 @@ void model_set_weight(ModelImpl& m, int kind, int layer, int qtype, int rows, in
     t.cols = nc;
     t.pitch = (size_t)nc * 4;
     t.buf.alloc(t.pitch);
-    MLB_CUDA(cudaMemcpy(t.buf.p, static_cast<const float*>(data) + c0, t.pitch, cudaMemcpyHostToDevice));
+    copy_to_device_now(t.buf.p, static_cast<const float*>(data) + c0, t.pitch);
   } else {
     shard_rows(m, kind, rows, &r0, &nr);
     t.rows = nr;
     t.cols = cols;
     t.pitch = pitch;
     t.buf.alloc(pitch * (size_t)nr);
-    MLB_CUDA(cudaMemcpy(t.buf.p, static_cast<const uint8_t*>(data) + pitch * (size_t)r0,
-                        pitch * (size_t)nr, cudaMemcpyHostToDevice));
+    copy_to_device_now(t.buf.p, static_cast<const uint8_t*>(data) + pitch * (size_t)r0,
+                        pitch * (size_t)nr);
   }
   put_pending(m, kind, layer, std::move(t));
 }
@@ -495,8 +495,8 @@ ContextImpl* context_create(ModelImpl& m, int mode) {
   const size_t kv = (size_t)cf.n_layers * cf.max_seq_len * m.kv_heads * cf.head_dim * 4;
   c->keys.alloc(kv);
   c->values.alloc(kv);
-  MLB_CUDA(cudaMemset(c->keys.p, 0, kv));
-  MLB_CUDA(cudaMemset(c->values.p, 0, kv));
+  zero_now(c->keys.p, kv);
+  zero_now(c->values.p, kv);
   c->xa.alloc((size_t)cf.dim * 4);
   c->xb.alloc((size_t)cf.dim * 4);
   c->y.alloc((size_t)cf.dim * 4);
@@ -517,9 +517,9 @@ ContextImpl* context_create(ModelImpl& m, int mode) {
   upd(m.lm_head);
   c->gemv_ws.alloc(pf * 4);
   c->gemv_cnt.alloc(nt * 4);
-  MLB_CUDA(cudaMemset(c->gemv_cnt.p, 0, nt * 4));
+  zero_now(c->gemv_cnt.p, nt * 4);
   c->status.alloc(sizeof(DeviceStatus));
-  MLB_CUDA(cudaMemset(c->status.p, 0, sizeof(DeviceStatus)));
+  zero_now(c->status.p, sizeof(DeviceStatus));
   c->ws.partials = c->gemv_ws.as<float>();
   c->ws.partial_floats = pf;
   c->ws.counters = c->gemv_cnt.as<int>();
@@ -528,12 +528,12 @@ ContextImpl* context_create(ModelImpl& m, int mode) {
   c->attn_splits = attn_splits(m.kv_heads, sm_count(m.device), cf.max_seq_len);
   c->attn_ws.alloc(attn_ws_floats(m.q_heads, m.kv_heads, cf.head_dim, c->attn_splits) * 4);
   c->attn_cnt.alloc((size_t)m.kv_heads * 4);
-  MLB_CUDA(cudaMemset(c->attn_cnt.p, 0, (size_t)m.kv_heads * 4));
+  zero_now(c->attn_cnt.p, (size_t)m.kv_heads * 4);
   // scalars: [0] token, [1] pos, [2] step, [3] spare, then tokens[max_seq]
   c->scalars.alloc((size_t)(4 + cf.max_seq_len) * 4);
-  MLB_CUDA(cudaMemset(c->scalars.p, 0, c->scalars.bytes));
+  zero_now(c->scalars.p, c->scalars.bytes);
   c->argmax_key.alloc(sizeof(unsigned long long));
-  MLB_CUDA(cudaMemset(c->argmax_key.p, 0, sizeof(unsigned long long)));
+  zero_now(c->argmax_key.p, sizeof(unsigned long long));
   MLB_CUDA(cudaMallocHost(&c->h_scalars, 4 * sizeof(int)));
   MLB_CUDA(cudaMallocHost(&c->h_logits, (size_t)cf.vocab_size * 4));
   MLB_CUDA(cudaMallocHost(&c->h_tokens, (size_t)cf.max_seq_len * 4));
@@ -723,18 +723,16 @@ void ContextImpl::plan_step() {
 
   if ((int)ph.size() != nph) fail(MLB_ERR_INVALID, "decode step kernel: phase count mismatch");
   step_phases.alloc(ph.size() * sizeof(StepPhase));
-  MLB_CUDA(cudaMemcpy(step_phases.p, ph.data(), ph.size() * sizeof(StepPhase),
-                      cudaMemcpyHostToDevice));
+  copy_to_device_now(step_phases.p, ph.data(), ph.size() * sizeof(StepPhase));
   const std::vector<StepCta> tab = step_cta_table(ph, grid);
   step_cta.alloc(tab.size() * sizeof(StepCta));
-  MLB_CUDA(cudaMemcpy(step_cta.p, tab.data(), tab.size() * sizeof(StepCta),
-                      cudaMemcpyHostToDevice));
+  copy_to_device_now(step_cta.p, tab.data(), tab.size() * sizeof(StepCta));
   step_sync.alloc(2 * sizeof(unsigned int));
-  MLB_CUDA(cudaMemset(step_sync.p, 0, step_sync.bytes));
+  zero_now(step_sync.p, step_sync.bytes);
   const int gq = m->q_heads / m->kv_heads;
   step_attn_ws.alloc((size_t)std::max(grid, m->kv_heads) * gq * (D + 4) * 4);  // one record per item
   step_attn_cnt.alloc((size_t)m->kv_heads * 4);
-  MLB_CUDA(cudaMemset(step_attn_cnt.p, 0, step_attn_cnt.bytes));
+  zero_now(step_attn_cnt.p, step_attn_cnt.bytes);
   step.ok = true;
   step.qtype = qt;
   step.gq = gq;
@@ -804,12 +802,11 @@ void ContextImpl::setup_tp_exchange() {
   x.kflags_off = al(x.keys_off + (long long)n * 8);
   const long long total = al(x.kflags_off + (long long)n * 4);
   xchg.alloc((size_t)total);
-  MLB_CUDA(cudaMemset(xchg.p, 0, (size_t)total));
+  zero_now(xchg.p, (size_t)total);
   cudaIpcMemHandle_t h;
   MLB_CUDA(cudaIpcGetMemHandle(&h, xchg.p));
   DevBuf hb((size_t)n * sizeof(h));
-  MLB_CUDA(cudaMemcpy(hb.as<uint8_t>() + (size_t)me * sizeof(h), &h, sizeof(h),
-                      cudaMemcpyHostToDevice));
+  copy_to_device_now(hb.as<uint8_t>() + (size_t)me * sizeof(h), &h, sizeof(h));
   MLB_NCCL(ncclAllGather(hb.as<uint8_t>() + (size_t)me * sizeof(h), hb.p, sizeof(h), ncclChar,
                          m->comm, stream));
   MLB_CUDA(cudaStreamSynchronize(stream));
@@ -827,9 +824,9 @@ void ContextImpl::setup_tp_exchange() {
   }
   tpx = x;
   tp_desc.alloc(sizeof(TpXchg));
-  MLB_CUDA(cudaMemcpy(tp_desc.p, &x, sizeof(TpXchg), cudaMemcpyHostToDevice));
+  copy_to_device_now(tp_desc.p, &x, sizeof(TpXchg));
   tp_gen.alloc(2 * sizeof(unsigned int));
-  MLB_CUDA(cudaMemset(tp_gen.p, 0, 2 * sizeof(unsigned int)));
+  zero_now(tp_gen.p, 2 * sizeof(unsigned int));
   // every rank's buffer is zeroed and mapped before any rank's first step
   MLB_NCCL(ncclAllReduce(hb.p, hb.p, 1, ncclChar, ncclMax, m->comm, stream));
   MLB_CUDA(cudaStreamSynchronize(stream));
@@ -1043,7 +1040,7 @@ void ContextImpl::set_step_trace(bool on) {
   set_device(m->device);
   MLB_CUDA(cudaStreamSynchronize(stream));
   if (on && !step_trace.p) step_trace.alloc((size_t)step.nphases * step.grid * 2 * 8);
-  if (on) MLB_CUDA(cudaMemset(step_trace.p, 0, step_trace.bytes));
+  if (on) zero_now(step_trace.p, step_trace.bytes);
   trace_on = on;
   build_graph();
 }
@@ -1058,7 +1055,7 @@ void ContextImpl::read_step_trace(unsigned long long* stamps, size_t cap, int* n
   set_device(m->device);
   MLB_CUDA(cudaStreamSynchronize(stream));
   MLB_CUDA(cudaMemcpy(stamps, step_trace.p, step_trace.bytes, cudaMemcpyDeviceToHost));
-  MLB_CUDA(cudaMemset(step_trace.p, 0, step_trace.bytes));
+  zero_now(step_trace.p, step_trace.bytes);
   for (size_t i = 0; i < n; ++i)
     if (stamps[i] == 0ull)
       invalid("mlb_context_step_trace_read: no whole traced step since the last read");
@@ -1069,12 +1066,12 @@ void ContextImpl::check_status() {
   MLB_CUDA(cudaMemcpy(&st, status.p, sizeof(st), cudaMemcpyDeviceToHost));
   if (st.code != 0) {
     // a failed step may leave arrival counters and the argmax key mid-way
-    MLB_CUDA(cudaMemset(gemv_cnt.p, 0, gemv_cnt.bytes));
-    MLB_CUDA(cudaMemset(attn_cnt.p, 0, attn_cnt.bytes));
-    MLB_CUDA(cudaMemset(argmax_key.p, 0, argmax_key.bytes));
-    if (step_sync.p) MLB_CUDA(cudaMemset(step_sync.p, 0, step_sync.bytes));
-    if (step_attn_cnt.p) MLB_CUDA(cudaMemset(step_attn_cnt.p, 0, step_attn_cnt.bytes));
-    MLB_CUDA(cudaMemset(status.p, 0, sizeof(st)));
+    zero_now(gemv_cnt.p, gemv_cnt.bytes);
+    zero_now(attn_cnt.p, attn_cnt.bytes);
+    zero_now(argmax_key.p, argmax_key.bytes);
+    if (step_sync.p) zero_now(step_sync.p, step_sync.bytes);
+    if (step_attn_cnt.p) zero_now(step_attn_cnt.p, step_attn_cnt.bytes);
+    zero_now(status.p, sizeof(st));
     fail(st.code, "decode step: a device-side check failed (site " + std::to_string(st.where) + ")");
   }
 }

@@ -155,6 +155,41 @@ __device__ int block_min_i(int v, int* sw) {
   return t;
 }
 
+// Every thread visits i = tid, tid + 1024, ... < n, loading 8 of its values
+// before using any (one CTA streams the whole row several times, so each
+// thread keeps several loads in flight). f(v, i, valid) is called by every
+// lane of a warp the same number of times (valid false past n), so it may
+// use warp-wide primitives.
+constexpr int kBatch = 8;
+template <class F>
+__device__ __forceinline__ void for_strided(const float* __restrict__ x, int n, F f) {
+  for (int base = threadIdx.x - (threadIdx.x & 31); base < n; base += kBatch * kSampleThreads) {
+    float v[kBatch];
+#pragma unroll
+    for (int j = 0; j < kBatch; ++j) {
+      const int i = base + j * kSampleThreads + (threadIdx.x & 31);
+      v[j] = i < n ? __ldcg(x + i) : 0.0f;
+    }
+#pragma unroll
+    for (int j = 0; j < kBatch; ++j) {
+      const int i = base + j * kSampleThreads + (threadIdx.x & 31);
+      f(v[j], i, i < n);
+    }
+  }
+}
+// The same over this thread's contiguous range [lo, hi), in index order.
+template <class F>
+__device__ __forceinline__ void for_range(const float* __restrict__ x, int lo, int hi, F f) {
+  for (int base = lo; base < hi; base += kBatch) {
+    float v[kBatch];
+#pragma unroll
+    for (int j = 0; j < kBatch; ++j) v[j] = base + j < hi ? __ldcg(x + base + j) : 0.0f;
+#pragma unroll
+    for (int j = 0; j < kBatch; ++j)
+      if (base + j < hi) f(v[j], base + j);
+  }
+}
+
 // ------------------------------------------------------------------ kernel
 
 __global__ void __launch_bounds__(kSampleThreads, 1)
@@ -175,16 +210,16 @@ __global__ void __launch_bounds__(kSampleThreads, 1)
   float mx = -INFINITY;
   unsigned long long best = 0ull;
   int bad = 0;
-  for (int i = tid; i < n; i += kSampleThreads) {
-    const float v = logits[i];
+  for_strided(logits, n, [&](float v, int i, bool valid) {
+    if (!valid) return;
     if (!isfinite(v)) {
       bad = 1;
-      continue;
+      return;
     }
     mx = fmaxf(mx, v);
     const unsigned long long k = argmax_key_of(v, i);
     best = k > best ? k : best;
-  }
+  });
   bad = __syncthreads_or(bad);
   if (bad) {
     if (tid == 0 && atomicCAS(&status->code, 0, MLB_ERR_INVALID) == 0)
@@ -236,10 +271,18 @@ __global__ void __launch_bounds__(kSampleThreads, 1)
         for (int j = tid; j < kSampleWarps * 256; j += kSampleThreads) hist[j] = 0u;
         __syncthreads();
         const unsigned int prefix = s_prefix, mask = s_mask;
-        for (int i = tid; i < n; i += kSampleThreads) {
-          const unsigned int u = key_hi(argmax_key_of(logits[i], i));
-          if ((u & mask) == prefix) atomicAdd(&hist[warp * 256 + ((u >> shift) & 255u)], 1u);
-        }
+        // lanes of a warp that fall in the same bin add once (logits crowd
+        // into a few bins of the leading bytes)
+        for_strided(logits, n, [&](float v, int i, bool valid) {
+          const unsigned int u = valid ? key_hi(argmax_key_of(v, i)) : 0u;
+          const bool act = valid && (u & mask) == prefix;
+          const unsigned int am = __ballot_sync(0xffffffffu, act);
+          if (act) {
+            const unsigned int bin = (u >> shift) & 255u;
+            const unsigned int peers = __match_any_sync(am, bin);
+            if (lane == __ffs(peers) - 1) atomicAdd(&hist[warp * 256 + bin], __popc(peers));
+          }
+        });
         __syncthreads();
         if (tid < 256) {
           unsigned int t = 0;
@@ -268,20 +311,22 @@ __global__ void __launch_bounds__(kSampleThreads, 1)
       unsigned long long* cand = reinterpret_cast<unsigned long long*>(dyn);  // [kp]
       if (tid == 0) s_cnt = 0;
       __syncthreads();
-      for (int i = tid; i < n; i += kSampleThreads) {
-        const unsigned long long k = argmax_key_of(logits[i], i);
-        if (key_hi(k) > thr) cand[atomicAdd(&s_cnt, 1)] = k;
-      }
+      for_strided(logits, n, [&](float v, int i, bool valid) {
+        const unsigned long long k = argmax_key_of(v, i);
+        if (valid && key_hi(k) > thr) cand[atomicAdd(&s_cnt, 1)] = k;
+      });
       // the keys equal to the threshold: the first need_eq in index order
       const int chunk = (n + kSampleThreads - 1) / kSampleThreads;
       const int lo = min(n, tid * chunk), hi = min(n, lo + chunk);
       int c = 0;
-      for (int i = lo; i < hi; ++i) c += key_hi(argmax_key_of(logits[i], i)) == thr;
+      for_range(logits, lo, hi,
+                [&](float v, int i) { c += key_hi(argmax_key_of(v, i)) == thr; });
       int base = block_excl_scan(c, s_i);
-      for (int i = lo; i < hi && base < need_eq; ++i) {
-        const unsigned long long k = argmax_key_of(logits[i], i);
-        if (key_hi(k) == thr) cand[cnt_gt + base++] = k;
-      }
+      if (c > 0 && base < need_eq)
+        for_range(logits, lo, hi, [&](float v, int i) {
+          const unsigned long long k = argmax_key_of(v, i);
+          if (key_hi(k) == thr && base < need_eq) cand[cnt_gt + base++] = k;
+        });
       for (int j = kk + tid; j < kp; j += kSampleThreads) cand[j] = 0ull;
       __syncthreads();
       // bitonic sort, descending
@@ -332,20 +377,23 @@ __global__ void __launch_bounds__(kSampleThreads, 1)
       // [t chunk, (t + 1) chunk)
       const int chunk = (n + kSampleThreads - 1) / kSampleThreads;
       const int lo = min(n, tid * chunk), hi = min(n, lo + chunk);
+      auto weight = [&](float v) { return expf(__fdiv_rn(__fsub_rn(v, mx), temperature)); };
       float ls = 0.0f;
-      for (int i = lo; i < hi; ++i) ls += expf(__fdiv_rn(__fsub_rn(logits[i], mx), temperature));
+      for_range(logits, lo, hi, [&](float v, int) { ls += weight(v); });
       const float sum = block_sum_f(ls, s_f);
       float lq = 0.0f;
-      for (int i = lo; i < hi; ++i)
-        lq += __fdiv_rn(expf(__fdiv_rn(__fsub_rn(logits[i], mx), temperature)), sum);
+      for_range(logits, lo, hi, [&](float v, int) { lq += __fdiv_rn(weight(v), sum); });
       float cum = block_excl_scan_f(lq, s_f);
       int found = 0x7fffffff;
-      for (int i = lo; i < hi; ++i) {
-        cum += __fdiv_rn(expf(__fdiv_rn(__fsub_rn(logits[i], mx), temperature)), sum);
-        if (r < cum) {
-          found = i;
-          break;
-        }
+      // the running sum at element i is cum + (this thread's sum up to i,
+      // added from 0 as for lq), so only a thread with r < cum + lq holds
+      // the crossing
+      if (r < cum + lq) {
+        float part = 0.0f;
+        for_range(logits, lo, hi, [&](float v, int i) {
+          part += __fdiv_rn(weight(v), sum);
+          if (found == 0x7fffffff && r < cum + part) found = i;
+        });
       }
       found = block_min_i(found, s_i);
       id = found == 0x7fffffff ? n - 1 : found;

@@ -33,10 +33,16 @@ _vp = ctypes.c_void_p
 
 
 def build(ref: bool = True) -> None:
-    """Build the port (always) and the reference shim (when oracle/Makefile
-    finds the reference tree; REF_ROOT in the environment overrides where)."""
+    """Build the port (always) and the reference shim (when the reference tree
+    is found: $REF_ROOT, else the checkout named `reference` beside this
+    repository)."""
     targets = ["port"] + (["ref-if-present"] if ref else [])
-    subprocess.run(["make", "-s", "-C", HERE] + targets, check=True)
+    args = []
+    if ref:
+        root = os.environ.get("REF_ROOT") or os.path.join(
+            os.path.dirname(os.path.dirname(HERE.rstrip(os.sep))), "reference")
+        args = [f"REF_ROOT={root}"]
+    subprocess.run(["make", "-s", "-C", HERE] + targets + args, check=True)
 
 
 def weight_bytes(qtype: int, rows: int, cols: int) -> int:

@@ -27,7 +27,8 @@ sys.path.insert(0, ROOT)
 import oracle  # noqa: E402
 from mini_llama_b200 import configs as C  # noqa: E402
 
-REF_ROOT = os.environ.get("REF_ROOT", "/root/reference")
+# the reference checkout: $REF_ROOT, else the one named `reference` beside this repository
+REF_ROOT = os.environ.get("REF_ROOT") or os.path.join(os.path.dirname(ROOT), "reference")
 
 # Small models covering the code paths (GQA, NeoX + bias, ragged shapes).
 SMALL = {
