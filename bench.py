@@ -65,6 +65,9 @@ def parse_args():
                         "separated ('none' for none)")
     p.add_argument("--batch-ctx", type=int, default=4096,
                    help="K/V depth of every sequence of the batched workloads")
+    p.add_argument("--batch", type=int, default=1,
+                   help="B > 1: the line is --workload decoded as B sequences in lockstep "
+                        "(the batched engine) at depth --batch-ctx, nothing else")
     p.add_argument("--sweep-n", type=str, default="4096,11008,14336")
     p.add_argument("--sweep-m", type=str, default="1,4,16,64")
     p.add_argument("--sweep-q", type=str, default="q4_0,q4_1,q8_0")
@@ -651,6 +654,9 @@ def run_gpu(args, cfg, qtype, bias, rank, world, local):
 
         dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=600))
     peak = measured_peaks()
+    if args.batch > 1:
+        run_batch_line(torch, mlb, dist, args, cfg, qtype, bias, rank, world, local, peak)
+        return
     head = measure_workload(torch, mlb, dist, args, args.workload, cfg, qtype, bias, rank, world,
                             local, args.steps, args.warmup, peak, check_single=True)
     extras = []
@@ -757,6 +763,28 @@ def run_gpu(args, cfg, qtype, bias, rank, world, local):
                          "greedy_ids": e["ids"][:N_CHECK], "gpu_launches": e["gpu_launches"],
                          "parallelism": f"tp{world}" if world > 1 else "single gpu"}
         print(json.dumps(line))
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def run_batch_line(torch, mlb, dist, args, cfg, qtype, bias, rank, world, local, peak):
+    """--batch B: one line for --workload decoded as B sequences in lockstep."""
+    r = measure_batch(torch, mlb, dist, args, args.workload, cfg, qtype, bias, args.batch,
+                      args.batch_ctx, rank, world, local, args.steps, args.warmup, peak)
+    if rank == 0:
+        print(json.dumps({
+            "metric": "decode tok/s", "value": r["value"], "unit": "tok/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": r["ms_per_step"],
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": C.QTYPE_NAMES[qtype] + "/fp32", "data": r["data"],
+            "config": {"workload": args.workload + (f" ({args.layers} layers)" if args.layers else ""),
+                       "batch": args.batch, "ctx": args.batch_ctx, "parallelism": r["parallelism"],
+                       "l2": "no flush: each step streams the weights and every sequence's K/V "
+                             "(> 126 MB L2)"},
+            "roofline": r["roofline"], "parity": r["parity"], "clocks": r["clocks"],
+            "greedy_ids_seq0": r["greedy_ids_seq0"], "gpu_launches": r["gpu_launches"],
+            "kernels_per_step": r["kernels_per_step"]}))
     if dist:
         dist.barrier()
         dist.destroy_process_group()

@@ -451,75 +451,10 @@ constexpr int kStageBatch = 4;  // float4 of x each thread loads per round trip
 // then the warp sums in warp order, the same order as norm_inv_rms; longer
 // rows take norm_inv_rms's extra pass. A norm needs the CTA to stage all of K
 // (g0 .. g1 cover every chunk group). The caller synchronises afterwards.
-// Tensor-parallel form: x is base + parts[0] + ... + parts[nparts - 1] (rows of
-// length ldp of tagged words, summed in rank order, so every rank stages the
-// same values); each word is read until it carries `tag` (bounded: on
-// timeout the status records it and *failed is set). When store is non-null
-// this CTA writes its 1/gridDim slice of that sum there (the residual stream
-// for later phases). Needs the whole K staged.
-struct TpSum {
-  const uint2* parts;
-  int nparts, ldp;
-  unsigned int tag;
-  float* store;
-  DeviceStatus* status;
-  int* failed;  // shared flag, set to 1 on timeout
-};
-
-// Two tagged words {fp32 bits (low half), tag (high half)} from a 16-byte
-// aligned address, each 8-byte word read whole (single-copy atomic u64).
-__device__ __forceinline__ void ld_tagged_pair(const void* p, unsigned long long& a,
-                                               unsigned long long& b) {
-  asm volatile("ld.relaxed.sys.global.v2.u64 {%0, %1}, [%2];"
-               : "=l"(a), "=l"(b)
-               : "l"(p)
-               : "memory");
-}
-
-// Adds every rank's tagged partial sums of inputs k0 .. k0 + 3 (k0 a multiple
-// of 4) to v in rank order: per rank two 16-byte loads of two tagged words
-// each, re-loading only a pair whose tags are not yet this exchange step's
-// (bounded; on timeout the status records it and *failed is set). Words past
-// k count as zero. Out of line and one rank at a time: the callers keep
-// several staged quads per thread in registers, and holding every rank's
-// words at once (or inlining this into each caller) spills them.
-static __device__ __noinline__ void tp_add_all(const TpSum& t, int k0, int k, float4& v) {
-  const unsigned long long tag = t.tag;
-  const long long t0 = clock64();
-#pragma unroll 1
-  for (int rr = 0; rr < t.nparts; ++rr) {
-    const uint2* p = t.parts + (size_t)rr * t.ldp + k0;
-    unsigned long long w[4];
-    ld_tagged_pair(p, w[0], w[1]);
-    ld_tagged_pair(p + 2, w[2], w[3]);
-#pragma unroll
-    for (int hh = 0; hh < 2; ++hh) {
-      const bool need0 = k0 + 2 * hh < k, need1 = k0 + 2 * hh + 1 < k;
-      while ((need0 && (w[2 * hh] >> 32) != tag) || (need1 && (w[2 * hh + 1] >> 32) != tag)) {
-        if (clock64() - t0 > 4000000000LL || *(volatile int*)t.failed) {
-          if (t.status && atomicCAS(&t.status->code, 0, MLB_ERR_TIMEOUT) == 0)
-            atomicExch(&t.status->where, 400);
-          *(volatile int*)t.failed = 1;
-          w[2 * hh] = w[2 * hh + 1] = tag << 32;
-          break;
-        }
-        ld_tagged_pair(p + 2 * hh, w[2 * hh], w[2 * hh + 1]);
-      }
-      if (!need0) w[2 * hh] = 0ull;
-      if (!need1) w[2 * hh + 1] = 0ull;
-    }
-    v.x += __uint_as_float((unsigned int)w[0]);
-    v.y += __uint_as_float((unsigned int)w[1]);
-    v.z += __uint_as_float((unsigned int)w[2]);
-    v.w += __uint_as_float((unsigned int)w[3]);
-  }
-}
-
 template <int QT>
 __device__ __forceinline__ void stage_x_m1(const float* x, int k, const float* norm_w, float eps,
                                            int gc, int nchunks, int g0, int g1, uint32_t* frag,
-                                           float* side, float* part, float* inv_rms,
-                                           const TpSum* tps = nullptr) {
+                                           float* side, float* part, float* inv_rms) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nthr = blockDim.x;
   const int c0 = g0 * gc, c1 = min(nchunks, (g1 + 1) * gc);
   const int nq = (c1 - c0) * 64;
@@ -536,19 +471,6 @@ __device__ __forceinline__ void stage_x_m1(const float* x, int k, const float* n
       w[j] = make_float4(0.f, 0.f, 0.f, 0.f);
       if (idx < nq) {
         v[j] = load_quad(x, kbase + idx * 4, k, false);
-        if (tps) {
-          tp_add_all(*tps, kbase + idx * 4, k, v[j]);
-          if (tps->store) {  // this CTA's slice of the summed row
-            const int lo = (int)((long long)nq * blockIdx.x / gridDim.x);
-            const int hi = (int)((long long)nq * (blockIdx.x + 1) / gridDim.x);
-            if (idx >= lo && idx < hi) {
-              const int k0 = kbase + idx * 4;
-              const float e4[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
-              for (int i = 0; i < 4; ++i)
-                if (k0 + i < k) tps->store[k0 + i] = e4[i];
-            }
-          }
-        }
         if (norm_w) w[j] = load_quad(norm_w, kbase + idx * 4, k, true);
       }
     }
@@ -597,21 +519,6 @@ __device__ __forceinline__ void stage_x_m1(const float* x, int k, const float* n
         if (valid && (q4 & 7) == 0) sd[8 + (q4 >> 3)] = s4;
       }
     }
-  }
-}
-
-// Block-wide: this CTA's 1/gridDim slice (in float4 units, as stage_x_m1
-// cuts it) of x + every rank's partial sums, written to tps.store.
-__device__ __forceinline__ void tp_store_slice(const float* x, int k, const TpSum& tps) {
-  const int nq = (k + kChunkK - 1) / kChunkK * 64;  // quads of whole chunks, as staged
-  const int lo = (int)((long long)nq * blockIdx.x / gridDim.x);
-  const int hi = (int)((long long)nq * (blockIdx.x + 1) / gridDim.x);
-  for (int idx = lo + threadIdx.x; idx < hi; idx += blockDim.x) {
-    float4 v = load_quad(x, idx * 4, k, false);
-    tp_add_all(tps, idx * 4, k, v);
-    const float e4[4] = {v.x, v.y, v.z, v.w};
-    for (int i = 0; i < 4; ++i)
-      if (idx * 4 + i < k) tps.store[idx * 4 + i] = e4[i];
   }
 }
 

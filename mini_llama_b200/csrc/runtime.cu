@@ -609,38 +609,26 @@ void ContextImpl::plan_step() {
     p.g.eps = cf.rms_norm_eps;
     p.g.epi = e;
     p.g.tp_ar = -1;
-    p.g.x_slot = -1;
-    p.g.x_ar = -1;
-    p.g.x_store = nullptr;
     ph.push_back(p);
   };
   int* d_pos = scalars.as<int>() + 1;
   if (tp) setup_tp_exchange();
-  // one GPU: the residual epilogues of wo and w_down leave per-tile sums of
-  // squares of x, from which the next RMSNorm reads its statistic
+  // the residual epilogues of wo and w_down (one GPU) or the exchange sums
+  // after them (tensor parallel) leave per-tile sums of squares of x, from
+  // which the next RMSNorm reads its statistic
   const int ss_n = (cf.dim + kTileRows - 1) / kTileRows;
-  float* ss_xa = nullptr;
-  float* ss_xb = nullptr;
-  if (!tp) {
-    ss_x.alloc((size_t)2 * ss_n * 4);
-    ss_xa = ss_x.as<float>();
-    ss_xb = ss_xa + ss_n;
-  }
+  ss_x.alloc((size_t)2 * ss_n * 4);
+  float* ss_xa = ss_x.as<float>();
+  float* ss_xb = ss_xa + ss_n;
   auto ss_in = [&](StepPhase& p, const float* ss) {
     p.g.ss_in = ss;
     p.g.ss_n = ss ? ss_n : 0;
   };
   const TpXchg* tpd = tp ? tp_desc.as<TpXchg>() : nullptr;
   // Tensor parallel: exchange step 2l is layer l's wo partial sums (slot 0),
-  // 2l + 1 its w_down partial sums (slot 1). The producing phase ends with the
-  // fused cross-rank barrier; the consuming phase adds every rank's partials
-  // to the residual and keeps the result as the next residual.
-  auto tp_in = [&](StepPhase& p, int slot, int ar, const float* base, float* store) {
-    p.g.x = base;
-    p.g.x_slot = slot;
-    p.g.x_ar = ar;
-    p.g.x_store = store;
-  };
+  // 2l + 1 its w_down partial sums (slot 1). The producing phase adds every
+  // rank's partials to the residual (each CTA its tiles) before its barrier,
+  // so the consuming phase reads the next residual like a single GPU.
   for (int l = 0; l < cf.n_layers; ++l) {
     const LayerPlan& L = m->layers[l];
     const float* x_in = l == 0 ? nullptr : xa.as<float>();  // null: embedding row
@@ -659,7 +647,6 @@ void ContextImpl::plan_step() {
     e.values = values.as<float>() + (size_t)l * layer_kv;
     e.q_out = q.as<float>();
     gemv(L.qkv, x_in, L.attn_norm.as<float>(), e);
-    if (tp && l > 0) tp_in(ph.back(), 1, 2 * (l - 1) + 1, xb.as<float>(), xa.as<float>());
     if (l > 0) ss_in(ph.back(), ss_xa);
 
     StepPhase a{};
@@ -693,7 +680,6 @@ void ContextImpl::plan_step() {
     eg.ldy = m->ffn_rows;
     eg.n_out = m->ffn_rows;
     gemv(L.gateup, xb.as<float>(), L.ffn_norm.as<float>(), eg);
-    if (tp) tp_in(ph.back(), 0, 2 * l, x_in, xb.as<float>());
     ss_in(ph.back(), ss_xb);
 
     EpiParams ed{};
@@ -718,8 +704,6 @@ void ContextImpl::plan_step() {
   el.tp = tpd;
   gemv(m->lm_head, cf.n_layers == 0 ? nullptr : xa.as<float>(), m->final_norm.as<float>(), el);
   if (cf.n_layers > 0) ss_in(ph.back(), ss_xa);
-  if (tp && cf.n_layers > 0)
-    tp_in(ph.back(), 1, 2 * (cf.n_layers - 1) + 1, xb.as<float>(), nullptr);
 
   if ((int)ph.size() != nph) fail(MLB_ERR_INVALID, "decode step kernel: phase count mismatch");
   step_phases.alloc(ph.size() * sizeof(StepPhase));

@@ -450,42 +450,22 @@ __device__ bool gemv_phase(StepShared& sh, StepPhase& cur, const StepCta& ct, ui
   const int warp = threadIdx.x >> 5;
   const int cb = ct.cb, ce = ct.ce;
   const float* x = g.x ? g.x : a.embedding + (size_t)sh.token * a.dim;
-  TpSum tps{};
-  if (g.x_slot >= 0) {
-    tps.parts = reinterpret_cast<const uint2*>(a.tp->peers[a.tp->me] + a.tp->parts_off) +
-                (size_t)g.x_slot * a.tp->n * a.tp->dim;
-    tps.nparts = a.tp->n;
-    tps.ldp = a.tp->dim;
-    tps.tag = sh.tp_gen0 + (unsigned int)g.x_ar + 1u;
-    tps.store = g.x_store;
-    tps.status = a.status;
-    tps.failed = &sh.tp_fail;
-  }
   if (g.tp_ar >= 0 && threadIdx.x == 0)  // this phase's exchange step tag (read after syncs)
     cur.g.epi.tp_tag = sh.tp_gen0 + (unsigned int)g.tp_ar + 1u;
-  if (cb >= ce) {
-    // no tiles here, but this CTA's slice of the summed residual is still owed
-    if (g.x_slot >= 0 && tps.store) {
-      tp_store_slice(x, g.k, tps);
-      __syncthreads();
-      if (sh.tp_fail) return false;
-    }
-    return true;
-  }
+  if (cb >= ce) return true;
   const GemvScratch sc = gemv_scratch<QT>(scratch, g);
   const int g0 = ct.grp[0], g1 = ct.grp[ct.nseg - 1];
   // Every warp needs only its own chunks of x: it stages them itself and
   // starts at once (the RMSNorm statistic, when there is one, from the
-  // producing phase's per-tile sums of squares). Otherwise (statistic of the
-  // embedding row, tensor-parallel sums) the block stages all of x first.
-  if (g.x_slot < 0 && (g.norm_w == nullptr || g.ss_in != nullptr)) {
+  // producing phase's per-tile sums of squares). Otherwise (the statistic of
+  // the embedding row) the block stages all of x first.
+  if (g.norm_w == nullptr || g.ss_in != nullptr) {
     stage_chunks_warp<QT>(x, g.k, g.norm_w, g.ss_in, g.ss_n, g.eps, ct, g.gc, sc.frag, sc.side);
     __syncwarp();
   } else {
     stage_x_m1<QT>(x, g.k, g.norm_w, g.eps, g.gc, g.nchunks, g0, g1, sc.frag, sc.side, sh.part,
-                   sh.inv_rms, g.x_slot >= 0 ? &tps : nullptr);
+                   sh.inv_rms);
     __syncthreads();
-    if (sh.tp_fail) return false;  // a tagged read of the staged sum gave up (block-uniform)
   }
   // residual of the first layer: the embedding row (patched before the
   // barrier below, read only after it)
@@ -559,6 +539,79 @@ __device__ bool gemv_phase(StepShared& sh, StepPhase& cur, const StepCta& ct, ui
     sbase += T * nc;
   }
   return true;
+}
+
+// ------------------------------------------- tensor-parallel exchange
+
+__device__ __forceinline__ unsigned long long ld_relaxed_sys_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Tensor parallel, after a phase whose epilogue stored its partial sums into
+// every rank's exchange slot (kEpiTpPartial): this CTA's share of the row
+// tiles of the sum, before the grid barrier that ends the phase. Row i:
+//   y[i] = resid[i] + part_0[i] + ... + part_{n-1}[i]
+// in rank order (the same on every rank, so every rank holds bit-identical
+// residuals), each partial read until it carries this exchange step's tag
+// (bounded), and the tile's sum of squares into ss_out with the residual
+// epilogue's tree, from which the next RMSNorm takes its statistic. Every CTA
+// of every rank reads only its own tiles' n words per row, all issued at
+// once, so the next phase stages x like a single GPU. Returns false (block-
+// uniform) when a read gave up. Out of line: its registers stay out of the
+// GEMV loop's budget.
+__device__ __noinline__ bool tp_reduce_slice(StepShared& sh, const StepGemv& g,
+                                             const StepArgs& a) {
+  const EpiParams& e = g.epi;
+  const TpXchg* x = a.tp;
+  const int n = x->n, dim = x->dim;
+  const unsigned long long tag = sh.tp_gen0 + (unsigned int)g.tp_ar + 1u;
+  const unsigned long long* parts =
+      reinterpret_cast<const unsigned long long*>(x->peers[x->me] + x->parts_off) +
+      (size_t)e.tp_slot * n * dim;
+  const float* prev = e.resid ? e.resid : a.embedding + (size_t)sh.token * a.dim;
+  const int ntile = (e.n_out + 15) / 16;
+  const int lo = (int)((long long)ntile * blockIdx.x / gridDim.x);
+  const int hi = (int)((long long)ntile * (blockIdx.x + 1) / gridDim.x);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const long long t0 = clock64();
+  for (int t = lo + warp; t < hi; t += kStepWarps) {
+    const int row = t * 16 + lane;
+    const bool mine = lane < 16 && row < e.n_out;
+    float v = 0.0f;
+    if (mine) {
+      unsigned long long w[kMaxTp];
+#pragma unroll
+      for (int r = 0; r < kMaxTp; ++r)
+        if (r < n) w[r] = ld_relaxed_sys_u64(parts + (size_t)r * dim + row);
+      v = __ldcg(prev + row);
+#pragma unroll
+      for (int r = 0; r < kMaxTp; ++r) {
+        if (r >= n) break;
+        while ((w[r] >> 32) != tag) {
+          if (clock64() - t0 > kWaitCycles || *(volatile int*)&sh.tp_fail) {
+            if (atomicCAS(&a.status->code, 0, MLB_ERR_TIMEOUT) == 0)
+              atomicExch(&a.status->where, 400);
+            *(volatile int*)&sh.tp_fail = 1;
+            w[r] = tag << 32;
+            break;
+          }
+          w[r] = ld_relaxed_sys_u64(parts + (size_t)r * dim + row);
+        }
+        v = __fadd_rn(v, __uint_as_float((unsigned int)w[r]));
+      }
+      e.y[row] = v;
+    }
+    float sq = mine ? v * v : 0.0f;
+    sq += __shfl_xor_sync(0xffffffffu, sq, 8);
+    sq += __shfl_xor_sync(0xffffffffu, sq, 4);
+    sq += __shfl_xor_sync(0xffffffffu, sq, 2);
+    sq += __shfl_xor_sync(0xffffffffu, sq, 1);
+    if (lane == 0) e.ss_out[t] = sq;
+  }
+  __syncthreads();
+  return !sh.tp_fail;
 }
 
 // ------------------------------------------------------ attention phase
@@ -928,7 +981,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
   for (int i = threadIdx.x; i < kDesc16; i += kStepThreads)
     reinterpret_cast<int4*>(&sh.cur[0])[i] = __ldg(reinterpret_cast<const int4*>(a.phases) + i);
   bool ok = true;
-  unsigned int nbar = 0;  // grid barriers passed (fused TP barriers do not count)
+  unsigned int nbar = 0;  // grid barriers passed
   for (int p = 0; p < a.nphases && ok; ++p) {
     StepPhase& cur = sh.cur[p & 1];
     if (threadIdx.x == 0) sh.flag = 1;
@@ -941,19 +994,18 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
       for (int i = threadIdx.x; i < kDesc16; i += kStepThreads) cp_async16(dst + i, src + i);
       cp_async_commit();
     }
-    if (cur.kind == kPhaseGemv)
+    if (cur.kind == kPhaseGemv) {
       ok = gemv_phase<QT>(sh, cur, tab[p], scratch, rg, pr, run, tab, a);
-    else
+      // tensor parallel: this phase's partial sums, added across ranks
+      if (ok && cur.g.tp_ar >= 0) ok = tp_reduce_slice(sh, cur.g, a);
+    } else {
       ok = attn_phase<HG>(sh, cur, scratch, a);
+    }
     cp_async_wait_all();
     if (a.trace && threadIdx.x == 0)
       a.trace[((size_t)p * gridDim.x + blockIdx.x) * 2 + 1] = global_ns();
-    if (cur.kind == kPhaseGemv && cur.g.tp_ar >= 0) {
-      // tensor parallel: the next phase reads this one's partial sums as
-      // tagged words and waits for the tags itself; no barrier
-    } else if (ok && p + 1 < a.nphases) {
+    if (ok && p + 1 < a.nphases)
       ok = grid_barrier(&a.sync[0], ++nbar, a.status, 100 + p, &sh.flag);
-    }
   }
   if (!ok) {
     if (lane == 0) ring_drain(rg.bars, rg.stages, rg.slot, rg.parity, rg.inflight);

@@ -26,13 +26,11 @@ struct StepGemv {
   float eps;
   EpiParams epi;        // kEpiResidual with resid null: residual = the embedding row
   // Tensor parallel: tp_ar >= 0 marks a phase whose epilogue writes exchange
-  // step tp_ar of this decode step into every rank as tagged words (no
-  // barrier follows it: readers wait for the tags); when x_slot >= 0 the input
-  // is x (or the embedding row) plus every rank's partial sums of exchange
-  // step x_ar in x_slot, and x_store receives this CTA's slice of that sum.
+  // step tp_ar of this decode step into every rank as tagged words
+  // (kEpiTpPartial, slot epi.tp_slot); before the barrier that ends the phase
+  // each CTA adds its tiles of the exchange to epi.resid (null: the embedding
+  // row) into epi.y, with per-tile sums of squares into epi.ss_out.
   int tp_ar;
-  int x_slot, x_ar;
-  float* x_store;
   // RMSNorm statistic of x as the producing phase's per-tile sums of squares
   // (ss_n tiles), or null
   const float* ss_in;
