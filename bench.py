@@ -74,6 +74,8 @@ def parse_args():
     p.add_argument("--no-sweep", action="store_true", help="skip the GEMV sweep of the N=1 line")
     p.add_argument("--ctx", type=int, default=512, help="KV positions filled before timing")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-gguf-load", action="store_true",
+                   help="skip the GGUF load measurement of the N=1 line")
     p.add_argument("--layers", type=int, default=0,
                    help="override the layer count (small profiling cases only; not a bench line)")
     p.add_argument("--per-op", action="store_true",
@@ -683,8 +685,15 @@ def run_gpu(args, cfg, qtype, bias, rank, world, local):
 
     gemv_roof = sweep = sweep_cpu = None
     cpu = None
+    gguf = None
     if rank == 0 and world == 1:
         gemv_roof = gemv_roofline(torch, mlb, cfg, qtype, world, peak)
+        if not args.no_gguf_load and not args.layers:
+            try:
+                gguf = gguf_load(torch, mlb, cfg, qtype, bias, local,
+                                 with_ref=not args.no_cpu_baseline)
+            except Exception as e:  # reported, not fatal
+                gguf = {"error": str(e)[:300]}
         if not args.no_sweep and not args.layers:
             with Clocks([local]) as clk:
                 sweep, windows, sweep_cpu = gemv_sweep(torch, mlb, args, peak,
@@ -742,6 +751,8 @@ def run_gpu(args, cfg, qtype, bias, rank, world, local):
         }
         if gemv_roof:
             line["gemv_roofline"] = gemv_roof
+        if gguf:
+            line["gguf_load"] = gguf
         if sweep:
             line["gemv_sweep"] = {"rows": sweep, "cpu_baseline": sweep_cpu,
                                   "clocks": sweep_clocks,
@@ -766,6 +777,59 @@ def run_gpu(args, cfg, qtype, bias, rank, world, local):
     if dist:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def gguf_load(torch, mlb, cfg, qtype, bias, local, with_ref):
+    """The workload's model written as a GGUF v3 file (seeded weights, one
+    tensor at a time) and loaded with mlb_model_load_gguf: wall time from the
+    call to a finalized model (parse, pinned staged upload of every tensor,
+    repack), the file then in the host page cache. Checked: the loaded model's
+    logits at position 0 equal those of the same model synthesised on the
+    device. with_ref: the reference's LoadGgufModel reading the same file into
+    host memory (its upload to a GPU is not part of its CPU build)."""
+    import shutil
+
+    from mini_llama_b200 import gguf_writer as GW
+
+    d = tempfile.mkdtemp(prefix="mlb_gguf_")
+    path = os.path.join(d, "model.gguf")
+    try:
+        t0 = time.perf_counter()
+        nbytes = GW.write_synthetic_model(path, cfg, qtype, SEED, bias, threads=cpu_threads())
+        t_write = time.perf_counter() - t0
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        m = mlb.CudaModel.from_gguf(path, device_id=local)
+        torch.cuda.synchronize()
+        t_load = time.perf_counter() - t0
+        tok = C.prompt_ids(SEED, 1, cfg["vocab_size"])[0]
+        c = m.context(mlb.ATTN_CPU_COMPAT)
+        lg = c.forward_token(tok, 0)
+        c.close()
+        uploaded = m.gguf_bytes
+        m.close()
+        s = mlb.CudaModel(cfg, device_id=local).synthesize(qtype, SEED, with_bias=bias)
+        c = s.context(mlb.ATTN_CPU_COMPAT)
+        same = bool(np.array_equal(lg, c.forward_token(tok, 0)))
+        c.close()
+        s.close()
+        out = {"file_bytes": nbytes, "uploaded_bytes": uploaded, "load_s": t_load,
+               "gbs": nbytes / t_load / 1e9, "write_s": t_write,
+               "logits_equal_synthesized": same,
+               "api": "mlb_model_load_gguf (mmap, pinned staging, repack, finalize)",
+               "note": "file just written, so read from the host page cache"}
+        if with_ref:
+            import oracle
+
+            if oracle.ref_available():
+                t0 = time.perf_counter()
+                rm = oracle.ref().load_gguf(path)
+                out["reference_load_s"] = time.perf_counter() - t0
+                out["reference_api"] = "LoadGgufModel into host memory (CPU build)"
+                del rm
+        return out
+    finally:
+        shutil.rmtree(d, ignore_errors=True)
 
 
 def run_batch_line(torch, mlb, dist, args, cfg, qtype, bias, rank, world, local, peak):

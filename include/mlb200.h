@@ -278,6 +278,29 @@ int mlb_model_set_weight(mlb_model* m, int kind, int layer, int qtype, int rows,
 int mlb_model_synthesize(mlb_model* m, int qtype, uint64_t seed, int with_bias);
 /* Checks that every weight is present and builds the decode plan. */
 int mlb_model_finalize(mlb_model* m);
+/* The ModelConfig that LoadGgufModel builds from a GGUF v3 file's metadata
+ * (BuildConfig, src/gguf_loader.cc:13-88: qwen2.* keys, else llama.* keys,
+ * else 0; NeoX RoPE for general.architecture "qwen2"; vocab_size = length of
+ * tokenizer.ggml.tokens; head_dim = dim / n_heads). Host only (no device).
+ * Parse and config errors return MLB_ERR_INVALID with the reference's
+ * messages ("GGUF parse error: invalid GGUF magic", "... unsupported GGUF
+ * version: 2", "Failed to build config: ..."). */
+int mlb_gguf_read_config(const char* path, mlb_config* out);
+/* Replaces LoadGgufModel (src/gguf_loader.cc:302-418) followed by
+ * UploadModelWeightsToCuda (src/model.cc:345-374): parses the GGUF v3 file,
+ * creates the model (tensor-parallel shard as mlb_model_create), uploads the
+ * tensors the model uses straight from the memory-mapped file through pinned
+ * staging buffers (this rank's rows only) and finalizes. Tensor names and
+ * shapes follow MapTensorName / MapShape; a missing output.weight ties the
+ * lm_head to the embedding; quantised or F16 norms, biases and embeddings are
+ * widened to F32 with the reference's dequantisation. Unlike the reference,
+ * F16 linear weights are accepted (widened to F32, exact); quantised rows must
+ * be whole 32-element blocks. max_seq_len > 0 replaces the file's
+ * context_length (the KV cache size); bytes_uploaded (optional) receives the
+ * bytes copied to the device. */
+int mlb_model_load_gguf(const char* path, int device_id, int tp_rank, int tp_size,
+                        const void* nccl_id, int max_seq_len, mlb_model** out,
+                        size_t* bytes_uploaded);
 int mlb_model_destroy(mlb_model* m);
 /* Resident bytes of the weights on this device (ModelCudaMemoryBytes,
  * include/mini_llama/model.h:119) and algorithmic GGUF bytes one decode step

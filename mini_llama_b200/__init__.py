@@ -11,6 +11,7 @@ kernels. Errors raise ``MlbError`` (the reference's std::runtime_error) or
 from __future__ import annotations
 
 import ctypes
+import os
 
 import numpy as np
 
@@ -397,6 +398,27 @@ class CudaModel:
                                      ctypes.byref(h)))
         self.h = h
 
+    @classmethod
+    def from_gguf(cls, path: str, device_id=0, tp_rank=0, tp_size=1, nccl_id: bytes | None = None,
+                  max_seq_len: int = 0):
+        """LoadGgufModel + UploadModelWeightsToCuda (mlb_model_load_gguf): the model
+        of a GGUF v3 file, uploaded from the mapped file and finalized.
+        max_seq_len > 0 replaces the file's context_length. The bytes copied to
+        the device are in .gguf_bytes."""
+        self = cls.__new__(cls)
+        self.cfg = read_gguf_config(path)
+        if max_seq_len > 0:
+            self.cfg["max_seq_len"] = max_seq_len
+        self.device_id = device_id
+        h = ctypes.c_void_p()
+        n = ctypes.c_size_t()
+        idbuf = None if nccl_id is None else ctypes.create_string_buffer(bytes(nccl_id), 128)
+        check(lib().mlb_model_load_gguf(os.fsencode(path), device_id, tp_rank, tp_size, idbuf,
+                                        int(max_seq_len), ctypes.byref(h), ctypes.byref(n)))
+        self.h = h
+        self.gguf_bytes = n.value
+        return self
+
     def set_weight(self, kind, layer, qtype, rows, cols, data: np.ndarray):
         data = np.ascontiguousarray(data)
         check(lib().mlb_model_set_weight(self.h, kind, layer, qtype, rows, cols, data.ctypes.data,
@@ -624,6 +646,13 @@ class Batch:
 def ForwardToken(ctx: Context, token: int) -> np.ndarray:
     """ForwardToken(ctx, model, token) (include/mini_llama/forward.h:11) at ctx.pos."""
     return ctx.forward_token(token, ctx.pos)
+
+
+def read_gguf_config(path: str) -> dict:
+    """The model config LoadGgufModel builds from a GGUF file (host only)."""
+    c = MlbConfig()
+    check(lib().mlb_gguf_read_config(os.fsencode(path), ctypes.byref(c)))
+    return {k: getattr(c, k) for k, _ in MlbConfig._fields_}
 
 
 def tp_plan(cfg: dict, tp_rank: int, tp_size: int) -> dict:

@@ -78,6 +78,9 @@ SIGNATURES = [
     ("mlb_model_finalize", _c_int, [_vp]),
     ("mlb_model_destroy", _c_int, [_vp]),
     ("mlb_model_bytes", _c_int, [_vp, ctypes.POINTER(_c_size_t), ctypes.POINTER(_c_size_t)]),
+    ("mlb_gguf_read_config", _c_int, [ctypes.c_char_p, ctypes.POINTER(MlbConfig)]),
+    ("mlb_model_load_gguf", _c_int, [ctypes.c_char_p, _c_int, _c_int, _c_int, _vp, _c_int,
+                                     ctypes.POINTER(_vp), ctypes.POINTER(_c_size_t)]),
     ("mlb_context_create", _c_int, [_vp, _c_int, ctypes.POINTER(_vp)]),
     ("mlb_context_destroy", _c_int, [_vp]),
     ("mlb_context_reset", _c_int, [_vp]),

@@ -522,6 +522,32 @@ int mlb_model_synthesize(mlb_model* m, int qtype, uint64_t seed, int with_bias) 
   });
 }
 
+int mlb_gguf_read_config(const char* path, mlb_config* out) {
+  return guarded([&] {
+    if (!path || !out) invalid("mlb_gguf_read_config: null argument");
+    std::unique_ptr<GgufFile, void (*)(GgufFile*)> g(gguf_open(path), gguf_close);
+    *out = gguf_config(*g);
+  });
+}
+
+int mlb_model_load_gguf(const char* path, int device_id, int tp_rank, int tp_size,
+                        const void* nccl_id, int max_seq_len, mlb_model** out,
+                        size_t* bytes_uploaded) {
+  return guarded([&] {
+    if (!path || !out) invalid("mlb_model_load_gguf: null argument");
+    if (max_seq_len < 0) invalid("mlb_model_load_gguf: negative max_seq_len");
+    std::unique_ptr<GgufFile, void (*)(GgufFile*)> g(gguf_open(path), gguf_close);
+    mlb_config cfg = gguf_config(*g);
+    if (max_seq_len > 0) cfg.max_seq_len = max_seq_len;
+    std::unique_ptr<ModelImpl, void (*)(ModelImpl*)> impl(
+        model_create(&cfg, device_id, tp_rank, tp_size, nccl_id), model_destroy);
+    const size_t n = gguf_upload(*impl, *g);
+    model_finalize(*impl);
+    if (bytes_uploaded) *bytes_uploaded = n;
+    *out = new mlb_model{impl.release()};
+  });
+}
+
 int mlb_model_finalize(mlb_model* m) {
   return guarded([&] {
     if (!m) invalid("mlb_model_finalize: null model");

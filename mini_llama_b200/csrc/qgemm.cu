@@ -253,39 +253,82 @@ __device__ __forceinline__ void dq_pair(uint32_t magic, __half2 d2, uint32_t& hi
   lo = h2_as_u32(l);
 }
 
-// One weight row's GGUF block b of a super-block as 16 hi and 16 lo half2
-// columns in input order (column p holds inputs 2p, 2p + 1 of the block). The
-// row is row g + 8 h of the super-block; its codes sit where repack_kernel
-// put them for mma.sync lane g * 4 + cl.
+// One weight row's GGUF blocks 2 bp and 2 bp + 1 of a super-block as 16 hi
+// and 16 lo half2 columns each, in input order (column p holds inputs 2p,
+// 2p + 1 of the block); the row is row g + 8 h of the super-block, its codes
+// where repack_kernel put them for mma.sync lane g * 4 + cl. Read
+// without shared-memory bank conflicts. A warp's 32 rows are rows g + 8 h of
+// two super-blocks (jb = 0, 1), and row g's code word for chunk column cl sits
+// at bank 16 (g % 2) + 4 cl + 2 (block % 2) + h (super-blocks are a multiple
+// of 128 bytes apart): read in the same column order, rows g, g + 2, g + 4,
+// g + 6 and the two super-blocks collide (8 ways). So row g reads column
+// (i + g / 2) % 4 at step i, and super-block 1 reads the pair's blocks in
+// swapped order; selects put the words back in (block, column) order.
 template <int QT>
-__device__ __forceinline__ void dq_block(const uint8_t* sb, int g, int h, int b, uint32_t (&hv)[16],
-                                         uint32_t (&lv)[16]) {
+__device__ __forceinline__ void dq_block_pair(const uint8_t* sb, int g, int h, int jb, int bp,
+                                              uint32_t (&hv)[2][16], uint32_t (&lv)[2][16]) {
   constexpr int qbytes = QT == MLB_Q8_0 ? 4096 : 2048;
-  const uint8_t* sc = sb + qbytes + (g * 8 + b) * 4 + 2 * h;
-  const __half d = __ushort_as_half(*reinterpret_cast<const unsigned short*>(sc));
-  const __half2 d2 = __halves2half2(d, d);
+  const int r = (g >> 1) & 3;
+  constexpr int W = QT == MLB_Q8_0 ? 2 : 1;  // 32-bit code words per (block, column, row)
+  uint32_t w[2][4][W];                       // [block parity][column][word]
+  {
+    uint32_t t[4][2][W];  // [step][pair slot][word]: block 2 bp + (slot ^ jb), column (i + r) % 4
 #pragma unroll
-  for (int cl = 0; cl < 4; ++cl) {
-    const int lane = g * 4 + cl;
-    uint32_t mg[4];
-    if (QT == MLB_Q8_0) {
-      const uint2 w = *reinterpret_cast<const uint2*>(sb + (size_t)(b * 32 + lane) * 16 + h * 8);
-      const uint32_t xa = w.x ^ 0x80808080u, xb = w.y ^ 0x80808080u;
-      mg[0] = __byte_perm(xa, 0x64646464u, 0x4140);  // inputs 2cl, 2cl + 1
-      mg[1] = __byte_perm(xa, 0x64646464u, 0x4342);  // 2cl + 8, 2cl + 9
-      mg[2] = __byte_perm(xb, 0x64646464u, 0x4140);  // 2cl + 16, 2cl + 17
-      mg[3] = __byte_perm(xb, 0x64646464u, 0x4342);  // 2cl + 24, 2cl + 25
-    } else {
-      const uint32_t w = *reinterpret_cast<const uint32_t*>(
-          sb + (size_t)((b >> 1) * 32 + lane) * 16 + (b & 1) * 8 + h * 4);
-      const uint32_t M1 = 0x000F000Fu, E = 0x64006400u;
-      mg[0] = lop3_and_or(w, M1, E);        // low nibbles of bytes 0, 2: inputs 2cl, 2cl + 1
-      mg[1] = lop3_and_or(w >> 8, M1, E);   // bytes 1, 3: 2cl + 8, 2cl + 9
-      mg[2] = lop3_and_or(w >> 4, M1, E);   // high nibbles of 0, 2: 2cl + 16, 2cl + 17
-      mg[3] = lop3_and_or(w >> 12, M1, E);  // high nibbles of 1, 3: 2cl + 24, 2cl + 25
+    for (int i = 0; i < 4; ++i) {
+      const int cl = (i + r) & 3;
+#pragma unroll
+      for (int p = 0; p < 2; ++p) {
+        const int b = 2 * bp + (p ^ jb);
+        if (QT == MLB_Q8_0) {
+          const uint2 v = *reinterpret_cast<const uint2*>(sb + (size_t)(b * 32 + g * 4 + cl) * 16 + h * 8);
+          t[i][p][0] = v.x;
+          t[i][p][W - 1] = v.y;
+        } else {
+          t[i][p][0] = *reinterpret_cast<const uint32_t*>(
+              sb + (size_t)(bp * 32 + g * 4 + cl) * 16 + (b & 1) * 8 + h * 4);
+        }
+      }
     }
 #pragma unroll
-    for (int e = 0; e < 4; ++e) dq_pair<QT>(mg[e], d2, hv[4 * e + cl], lv[4 * e + cl]);
+    for (int P = 0; P < 2; ++P)
+#pragma unroll
+      for (int k = 0; k < W; ++k) {
+        uint32_t u[4], v1[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) u[i] = jb ? t[i][P ^ 1][k] : t[i][P][k];
+        // column cl was read at step (cl - r) % 4
+#pragma unroll
+        for (int c = 0; c < 4; ++c) v1[c] = (r & 1) ? u[(c + 3) & 3] : u[c];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) w[P][c][k] = (r & 2) ? v1[(c + 2) & 3] : v1[c];
+      }
+  }
+#pragma unroll
+  for (int P = 0; P < 2; ++P) {
+    const int b = 2 * bp + P;
+    const uint8_t* sc = sb + qbytes + (g * 8 + b) * 4 + 2 * h;
+    const __half d = __ushort_as_half(*reinterpret_cast<const unsigned short*>(sc));
+    const __half2 d2 = __halves2half2(d, d);
+#pragma unroll
+    for (int cl = 0; cl < 4; ++cl) {
+      uint32_t mg[4];
+      if (QT == MLB_Q8_0) {
+        const uint32_t xa = w[P][cl][0] ^ 0x80808080u, xb = w[P][cl][W - 1] ^ 0x80808080u;
+        mg[0] = __byte_perm(xa, 0x64646464u, 0x4140);  // inputs 2cl, 2cl + 1
+        mg[1] = __byte_perm(xa, 0x64646464u, 0x4342);  // 2cl + 8, 2cl + 9
+        mg[2] = __byte_perm(xb, 0x64646464u, 0x4140);  // 2cl + 16, 2cl + 17
+        mg[3] = __byte_perm(xb, 0x64646464u, 0x4342);  // 2cl + 24, 2cl + 25
+      } else {
+        const uint32_t x = w[P][cl][0];
+        const uint32_t M1 = 0x000F000Fu, E = 0x64006400u;
+        mg[0] = lop3_and_or(x, M1, E);        // low nibbles of bytes 0, 2: inputs 2cl, 2cl + 1
+        mg[1] = lop3_and_or(x >> 8, M1, E);   // bytes 1, 3: 2cl + 8, 2cl + 9
+        mg[2] = lop3_and_or(x >> 4, M1, E);   // high nibbles of 0, 2: 2cl + 16, 2cl + 17
+        mg[3] = lop3_and_or(x >> 12, M1, E);  // high nibbles of 1, 3: 2cl + 24, 2cl + 25
+      }
+#pragma unroll
+      for (int e = 0; e < 4; ++e) dq_pair<QT>(mg[e], d2, hv[P][4 * e + cl], lv[P][4 * e + cl]);
+    }
   }
 }
 
@@ -629,19 +672,21 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const TcArgs a) 
             ok = false;
             break;
           }
-#pragma unroll
-          for (int bb = 0; bb < 2; ++bb) {
-            const int bl = 2 * half + bb;  // block within the half chunk
-            uint32_t hv[16], lv[16];
+          {
+            // blocks 4 kh + 2 half + bb of the chunk: block pair 2 kh + half
+            uint32_t hv[2][16], lv[2][16];
             if (valid) {
-              dq_block<QT>(sb, g, h, 4 * kh + bl, hv, lv);
+              dq_block_pair<QT>(sb, g, h, j & 1, 2 * kh + half, hv, lv);
             } else {
 #pragma unroll
-              for (int i = 0; i < 16; ++i) hv[i] = lv[i] = 0u;
+              for (int i = 0; i < 16; ++i) hv[0][i] = lv[0][i] = hv[1][i] = lv[1][i] = 0u;
             }
-            const uint32_t col = tbase + lane_base + t * kAStageCols + 16 * bl;
-            tmem_st16(col, hv);
-            tmem_st16(col + 64, lv);
+#pragma unroll
+            for (int bb = 0; bb < 2; ++bb) {
+              const uint32_t col = tbase + lane_base + t * kAStageCols + 16 * (2 * half + bb);
+              tmem_st16(col, hv[bb]);
+              tmem_st16(col + 64, lv[bb]);
+            }
           }
           if (QT == MLB_Q4_1 && kh == 1) {
             // the mins of this warp's blocks {2 half, 2 half + 1, 4 + 2 half, 5 + 2 half}

@@ -263,6 +263,28 @@ void model_set_weight(ModelImpl& m, int kind, int layer, int qtype, int rows, in
   put_pending(m, kind, layer, std::move(t));
 }
 
+WeightSlot model_weight_slot(const ModelImpl& m, int kind, int layer) {
+  if (kind < 0 || kind > MLB_W_DOWN) out_of_range("weight kind out of range");
+  if (kind >= 3 && (layer < 0 || layer >= m.cfg.n_layers)) out_of_range("weight layer out of range");
+  const Expect e = expected_shape(m, kind);
+  WeightSlot w;
+  w.rows = e.rows;
+  w.cols = e.cols;
+  w.f32_only = e.f32_only;
+  w.by_cols = kind == MLB_W_BQ || kind == MLB_W_BK || kind == MLB_W_BV;
+  if (w.by_cols)
+    shard_rows(m, kind == MLB_W_BQ ? MLB_W_WQ : MLB_W_WK, e.cols, &w.first, &w.count);
+  else
+    shard_rows(m, kind, e.rows, &w.first, &w.count);
+  w.name = weight_name(kind, layer);
+  return w;
+}
+
+void model_put_raw(ModelImpl& m, int kind, int layer, RawTensor&& t) {
+  if (m.finalized) invalid("mlb_model_set_weight: model already finalized");
+  put_pending(m, kind, layer, std::move(t));
+}
+
 static uint64_t stream_id(int kind, int layer) {
   return (uint64_t)kind * (1ull << 20) + (uint64_t)(layer < 0 ? 0 : layer);
 }

@@ -69,6 +69,29 @@ struct ModelImpl {
   size_t step_weight_bytes() const;
 };
 
+// Where an upload of weight (kind, layer) lands on this rank: the full
+// tensor's shape, whether it must be F32, and the shard kept: rows
+// [first, first + count) of the tensor, or for the q/k/v biases (by_cols)
+// columns [first, first + count) of its single row.
+struct WeightSlot {
+  int rows = 0, cols = 0;
+  bool f32_only = false, by_cols = false;
+  int first = 0, count = 0;
+  std::string name;
+};
+WeightSlot model_weight_slot(const ModelImpl& m, int kind, int layer);
+// Hands a shard already on the device to the model (finalize fuses it).
+void model_put_raw(ModelImpl& m, int kind, int layer, RawTensor&& t);
+
+// GGUF files (gguf.cu): a parsed, memory-mapped file; its model config
+// (BuildConfig semantics); the upload of every tensor the model uses (this
+// rank's shards) through pinned staging buffers, returning the bytes copied.
+struct GgufFile;
+GgufFile* gguf_open(const char* path);
+void gguf_close(GgufFile* g);
+mlb_config gguf_config(const GgufFile& g);
+size_t gguf_upload(ModelImpl& m, const GgufFile& g);
+
 struct BatchEngine;  // batch.cu: scratch of one batched pass
 void batch_engine_free(BatchEngine* e);
 

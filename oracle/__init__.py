@@ -241,6 +241,8 @@ class Ref(_Lib):
                                                              ctypes.c_int]
         L.ref_model_create.restype = _vp
         L.ref_model_destroy.argtypes = [_vp]
+        L.ref_model_load_gguf.argtypes = [ctypes.c_char_p]
+        L.ref_model_load_gguf.restype = _vp
         L.ref_model_set_weight.argtypes = [_vp] + [ctypes.c_int] * 5 + [_vp]
         L.ref_model_config.argtypes = [_vp, ctypes.POINTER(ctypes.c_int)]
         L.ref_ctx_create.argtypes = [_vp]
@@ -268,6 +270,13 @@ class Ref(_Lib):
 
     def sampler(self, seed):
         return RefSampler(self, seed)
+
+    def load_gguf(self, path):
+        """A model read by the reference's own LoadGgufModel."""
+        h = self.lib.ref_model_load_gguf(os.fsencode(path))
+        if not h:
+            raise RuntimeError(self.lib.ref_last_error().decode())
+        return RefModel(self, handle=h)
 
 
 class RefSampler:

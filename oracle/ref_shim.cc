@@ -9,9 +9,11 @@
 // (include/mini_llama/ops.h, quant.h), Dequantize*/Quantize* (quant.h),
 // RmsNorm/Softmax/SwiGlu/Rope/ArgMax (ops.h), and ForwardToken on a
 // MiniLlamaModel with cuda_weights == nullptr (forward.h:11), SetThreadCount
-// (thread_pool.h:10) and MiniSampler (sampler.h).
+// (thread_pool.h:10), MiniSampler (sampler.h) and LoadGgufModel
+// (gguf_loader.h).
 #include "mini_llama/context.h"
 #include "mini_llama/forward.h"
+#include "mini_llama/gguf_loader.h"
 #include "mini_llama/model.h"
 #include "mini_llama/ops.h"
 #include "mini_llama/quant.h"
@@ -221,6 +223,23 @@ void* ref_model_create(int vocab_size, int dim, int hidden_dim, int n_layers,
 }
 
 void ref_model_destroy(void* h) { delete static_cast<RefModel*>(h); }
+
+// LoadGgufModel (src/gguf_loader.cc:302-418) on a GGUF file; null (with the
+// model's load_error as the message) when the reference refuses the file.
+void* ref_model_load_gguf(const char* path) {
+  try {
+    auto m = std::make_unique<RefModel>();
+    m->model = LoadGgufModel(path);
+    if (!m->model.loaded) {
+      g_err = m->model.load_error;
+      return nullptr;
+    }
+    return m.release();
+  } catch (const std::exception& e) {
+    Fail(e);
+    return nullptr;
+  }
+}
 
 // kind follows the upload order of src/model.cc:353-369.
 int ref_model_set_weight(void* h, int kind, int layer, int qtype, int rows,
