@@ -60,11 +60,14 @@ def parse_args():
     p.add_argument("--impl", choices=["b200", "reference"], default="b200")
     p.add_argument("--workload", choices=sorted(C.WORKLOADS) + ["gemv-sweep"],
                    default="llama2-7b-q4_0")
-    p.add_argument("--also", type=str, default="llama3-8b-q8_0@32,qwen2-72b-q4_1@32",
-                   help="more workloads timed in the same run: NAME or NAME@BATCH, comma "
-                        "separated ('none' for none)")
+    p.add_argument("--also", type=str,
+                   default="llama3-8b-q8_0@32,qwen2-72b-q4_1@32,qwen2-72b-q4_1@32:bf16",
+                   help="more workloads timed in the same run: NAME, NAME@BATCH or "
+                        "NAME@BATCH:bf16 (bf16 KV cache), comma separated ('none' for none)")
     p.add_argument("--batch-ctx", type=int, default=4096,
                    help="K/V depth of every sequence of the batched workloads")
+    p.add_argument("--batch-kv", choices=["f32", "bf16"], default="f32",
+                   help="KV cache element type of the --batch line")
     p.add_argument("--batch", type=int, default=1,
                    help="B > 1: the line is --workload decoded as B sequences in lockstep "
                         "(the batched engine) at depth --batch-ctx, nothing else")
@@ -545,7 +548,7 @@ def measure_workload(torch, mlb, dist, args, name, cfg, qtype, bias, rank, world
 
 
 def measure_batch(torch, mlb, dist, args, name, cfg, qtype, bias, B, ctx0, rank, world, local,
-                  steps, warmup, peak):
+                  steps, warmup, peak, kv_bf16=False):
     """B sequences decoded in lockstep (mlb_batch_decode_greedy: the tcgen05
     GEMM for every projection, batched attention), each from its own seeded
     K/V state at depth ctx0. Time: CUDA events on the batch stream around the
@@ -570,7 +573,7 @@ def measure_batch(torch, mlb, dist, args, name, cfg, qtype, bias, B, ctx0, rank,
     model = mlb.CudaModel(cfg, device_id=local, tp_rank=rank, tp_size=world, nccl_id=nccl_id)
     model.synthesize(qtype, SEED, with_bias=bias)
     _, step_weights = model.bytes()
-    b = mlb.Batch(model, B)
+    b = mlb.Batch(model, B, kv_type=mlb.KV_BF16 if kv_bf16 else mlb.KV_F32)
     for s in range(B):
         b.fill_kv(s, ctx0, KV_SEED + s, KV_SCALE)
     toks = C.prompt_ids(SEED + 7, B, cfg["vocab_size"])
@@ -594,7 +597,12 @@ def measure_batch(torch, mlb, dist, args, name, cfg, qtype, bias, B, ctx0, rank,
     b.close()
     model.close()
     check = None
-    if rank == 0:
+    if rank == 0 and kv_bf16:
+        check = {"seq_ids_match": None,
+                 "note": "bf16 KV cache: results follow the reference CPU path with K and V "
+                         "rounded to bf16, checked against the C port in "
+                         "tests/test_gpu_batch.py; the fp32 step kernel is not its comparator"}
+    elif rank == 0:
         # Teacher-forced: one GPU's single-sequence step kernel is fed the
         # batch's own ids, and its argmax at every step must be the batch's
         # next id. Where it is not, the step kernel's top-2 margin there is
@@ -621,7 +629,8 @@ def measure_batch(torch, mlb, dist, args, name, cfg, qtype, bias, B, ctx0, rank,
                  "against": "one GPU's single-sequence step kernel, teacher-forced on the "
                             "batch's ids from the same seeded state"}
     barrier()
-    kv_per_pos = 2 * cfg["n_layers"] * (cfg["n_kv_heads"] // world) * cfg["head_dim"] * 4
+    kv_per_pos = 2 * cfg["n_layers"] * (cfg["n_kv_heads"] // world) * cfg["head_dim"] * (
+        2 if kv_bf16 else 4)
     mid_ctx = ctx0 + warmup + steps / 2
     step_bytes = step_weights + B * kv_per_pos * mid_ctx
     step_s = ms / 1e3 / steps
@@ -634,11 +643,13 @@ def measure_batch(torch, mlb, dist, args, name, cfg, qtype, bias, B, ctx0, rank,
                      "bytes_per_step": step_bytes, "weight_bytes": step_weights,
                      "kv_bytes": B * kv_per_pos * mid_ctx,
                      "note": "algorithmic bytes: GGUF weights of this rank once per step + every "
-                             "sequence's fp32 K and V at the mean timed context",
+                             "sequence's K and V (%s) at the mean timed context"
+                             % ("bf16" if kv_bf16 else "fp32"),
                      "peak_source": peak[1] + " (MEASURED_PEAKS.json hbm_gbs, burst)"},
         "clocks": clocks, "parity": check, "greedy_ids_seq0": [int(v) for v in ids[:N_CHECK, 0]],
         "kernels_per_step": kps, "gpu_launches": kps * steps,
         "data": "seeded weights; each sequence's K/V rows seeded to depth ctx; seeded tokens",
+        "kv_cache": "bf16" if kv_bf16 else "fp32",
     }
 
 
@@ -664,6 +675,7 @@ def run_gpu(args, cfg, qtype, bias, rank, world, local):
     extras = []
     for spec in [] if args.also in ("", "none") or args.layers else args.also.split(","):
         name, _, bsz = spec.partition("@")
+        bsz, _, kvt = bsz.partition(":")
         B = int(bsz) if bsz else 1
         if name == args.workload and B == 1:
             continue
@@ -672,8 +684,8 @@ def run_gpu(args, cfg, qtype, bias, rank, world, local):
             if B > 1:
                 r = measure_batch(torch, mlb, dist, args, name, ecfg, eq, eb, B, args.batch_ctx,
                                   rank, world, local, min(args.steps, 16),
-                                  max(3, min(args.warmup, 4)), peak)
-                r["name"] = f"{name}_b{B}"
+                                  max(3, min(args.warmup, 4)), peak, kv_bf16=kvt == "bf16")
+                r["name"] = f"{name}_b{B}" + ("_bf16kv" if kvt == "bf16" else "")
                 extras.append(r)
             else:
                 extras.append(measure_workload(torch, mlb, dist, args, name, ecfg, eq, eb, rank,
@@ -835,7 +847,8 @@ def gguf_load(torch, mlb, cfg, qtype, bias, local, with_ref):
 def run_batch_line(torch, mlb, dist, args, cfg, qtype, bias, rank, world, local, peak):
     """--batch B: one line for --workload decoded as B sequences in lockstep."""
     r = measure_batch(torch, mlb, dist, args, args.workload, cfg, qtype, bias, args.batch,
-                      args.batch_ctx, rank, world, local, args.steps, args.warmup, peak)
+                      args.batch_ctx, rank, world, local, args.steps, args.warmup, peak,
+                      kv_bf16=args.batch_kv == "bf16")
     if rank == 0:
         print(json.dumps({
             "metric": "decode tok/s", "value": r["value"], "unit": "tok/s", "n_gpus": world,
@@ -844,6 +857,7 @@ def run_batch_line(torch, mlb, dist, args, cfg, qtype, bias, rank, world, local,
             "dtype": C.QTYPE_NAMES[qtype] + "/fp32", "data": r["data"],
             "config": {"workload": args.workload + (f" ({args.layers} layers)" if args.layers else ""),
                        "batch": args.batch, "ctx": args.batch_ctx, "parallelism": r["parallelism"],
+                       "kv_cache": r["kv_cache"],
                        "l2": "no flush: each step streams the weights and every sequence's K/V "
                              "(> 126 MB L2)"},
             "roofline": r["roofline"], "parity": r["parity"], "clocks": r["clocks"],

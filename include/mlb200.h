@@ -69,6 +69,12 @@ extern "C" {
 #define MLB_ATTN_CPU_COMPAT 0
 #define MLB_ATTN_STANDARD 1
 
+/* KV cache element types of a batch (mlb_batch_create_kv). F32 is the
+ * reference's CudaKvCache layout and the parity mode; BF16 stores each K and
+ * V value rounded to bf16 (nearest even) and halves the cache's bytes. */
+#define MLB_KV_F32 0
+#define MLB_KV_BF16 1
+
 /* Thread-local message of the last failed call on this thread. */
 const char* mlb_last_error(void);
 
@@ -421,6 +427,13 @@ int mlb_forward_batch(mlb_context* c, int n_tokens, const int* tokens,
  * replaces that many contexts stepping in lockstep. */
 typedef struct mlb_batch mlb_batch;
 int mlb_batch_create(mlb_model* m, int n_seqs, int attention_mode, mlb_batch** out);
+/* The same with the KV cache element type (MLB_KV_F32 or MLB_KV_BF16;
+ * cuda_kv_cache.cc:60-92 keeps fp32 only). A bf16 cache needs head_dim a
+ * multiple of 4 up to 128 and 1, 2, 4 or 8 query heads per KV head; its
+ * results follow the reference CPU path with every K and V value rounded to
+ * bf16 when written, not the fp32 path. */
+int mlb_batch_create_kv(mlb_model* m, int n_seqs, int attention_mode, int kv_type,
+                        mlb_batch** out);
 int mlb_batch_destroy(mlb_batch* b);
 /* Clears every sequence's KV cache. */
 int mlb_batch_reset(mlb_batch* b);

@@ -23,6 +23,7 @@ from .configs import (F32, Q4_0, Q4_1, Q8_0, W_BK, W_BQ, W_BV, W_DOWN, W_FFN_NOR
 
 ROPE_NORMAL, ROPE_NEOX = 0, 1
 ATTN_CPU_COMPAT, ATTN_STANDARD = 0, 1
+KV_F32, KV_BF16 = 0, 1  # MLB_KV_F32, MLB_KV_BF16: KV cache element type of a Batch
 ERR_TIMEOUT = -5  # MLB_ERR_TIMEOUT: a bounded device wait gave up
 
 __all__ = [
@@ -592,11 +593,15 @@ class Sampler:
 class Batch:
     """n_seqs sequences decoded together (mlb_batch_*), each with its own KV cache."""
 
-    def __init__(self, model: CudaModel, n_seqs: int, attention_mode=ATTN_CPU_COMPAT):
+    def __init__(self, model: CudaModel, n_seqs: int, attention_mode=ATTN_CPU_COMPAT,
+                 kv_type: int = 0):
+        """kv_type: KV_F32 (the reference's fp32 cache) or KV_BF16."""
         self.model = model
         self.n_seqs = n_seqs
+        self.kv_type = kv_type
         h = ctypes.c_void_p()
-        check(lib().mlb_batch_create(model.h, int(n_seqs), attention_mode, ctypes.byref(h)))
+        check(lib().mlb_batch_create_kv(model.h, int(n_seqs), attention_mode, int(kv_type),
+                                        ctypes.byref(h)))
         self.h = h
 
     def reset(self):

@@ -103,6 +103,7 @@ SIGNATURES = [
     ("mlb_decode_sample", _c_int, [_vp, _vp, _c_float, _c_int, _c_int, _c_int, _c_int, _vp]),
     ("mlb_forward_batch", _c_int, [_vp, _c_int, _vp, _vp, _vp]),
     ("mlb_batch_create", _c_int, [_vp, _c_int, _c_int, ctypes.POINTER(_vp)]),
+    ("mlb_batch_create_kv", _c_int, [_vp, _c_int, _c_int, _c_int, ctypes.POINTER(_vp)]),
     ("mlb_batch_destroy", _c_int, [_vp]),
     ("mlb_batch_reset", _c_int, [_vp]),
     ("mlb_batch_fill_kv", _c_int, [_vp, _c_int, _c_int, _c_u64, _c_float]),

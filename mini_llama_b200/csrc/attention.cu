@@ -18,6 +18,8 @@
 #include <algorithm>
 #include <cfloat>
 
+#include <cuda_bf16.h>
+
 #include "attention.cuh"
 
 namespace mlb {
@@ -44,6 +46,7 @@ struct AttnKArgs {
   const int* row_pos;
   const int* row_seq;
   long long seq_stride;
+  int kv_bf16;
 };
 
 template <int N>
@@ -312,7 +315,18 @@ __device__ __forceinline__ void rows_multi_sum(float (&v)[NV], int lane) {
 // the current one is computed. The CTA then combines its 8 warps in warp
 // order and, as in the tiled kernel, the last split of a head combines the
 // splits in split order. head_dim is a multiple of 4 and at most 128.
-template <int G, int PB>
+// Four consecutive K or V elements of a row as fp32 (BF: stored as bf16,
+// widened exactly).
+template <bool BF>
+__device__ __forceinline__ float4 kv_load4(const float* base, size_t elem) {
+  if (!BF) return __ldcs(reinterpret_cast<const float4*>(base + elem));
+  const uint2 u = __ldcs(reinterpret_cast<const uint2*>(
+      reinterpret_cast<const __nv_bfloat16*>(base) + elem));
+  return make_float4(__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xffff0000u),
+                     __uint_as_float(u.y << 16), __uint_as_float(u.y & 0xffff0000u));
+}
+
+template <int G, int PB, bool BF>
 __global__ void __launch_bounds__(kRowsThreads, 2) attn_rows_kernel(const AttnKArgs a) {
   constexpr int NV = G * PB;
   static_assert(NV <= 32, "GQA group too large for one pass");
@@ -329,8 +343,6 @@ __global__ void __launch_bounds__(kRowsThreads, 2) attn_rows_kernel(const AttnKA
   pdl_launch_dependents();  // dependents still wait for this grid to complete
   pdl_wait();
   const int seq = a.row_seq ? a.row_seq[row] : row;
-  const float* keys = a.keys + (size_t)seq * a.seq_stride;
-  const float* values = a.values + (size_t)seq * a.seq_stride;
   const float* qrow = a.q + (size_t)row * a.H * D;
   float* outrow = a.out + (size_t)row * a.H * D;
   float* wsrow = a.ws + (size_t)row * KV * a.nsplit * G * (D + 2);
@@ -344,8 +356,8 @@ __global__ void __launch_bounds__(kRowsThreads, 2) attn_rows_kernel(const AttnKA
   const int t_begin = min(n, split * per * PB), t_end = min(n, (split + 1) * per * PB);
   const bool dl = lane < (D >> 2);
   const size_t rstride = (size_t)KV * D;
-  const float* kb = keys + (size_t)kvh * D + 4 * lane;
-  const float* vb = values + (size_t)kvh * D + 4 * lane;
+  // element offset of this lane's 4 values in position 0's row of the sequence
+  const size_t e0 = (size_t)seq * a.seq_stride + (size_t)kvh * D + 4 * lane;
   float4 q[G], o[G];
 #pragma unroll
   for (int h = 0; h < G; ++h) {
@@ -358,11 +370,10 @@ __global__ void __launch_bounds__(kRowsThreads, 2) attn_rows_kernel(const AttnKA
 #pragma unroll
     for (int j = 0; j < PB; ++j) {
       const int t = tb + j;
-      kx[j] = (dl && t < t_end) ? __ldcs(reinterpret_cast<const float4*>(kb + (size_t)t * rstride))
+      kx[j] = (dl && t < t_end) ? kv_load4<BF>(a.keys, e0 + (size_t)t * rstride)
                                 : make_float4(0.f, 0.f, 0.f, 0.f);
-      vx[j] = (dl && t < t_end && t < v_end)
-                  ? __ldcs(reinterpret_cast<const float4*>(vb + (size_t)t * rstride))
-                  : make_float4(0.f, 0.f, 0.f, 0.f);
+      vx[j] = (dl && t < t_end && t < v_end) ? kv_load4<BF>(a.values, e0 + (size_t)t * rstride)
+                                             : make_float4(0.f, 0.f, 0.f, 0.f);
     }
   };
   float4 kn[PB], vn[PB];
@@ -600,6 +611,7 @@ void attn_launch(const AttnLaunch& l, cudaStream_t stream, bool pdl) {
   a.row_pos = l.row_pos;
   a.row_seq = l.row_seq;
   a.seq_stride = l.seq_stride;
+  a.kv_bf16 = l.kv_bf16;
   int dev = 0;
   MLB_CUDA(cudaGetDevice(&dev));
   if (l.rows < 1) invalid("attention: no rows");
@@ -616,16 +628,26 @@ void attn_launch(const AttnLaunch& l, cudaStream_t stream, bool pdl) {
     return;
   }
   const int G = l.H / l.KV;
-  if (l.row_pos && l.D % 4 == 0 && l.D <= 128 && (G == 1 || G == 2 || G == 4 || G == 8)) {
+  const bool rows_ok = l.D % 4 == 0 && l.D <= 128 && (G == 1 || G == 2 || G == 4 || G == 8);
+  if (l.kv_bf16 && (!l.row_pos || !rows_ok))
+    invalid("attention: a bf16 KV cache needs batched rows, head_dim a multiple of 4 up to 128 "
+            "and 1, 2, 4 or 8 query heads per KV head");
+  if (l.row_pos && rows_ok) {
     // batched rows: the register-streaming kernel (its combine keeps G x
     // nsplit split weights in 8 x G x 128 floats)
     a.nsplit = std::max(1, std::min(l.nsplit, kRowsWarps * 128));
     const dim3 grid(l.KV, a.nsplit, l.rows);
+    auto go = [&](auto f32_kernel, auto bf16_kernel) {
+      if (l.kv_bf16)
+        launch_pdl(bf16_kernel, grid, dim3(kRowsThreads), 0, stream, pdl, a);
+      else
+        launch_pdl(f32_kernel, grid, dim3(kRowsThreads), 0, stream, pdl, a);
+    };
     switch (G) {
-      case 1: launch_pdl(attn_rows_kernel<1, 4>, grid, dim3(kRowsThreads), 0, stream, pdl, a); break;
-      case 2: launch_pdl(attn_rows_kernel<2, 4>, grid, dim3(kRowsThreads), 0, stream, pdl, a); break;
-      case 4: launch_pdl(attn_rows_kernel<4, 4>, grid, dim3(kRowsThreads), 0, stream, pdl, a); break;
-      default: launch_pdl(attn_rows_kernel<8, 2>, grid, dim3(kRowsThreads), 0, stream, pdl, a); break;
+      case 1: go(attn_rows_kernel<1, 4, false>, attn_rows_kernel<1, 4, true>); break;
+      case 2: go(attn_rows_kernel<2, 4, false>, attn_rows_kernel<2, 4, true>); break;
+      case 4: go(attn_rows_kernel<4, 4, false>, attn_rows_kernel<4, 4, true>); break;
+      default: go(attn_rows_kernel<8, 2, false>, attn_rows_kernel<8, 2, true>); break;
     }
     return;
   }

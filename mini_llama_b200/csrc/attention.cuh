@@ -26,6 +26,9 @@ struct AttnLaunch {
   const int* row_pos = nullptr;
   const int* row_seq = nullptr;
   long long seq_stride = 0;
+  // Batched rows only: keys/values hold bf16 elements (same element
+  // indexing, two bytes each); the scores and sums stay fp32.
+  int kv_bf16 = 0;
 };
 
 void attn_check(int H, int KV, int D);

@@ -149,14 +149,21 @@ struct BatchEngine {
   }
 
   // The kernels of one pass of `rows` rows on stream s (rows_dev filled).
-  // keys/values: the first sequence's cache, sequences seq_stride floats
-  // apart. Returns the number of kernels launched.
-  int record(int rows, float* keys, float* values, long long seq_stride, cudaStream_t s) {
+  // keys/values: the first sequence's cache, sequences seq_stride elements
+  // apart, fp32 or (kv_bf16) bf16 elements. Returns the number of kernels
+  // launched.
+  int record(int rows, void* keys, void* values, long long seq_stride, bool kv_bf16,
+             cudaStream_t s) {
     const mlb_config& c = m->cfg;
     const int D = c.head_dim;
     const size_t layer_kv = (size_t)c.max_seq_len * m->kv_heads * D;
     const bool tp = m->tp_size > 1;
     int launches = 0;
+    const size_t esz = kv_bf16 ? 2 : 4;
+    // layer l's base of the first sequence's cache, typed as the kernels take it
+    auto kv_at = [&](void* base, int l) {
+      return reinterpret_cast<float*>(static_cast<uint8_t*>(base) + (size_t)l * layer_kv * esz);
+    };
     auto stage = [&](const float* src, int ld, int k, int chunks, const float* norm) {
       tc_stage_launch(src, ld, rows, k, chunks, norm, c.rms_norm_eps, nullptr,
                       staged.as<uint8_t>(), s, true);
@@ -185,16 +192,18 @@ struct BatchEngine {
       e.rope = m->rope.as<float2>();
       e.row_pos = pos();
       e.row_seq = seq();
-      e.keys = keys + l * layer_kv;
-      e.values = values + l * layer_kv;
+      e.keys = kv_at(keys, l);
+      e.values = kv_at(values, l);
       e.seq_stride = seq_stride;
+      e.kv_bf16 = kv_bf16;
       e.q_out = q.as<float>();
       gemm(L.qkv, e);
 
       AttnLaunch al;
       al.q = q.as<float>();
-      al.keys = keys + l * layer_kv;
-      al.values = values + l * layer_kv;
+      al.keys = kv_at(keys, l);
+      al.values = kv_at(values, l);
+      al.kv_bf16 = kv_bf16;
       al.H = m->q_heads;
       al.KV = m->kv_heads;
       al.D = D;
@@ -297,8 +306,9 @@ struct BatchImpl {
   ModelImpl* m = nullptr;
   int n_seqs = 0;
   cudaStream_t stream = nullptr;
-  DevBuf keys, values;  // [n_seqs][L][S][KV_local][D]
-  long long seq_stride = 0;
+  DevBuf keys, values;  // [n_seqs][L][S][KV_local][D], fp32 or bf16 elements
+  long long seq_stride = 0;  // elements
+  bool kv_bf16 = false;
   BatchEngine eng;
   int* h_rows = nullptr;       // pinned [3][64]
   int* h_out = nullptr;        // pinned decode tokens
@@ -334,12 +344,20 @@ static void validate_rows(const ModelImpl& m, int n_seqs, int n, const int* seqs
   }
 }
 
-BatchImpl* batch_create(ModelImpl& m, int n_seqs, int mode) {
+BatchImpl* batch_create(ModelImpl& m, int n_seqs, int mode, int kv_type) {
   if (!m.finalized) invalid("mlb_batch_create: model is not finalized");
   if (n_seqs < 1 || n_seqs > kTcMaxMp)
     invalid("mlb_batch_create: 1 to " + std::to_string(kTcMaxMp) + " sequences");
   if (mode != MLB_ATTN_CPU_COMPAT && mode != MLB_ATTN_STANDARD)
     invalid("mlb_batch_create: unknown attention mode");
+  if (kv_type != MLB_KV_F32 && kv_type != MLB_KV_BF16)
+    invalid("mlb_batch_create: unknown KV cache type");
+  const mlb_config& c0 = m.cfg;
+  const int g = m.q_heads / std::max(m.kv_heads, 1);
+  if (kv_type == MLB_KV_BF16 &&
+      (c0.head_dim % 4 != 0 || c0.head_dim > 128 || (g != 1 && g != 2 && g != 4 && g != 8)))
+    invalid("mlb_batch_create: a bf16 KV cache needs head_dim a multiple of 4 up to 128 and 1, "
+            "2, 4 or 8 query heads per KV head");
   set_device(m.device);
   auto b = std::make_unique<BatchImpl>();
   b->m = &m;
@@ -347,7 +365,8 @@ BatchImpl* batch_create(ModelImpl& m, int n_seqs, int mode) {
   MLB_CUDA(cudaStreamCreateWithFlags(&b->stream, cudaStreamNonBlocking));
   const mlb_config& c = m.cfg;
   b->seq_stride = (long long)c.n_layers * c.max_seq_len * m.kv_heads * c.head_dim;
-  const size_t kv = (size_t)n_seqs * b->seq_stride * 4;
+  b->kv_bf16 = kv_type == MLB_KV_BF16;
+  const size_t kv = (size_t)n_seqs * b->seq_stride * (b->kv_bf16 ? 2 : 4);
   b->keys.alloc(kv);
   b->values.alloc(kv);
   zero_now(b->keys.p, kv);
@@ -367,15 +386,16 @@ void batch_reset(BatchImpl& b) {
 }
 
 // Seeded K/V rows [0, n_pos) of one sequence (the values mlb_context_fill_kv writes).
-void fill_kv_rows(float* keys, float* values, const ModelImpl& m, int n_pos, uint64_t seed,
-                  float scale, cudaStream_t s);
+void fill_kv_rows(void* keys, void* values, bool bf16, const ModelImpl& m, int n_pos,
+                  uint64_t seed, float scale, cudaStream_t s);
 
 void batch_fill_kv(BatchImpl& b, int seq, int n_pos, uint64_t seed, float scale) {
   if (seq < 0 || seq >= b.n_seqs) out_of_range("mlb_batch_fill_kv: sequence id out of range");
   if (n_pos < 0 || n_pos > b.m->cfg.max_seq_len) out_of_range("mlb_batch_fill_kv: n_pos out of range");
   set_device(b.m->device);
-  fill_kv_rows(b.keys.as<float>() + (size_t)seq * b.seq_stride,
-               b.values.as<float>() + (size_t)seq * b.seq_stride, *b.m, n_pos, seed, scale, b.stream);
+  const size_t off = (size_t)seq * b.seq_stride * (b.kv_bf16 ? 2 : 4);
+  fill_kv_rows(b.keys.as<uint8_t>() + off, b.values.as<uint8_t>() + off, b.kv_bf16, *b.m, n_pos,
+               seed, scale, b.stream);
   MLB_CUDA(cudaStreamSynchronize(b.stream));
 }
 
@@ -404,8 +424,8 @@ static void rows_logits_to_host(BatchEngine& e, int rows, float* out, cudaStream
 
 // One pass over host rows; greedy ids (and optionally the logits) to host.
 static void engine_forward(BatchEngine& e, int n, const int* seqs, const int* toks, const int* poss,
-                           float* keys, float* values, long long seq_stride, int* h_rows,
-                           float* logits_host, int* next_host, cudaStream_t s) {
+                           void* keys, void* values, long long seq_stride, bool kv_bf16,
+                           int* h_rows, float* logits_host, int* next_host, cudaStream_t s) {
   const int R = e.max_rows;
   for (int i = 0; i < n; ++i) {
     h_rows[i] = toks[i];
@@ -413,7 +433,7 @@ static void engine_forward(BatchEngine& e, int n, const int* seqs, const int* to
     h_rows[2 * R + i] = seqs ? seqs[i] : 0;
   }
   MLB_CUDA(cudaMemcpyAsync(e.rows_dev.p, h_rows, (size_t)3 * R * 4, cudaMemcpyHostToDevice, s));
-  e.record(n, keys, values, seq_stride, s);
+  e.record(n, keys, values, seq_stride, kv_bf16, s);
   std::vector<unsigned long long> kh(n);
   MLB_CUDA(cudaMemcpyAsync(kh.data(), e.keys_dev.p, (size_t)n * 8, cudaMemcpyDeviceToHost, s));
   MLB_CUDA(cudaMemsetAsync(e.keys_dev.p, 0, (size_t)n * 8, s));
@@ -433,7 +453,7 @@ void batch_forward(BatchImpl& b, int n, const int* seqs, const int* toks, const 
     invalid("mlb_batch_forward: at most " + std::to_string(b.eng.max_rows) + " rows per call");
   validate_rows(*b.m, b.n_seqs, n, seqs, toks, poss);
   set_device(b.m->device);
-  engine_forward(b.eng, n, seqs, toks, poss, b.keys.as<float>(), b.values.as<float>(), b.seq_stride,
+  engine_forward(b.eng, n, seqs, toks, poss, b.keys.p, b.values.p, b.seq_stride, b.kv_bf16,
                  b.h_rows, logits_host, next_host, b.stream);
 }
 
@@ -472,7 +492,7 @@ void batch_decode_greedy(BatchImpl& b, const int* toks, const int* poss, int ste
     MLB_CUDA(cudaStreamBeginCapture(b.stream, cudaStreamCaptureModeThreadLocal));
     int k = 0;
     try {
-      k = e.record(n, b.keys.as<float>(), b.values.as<float>(), b.seq_stride, b.stream);
+      k = e.record(n, b.keys.p, b.values.p, b.seq_stride, b.kv_bf16, b.stream);
       batch_finalize_kernel<<<1, 64, 0, b.stream>>>(e.keys_dev.as<unsigned long long>(), e.tok(),
                                                     e.pos(), n, b.out_dev.as<int>(),
                                                     e.step_dev.as<int>());
@@ -516,9 +536,8 @@ void context_forward_batch(ContextImpl& c, int n, const int* toks, const int* po
     const int k = std::min(kTcMaxMp, n - i0);
     const bool tail = i0 + k == n;
     if (tail) last.resize((size_t)k * V);
-    engine_forward(*c.batch, k, nullptr, toks + i0, poss + i0, c.keys.as<float>(),
-                   c.values.as<float>(), 0, rows.data(), tail ? last.data() : nullptr, nullptr,
-                   c.stream);
+    engine_forward(*c.batch, k, nullptr, toks + i0, poss + i0, c.keys.p, c.values.p, 0, false,
+                   rows.data(), tail ? last.data() : nullptr, nullptr, c.stream);
   }
   std::memcpy(logits_host, last.data() + (last.size() - V), (size_t)V * 4);
 }

@@ -787,7 +787,7 @@ int mlb_nccl_unique_id(void* out128) {
 
 namespace mlb {
 struct BatchImpl;
-BatchImpl* batch_create(ModelImpl& m, int n_seqs, int mode);
+BatchImpl* batch_create(ModelImpl& m, int n_seqs, int mode, int kv_type);
 void batch_destroy(BatchImpl* b);
 void batch_reset(BatchImpl& b);
 void batch_fill_kv(BatchImpl& b, int seq, int n_pos, uint64_t seed, float scale);
@@ -815,7 +815,16 @@ int mlb_forward_batch(mlb_context* c, int n_tokens, const int* tokens, const int
 int mlb_batch_create(mlb_model* m, int n_seqs, int attention_mode, mlb_batch** out) {
   return guarded([&] {
     if (!m || !out) invalid("mlb_batch_create: null pointer");
-    BatchImpl* b = batch_create(*m->impl, n_seqs, attention_mode);
+    BatchImpl* b = batch_create(*m->impl, n_seqs, attention_mode, MLB_KV_F32);
+    *out = new mlb_batch{b};
+  });
+}
+
+int mlb_batch_create_kv(mlb_model* m, int n_seqs, int attention_mode, int kv_type,
+                        mlb_batch** out) {
+  return guarded([&] {
+    if (!m || !out) invalid("mlb_batch_create: null pointer");
+    BatchImpl* b = batch_create(*m->impl, n_seqs, attention_mode, kv_type);
     *out = new mlb_batch{b};
   });
 }

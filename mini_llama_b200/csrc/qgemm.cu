@@ -23,6 +23,8 @@
 // (bounded), TMEM is released and the CTA exits.
 #include "qgemm.cuh"
 
+#include <cuda_bf16.h>
+
 #include <algorithm>
 
 namespace mlb {
@@ -404,6 +406,14 @@ __device__ __forceinline__ bool tc_wait(uint64_t* bar, uint32_t parity, TcShared
   return true;
 }
 
+// One KV-cache element: fp32, or bf16 rounded to nearest even.
+__device__ __forceinline__ void kv_store(float* base, int bf16, size_t i, float v) {
+  if (bf16)
+    reinterpret_cast<__nv_bfloat16*>(base)[i] = __float2bfloat16_rn(v);
+  else
+    base[i] = v;
+}
+
 // The fused epilogue of one warp slice: rows n (this lane's) of a tile and
 // batch columns cbase .. cbase + NC - 1, values v.
 template <int NC>
@@ -463,7 +473,7 @@ __device__ __forceinline__ void tc_epilogue(const BEpi& e, int n, int lr, int la
       const int pos = e.row_pos[r];
       const int seq = e.row_seq ? e.row_seq[r] : r;
       if (sec == 2) {
-        e.values[(size_t)seq * e.seq_stride + (size_t)pos * e.kv_rows + L] = val;
+        kv_store(e.values, e.kv_bf16, (size_t)seq * e.seq_stride + (size_t)pos * e.kv_rows + L, val);
         continue;
       }
       // rotation of (this, partner) as src/ops.cc:155-156 / 174-175
@@ -474,7 +484,7 @@ __device__ __forceinline__ void tc_epilogue(const BEpi& e, int n, int lr, int la
       if (sec == 0)
         e.q_out[(size_t)r * e.q_rows + L] = out;
       else
-        e.keys[(size_t)seq * e.seq_stride + (size_t)pos * e.kv_rows + L] = out;
+        kv_store(e.keys, e.kv_bf16, (size_t)seq * e.seq_stride + (size_t)pos * e.kv_rows + L, out);
     }
     return;
   }

@@ -62,6 +62,7 @@ struct BEpi {
   float* keys;
   float* values;
   long long seq_stride;
+  int kv_bf16;         // keys/values hold bf16 elements (rounded to nearest even)
   float* q_out;        // [rows][q_rows]
   // greedy argmax per batch row (kEpiStore): keys_out[r] folds
   // argmax_key_of(value, argmax_base + n) with atomicMax

@@ -17,6 +17,7 @@
 // With tensor parallelism, wo and down write partial sums that an NCCL
 // all-reduce combines before the residual add, and the vocabulary-sharded
 // lm_head logits are all-gathered.
+#include <cuda_bf16.h>
 #include "runtime.cuh"
 #include "sample.cuh"
 
@@ -1170,7 +1171,17 @@ namespace mlb {
 // gauss(key, (pos * KV + head) * D + d) * scale, keys of streams 15 * 2^20 + l
 // (K) and 16 * 2^20 + l (V) -- a decode state at depth n_pos without running
 // n_pos steps (the CPU oracle writes the same values).
-__global__ void fill_kv_kernel(float* keys, float* values, int L, int S, int KVl, int KV, int kv0,
+template <class T>
+__device__ __forceinline__ T kv_value(float v);
+template <>
+__device__ __forceinline__ float kv_value<float>(float v) { return v; }
+template <>
+__device__ __forceinline__ __nv_bfloat16 kv_value<__nv_bfloat16>(float v) {
+  return __float2bfloat16_rn(v);
+}
+
+template <class T>
+__global__ void fill_kv_kernel(T* keys, T* values, int L, int S, int KVl, int KV, int kv0,
                                int D, int n_pos, uint64_t seed, float scale) {
   const long long per_layer = (long long)n_pos * KVl * D;
   const long long total = per_layer * L;
@@ -1185,18 +1196,25 @@ __global__ void fill_kv_kernel(float* keys, float* values, int L, int S, int KVl
     const uint64_t kk = synth::stream_key(seed, 15ull * (1ull << 20) + (uint64_t)l);
     const uint64_t kv = synth::stream_key(seed, 16ull * (1ull << 20) + (uint64_t)l);
     const size_t o = (((size_t)l * S + p) * KVl + h) * D + d;
-    keys[o] = synth::fmul(synth::gauss(kk, idx), scale);
-    values[o] = synth::fmul(synth::gauss(kv, idx), scale);
+    keys[o] = kv_value<T>(synth::fmul(synth::gauss(kk, idx), scale));
+    values[o] = kv_value<T>(synth::fmul(synth::gauss(kv, idx), scale));
   }
 }
 
-void fill_kv_rows(float* keys, float* values, const ModelImpl& m, int n_pos, uint64_t seed,
-                  float scale, cudaStream_t s) {
+void fill_kv_rows(void* keys, void* values, bool bf16, const ModelImpl& m, int n_pos,
+                  uint64_t seed, float scale, cudaStream_t s) {
   const mlb_config& cf = m.cfg;
   if (n_pos <= 0) return;
-  fill_kv_kernel<<<sm_count(m.device) * 8, 256, 0, s>>>(keys, values, cf.n_layers,
-                                                       cf.max_seq_len, m.kv_heads, cf.n_kv_heads,
-                                                       m.kv_head0, cf.head_dim, n_pos, seed, scale);
+  const int grid = sm_count(m.device) * 8;
+  if (bf16)
+    fill_kv_kernel<<<grid, 256, 0, s>>>(static_cast<__nv_bfloat16*>(keys),
+                                       static_cast<__nv_bfloat16*>(values), cf.n_layers,
+                                       cf.max_seq_len, m.kv_heads, cf.n_kv_heads, m.kv_head0,
+                                       cf.head_dim, n_pos, seed, scale);
+  else
+    fill_kv_kernel<<<grid, 256, 0, s>>>(static_cast<float*>(keys), static_cast<float*>(values),
+                                       cf.n_layers, cf.max_seq_len, m.kv_heads, cf.n_kv_heads,
+                                       m.kv_head0, cf.head_dim, n_pos, seed, scale);
   MLB_CUDA(cudaGetLastError());
 }
 
@@ -1204,7 +1222,7 @@ void context_fill_kv(ContextImpl& c, int n_pos, uint64_t seed, float scale) {
   const mlb_config& cf = c.m->cfg;
   if (n_pos < 0 || n_pos > cf.max_seq_len) out_of_range("mlb_context_fill_kv: n_pos out of range");
   set_device(c.m->device);
-  fill_kv_rows(c.keys.as<float>(), c.values.as<float>(), *c.m, n_pos, seed, scale, c.stream);
+  fill_kv_rows(c.keys.p, c.values.p, false, *c.m, n_pos, seed, scale, c.stream);
   MLB_CUDA(cudaStreamSynchronize(c.stream));
 }
 

@@ -172,6 +172,10 @@ class Port(_Lib):
         L.mlp_ctx_create.argtypes = [_vp]
         L.mlp_ctx_create.restype = _vp
         L.mlp_ctx_destroy.argtypes = [_vp]
+        L.mlp_ctx_set_kv_bf16.argtypes = [_vp, ctypes.c_int]
+        L.mlp_ctx_set_kv_bf16.restype = None
+        L.mlp_ctx_kv.argtypes = [_vp, ctypes.POINTER(_vp), ctypes.POINTER(_vp)]
+        L.mlp_ctx_kv.restype = None
         L.mlp_forward_token.argtypes = [_vp, ctypes.c_int, ctypes.c_int, _f]
 
     def attention(self, q, keys, values, layer, pos, n_heads, n_kv_heads, head_dim,
@@ -213,11 +217,30 @@ class PortModel:
         self.port._check(self.port.lib.mlp_model_set_weight(
             self.h, kind, layer, qtype, rows, cols, _ptr(data), data.nbytes))
 
-    def forward_token(self, token, pos):
+    def _context(self):
         if self.ctx is None:
             self.ctx = self.port.lib.mlp_ctx_create(self.h)
             if not self.ctx:
                 raise MemoryError("mlp_ctx_create failed")
+        return self.ctx
+
+    def set_kv_bf16(self, on: bool):
+        """K and V rounded to bf16 when written (the GPU's bf16 cache option;
+        not a reference mode)."""
+        self.port.lib.mlp_ctx_set_kv_bf16(self._context(), int(on))
+
+    def kv_cache(self):
+        """(keys, values) views [L, max_seq, KV, D] of the context's cache."""
+        k, v = _vp(), _vp()
+        self.port.lib.mlp_ctx_kv(self._context(), ctypes.byref(k), ctypes.byref(v))
+        shape = (self.cfg["n_layers"], self.cfg["max_seq_len"], self.cfg["n_kv_heads"],
+                 self.cfg["head_dim"])
+        n = int(np.prod(shape))
+        as_arr = lambda p: np.ctypeslib.as_array((ctypes.c_float * n).from_address(p.value)).reshape(shape)  # noqa: E731
+        return as_arr(k), as_arr(v)
+
+    def forward_token(self, token, pos):
+        self._context()
         out = np.zeros(self.cfg["vocab_size"], np.float32)
         self.port._check(self.port.lib.mlp_forward_token(self.ctx, token, pos, _fptr(out)))
         return out

@@ -10,6 +10,7 @@
 #include <math.h>
 #include <stdio.h>
 #include <stdlib.h>
+#include <stdint.h>
 #include <string.h>
 
 static __thread char g_err[512];
@@ -422,6 +423,7 @@ struct mlp_ctx {
   mlp_model* m;
   float* keys;
   float* values;
+  int kv_bf16; /* K and V rounded to bf16 when written (not a reference mode) */
   /* scratch */
   float *x, *h, *q, *k, *v, *att, *proj, *gate, *up, *act;
 };
@@ -507,6 +509,25 @@ void mlp_ctx_destroy(mlp_ctx* c) {
   free(c);
 }
 
+/* x rounded to the nearest bf16 (ties to even), kept as a float: the value a
+ * bf16 KV cache stores. Not part of the reference, which keeps fp32 K/V; the
+ * switch mirrors the GPU library's bf16 cache option. */
+static float bf16_round(float x) {
+  uint32_t u;
+  memcpy(&u, &x, 4);
+  if ((u & 0x7f800000u) != 0x7f800000u) u += 0x7fffu + ((u >> 16) & 1u);
+  u &= 0xffff0000u;
+  memcpy(&x, &u, 4);
+  return x;
+}
+
+void mlp_ctx_set_kv_bf16(mlp_ctx* c, int on) { c->kv_bf16 = on; }
+
+void mlp_ctx_kv(mlp_ctx* c, float** keys, float** values) {
+  *keys = c->keys;
+  *values = c->values;
+}
+
 static int lin(const weight_t* w, const float* x, float* y) {
   return mlp_linear(w->qtype, x, 1, w->cols, w->data, w->rows, y);
 }
@@ -549,6 +570,11 @@ int mlp_forward_token(mlp_ctx* cx, int token, int pos, float* logits) {
     add_bias(cx->v, W(MLP_W_BV));
     mlp_rope(cx->q, c->n_heads, cx->k, c->n_kv_heads, c->head_dim, pos,
              c->rope_theta, c->rope_type);
+    if (cx->kv_bf16)
+      for (size_t i = 0; i < kd; ++i) {
+        cx->k[i] = bf16_round(cx->k[i]);
+        cx->v[i] = bf16_round(cx->v[i]);
+      }
     size_t slot_off = ((size_t)l * c->max_seq_len + pos) * kd;
     memcpy(cx->keys + slot_off, cx->k, kd * sizeof(float));
     memcpy(cx->values + slot_off, cx->v, kd * sizeof(float));

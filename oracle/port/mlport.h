@@ -86,6 +86,11 @@ mlp_ctx* mlp_ctx_create(mlp_model* m);
 void mlp_ctx_destroy(mlp_ctx* c);
 /* ForwardToken: writes vocab_size logits. Returns 0 or a negative error. */
 int mlp_forward_token(mlp_ctx* c, int token, int pos, float* logits);
+/* Not a reference mode: K and V rounded to bf16 (nearest even) when written
+ * to the cache, the GPU library's bf16 KV option. */
+void mlp_ctx_set_kv_bf16(mlp_ctx* c, int on);
+/* The context's fp32 KV cache arrays [L][max_seq][KV][D] (tests fill them). */
+void mlp_ctx_kv(mlp_ctx* c, float** keys, float** values);
 const char* mlp_last_error(void);
 
 #ifdef __cplusplus

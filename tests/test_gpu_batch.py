@@ -169,3 +169,69 @@ def test_batch32_full_width_vs_reference(cuda, ref, workload, layers, steps, n_r
         for i in range(steps):
             tok = int(np.argmax(rm.forward_token(tok, depths[s] + i)))
             assert tok == int(got[i, s]), (s, i)
+
+
+def port_fill_kv(pm, n_pos, seed, scale=1.25, bf16=False):
+    """The values mlb_batch_fill_kv writes (mlb_context_fill_kv's definition:
+    generator streams 15 * 2^20 + l for K, 16 * 2^20 + l for V, element index
+    (pos * KV + kv_head) * D + d, times scale), into the C port's cache,
+    rounded to bf16 when the cache is bf16."""
+    from mini_llama_b200 import _lib
+
+    cfg = pm.cfg
+    kd = cfg["n_kv_heads"] * cfg["head_dim"]
+    keys, values = pm.kv_cache()
+    s = _lib.synth_lib()
+    for layer in range(cfg["n_layers"]):
+        for kind, dst in ((15, keys), (16, values)):
+            out = np.empty((n_pos, kd), np.float32)
+            s.mlbs_f32(C.stream_key(seed, kind, layer), scale, 0, n_pos, 0, kd, kd,
+                       out.ctypes.data, 4)
+            if bf16:
+                u = out.view(np.uint32).astype(np.uint64)
+                u = (u + 0x7FFF + ((u >> 16) & 1)) & 0xFFFF0000
+                out = u.astype(np.uint32).view(np.float32)
+            dst[layer, :n_pos] = out.reshape(n_pos, cfg["n_kv_heads"], cfg["head_dim"])
+
+
+@pytest.mark.parametrize("name", ["small_q4_0_gqa", "small_q4_1_neox_bias"])
+def test_batch_bf16_kv_cache_matches_oracle(cuda, port, name):
+    """A bf16 KV cache (mlb_batch_create_kv, MLB_KV_BF16): sequences at
+    different depths decoded in lockstep against the C port with every K and V
+    value rounded to bf16 when written (the seeded fill included): greedy ids
+    equal, and one pass's logits within the bar."""
+    mt = meta()[name]
+    cfg = mt["config"]
+    qtype = {v: k for k, v in C.QTYPE_NAMES.items()}[mt["qtype"]]
+    model = mlb.CudaModel(cfg).synthesize(qtype, 17, with_bias=mt["bias"])
+    n_seqs, steps = 4, 8
+    depths = [0, 5, 11, 2]
+    toks = [3, 77, 150, 9]
+    b = mlb.Batch(model, n_seqs, kv_type=mlb.KV_BF16)
+    for s in range(n_seqs):
+        b.fill_kv(s, depths[s], 100 + s)
+    got = b.decode_greedy(toks, depths, steps)
+    for s in range(n_seqs):
+        pm = port_model(port, cfg, qtype, 17, mt["bias"])
+        pm.set_kv_bf16(True)
+        port_fill_kv(pm, depths[s], 100 + s, bf16=True)
+        tok = toks[s]
+        for i in range(steps):
+            tok = int(np.argmax(pm.forward_token(tok, depths[s] + i)))
+            assert tok == int(got[i, s]), (s, i)
+    # one pass with logits against the port
+    b2 = mlb.Batch(model, 2, kv_type=mlb.KV_BF16)
+    pm = port_model(port, cfg, qtype, 17, mt["bias"])
+    pm.set_kv_bf16(True)
+    for pos, t in enumerate([5, 6, 7, 8]):
+        _, lg = b2.forward([0, 1], [t, t], [pos, pos], logits=True)
+        lp = pm.forward_token(t, pos)
+        assert np.abs(lg[0] - lp).max() <= LOGIT_TOL
+        assert np.array_equal(lg[0], lg[1])
+
+
+def test_batch_kv_type_validation(cuda):
+    cfg = meta()["small_q4_0_gqa"]["config"]
+    model = mlb.CudaModel(cfg).synthesize(C.Q4_0, 3)
+    with pytest.raises(mlb.MlbError, match="unknown KV cache type"):
+        mlb.Batch(model, 2, kv_type=7)
