@@ -317,14 +317,30 @@ __device__ __forceinline__ void rows_multi_sum(float (&v)[NV], int lane) {
 // splits in split order. head_dim is a multiple of 4 and at most 128.
 // Four consecutive K or V elements of a row as fp32 (BF: stored as bf16,
 // widened exactly).
+// Four consecutive K or V elements of a row as loaded (fp32: a float4; bf16:
+// a uint2, widened only when the block is used, so a prefetch does not wait
+// for its own data) and as fp32.
 template <bool BF>
-__device__ __forceinline__ float4 kv_load4(const float* base, size_t elem) {
-  if (!BF) return __ldcs(reinterpret_cast<const float4*>(base + elem));
-  const uint2 u = __ldcs(reinterpret_cast<const uint2*>(
-      reinterpret_cast<const __nv_bfloat16*>(base) + elem));
-  return make_float4(__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xffff0000u),
-                     __uint_as_float(u.y << 16), __uint_as_float(u.y & 0xffff0000u));
-}
+struct KvRaw {
+  using T = float4;
+  static __device__ __forceinline__ T load(const void* p) {
+    return __ldcs(static_cast<const float4*>(p));
+  }
+  static __device__ __forceinline__ T zero() { return make_float4(0.f, 0.f, 0.f, 0.f); }
+  static __device__ __forceinline__ float4 widen(const T& v) { return v; }
+};
+template <>
+struct KvRaw<true> {
+  using T = uint2;
+  static __device__ __forceinline__ T load(const void* p) {
+    return __ldcs(static_cast<const uint2*>(p));
+  }
+  static __device__ __forceinline__ T zero() { return make_uint2(0u, 0u); }
+  static __device__ __forceinline__ float4 widen(const T& u) {
+    return make_float4(__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xffff0000u),
+                       __uint_as_float(u.y << 16), __uint_as_float(u.y & 0xffff0000u));
+  }
+};
 
 template <int G, int PB, bool BF>
 __global__ void __launch_bounds__(kRowsThreads, 2) attn_rows_kernel(const AttnKArgs a) {
@@ -356,8 +372,13 @@ __global__ void __launch_bounds__(kRowsThreads, 2) attn_rows_kernel(const AttnKA
   const int t_begin = min(n, split * per * PB), t_end = min(n, (split + 1) * per * PB);
   const bool dl = lane < (D >> 2);
   const size_t rstride = (size_t)KV * D;
-  // element offset of this lane's 4 values in position 0's row of the sequence
-  const size_t e0 = (size_t)seq * a.seq_stride + (size_t)kvh * D + 4 * lane;
+  // this lane's 4 values in position 0's row of the sequence, and the bytes
+  // from one position's row to the next
+  constexpr size_t esz = BF ? 2 : 4;
+  const size_t e0 = ((size_t)seq * a.seq_stride + (size_t)kvh * D + 4 * lane) * esz;
+  const uint8_t* kb = reinterpret_cast<const uint8_t*>(a.keys) + e0;
+  const uint8_t* vb = reinterpret_cast<const uint8_t*>(a.values) + e0;
+  const size_t rbytes = rstride * esz;
   float4 q[G], o[G];
 #pragma unroll
   for (int h = 0; h < G; ++h) {
@@ -366,25 +387,25 @@ __global__ void __launch_bounds__(kRowsThreads, 2) attn_rows_kernel(const AttnKA
     o[h] = make_float4(0.f, 0.f, 0.f, 0.f);
   }
   float m_run = -INFINITY, l_run = 0.0f;  // lane i < NV: head i / PB
-  auto load_block = [&](int tb, float4 (&kx)[PB], float4 (&vx)[PB]) {
+  using Raw = KvRaw<BF>;
+  using RawT = typename Raw::T;
+  auto load_block = [&](int tb, RawT (&kx)[PB], RawT (&vx)[PB]) {
 #pragma unroll
     for (int j = 0; j < PB; ++j) {
       const int t = tb + j;
-      kx[j] = (dl && t < t_end) ? kv_load4<BF>(a.keys, e0 + (size_t)t * rstride)
-                                : make_float4(0.f, 0.f, 0.f, 0.f);
-      vx[j] = (dl && t < t_end && t < v_end) ? kv_load4<BF>(a.values, e0 + (size_t)t * rstride)
-                                             : make_float4(0.f, 0.f, 0.f, 0.f);
+      kx[j] = (dl && t < t_end) ? Raw::load(kb + (size_t)t * rbytes) : Raw::zero();
+      vx[j] = (dl && t < t_end && t < v_end) ? Raw::load(vb + (size_t)t * rbytes) : Raw::zero();
     }
   };
-  float4 kn[PB], vn[PB];
+  RawT kn[PB], vn[PB];
   const int tb0 = t_begin + warp * PB;
   if (tb0 < t_end) load_block(tb0, kn, vn);
   for (int tb = tb0; tb < t_end; tb += kRowsWarps * PB) {
     float4 kx[PB], vx[PB];
 #pragma unroll
     for (int j = 0; j < PB; ++j) {
-      kx[j] = kn[j];
-      vx[j] = vn[j];
+      kx[j] = Raw::widen(kn[j]);
+      vx[j] = Raw::widen(vn[j]);
     }
     if (tb + kRowsWarps * PB < t_end) load_block(tb + kRowsWarps * PB, kn, vn);
     float dv[NV];
