@@ -317,6 +317,12 @@ int mlb_model_bytes(const mlb_model* m, size_t* resident, size_t* per_step_weigh
  * CudaKvCache::Reset src/cuda_kv_cache.cc:60-92): allocates and zeroes the
  * fp32 KV cache for max_seq_len positions and all decode buffers once. */
 int mlb_context_create(mlb_model* m, int attention_mode, mlb_context** out);
+/* The same with the KV cache element type (MLB_KV_F32 or MLB_KV_BF16; the
+ * reference's CudaKvCache is fp32 only). A bf16 cache runs on the decode step
+ * kernel only (models the step kernel cannot take are refused, and
+ * mlb_context_set_step_kernel(c, 0) fails); its results follow the reference
+ * CPU path with every K and V value rounded to bf16 when written. */
+int mlb_context_create_kv(mlb_model* m, int attention_mode, int kv_type, mlb_context** out);
 int mlb_context_destroy(mlb_context* c);
 /* Clears the KV cache (CudaKvCache::Clear, src/cuda_kv_cache.cc:96-110). */
 int mlb_context_reset(mlb_context* c);

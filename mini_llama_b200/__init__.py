@@ -445,8 +445,8 @@ class CudaModel:
         check(lib().mlb_model_bytes(self.h, ctypes.byref(r), ctypes.byref(s)))
         return r.value, s.value
 
-    def context(self, attention_mode=ATTN_CPU_COMPAT, step_kernel=None):
-        return Context(self, attention_mode, step_kernel)
+    def context(self, attention_mode=ATTN_CPU_COMPAT, step_kernel=None, kv_type=0):
+        return Context(self, attention_mode, step_kernel, kv_type)
 
     def close(self):
         if getattr(self, "h", None):
@@ -463,10 +463,12 @@ class CudaModel:
 class Context:
     """MiniLlamaContext with its CUDA KV cache (include/mini_llama/context.h)."""
 
-    def __init__(self, model: CudaModel, attention_mode=ATTN_CPU_COMPAT, step_kernel=None):
+    def __init__(self, model: CudaModel, attention_mode=ATTN_CPU_COMPAT, step_kernel=None,
+                 kv_type: int = 0):
+        """kv_type: KV_F32 (the reference's fp32 cache) or KV_BF16 (step kernel only)."""
         self.model = model
         h = ctypes.c_void_p()
-        check(lib().mlb_context_create(model.h, attention_mode, ctypes.byref(h)))
+        check(lib().mlb_context_create_kv(model.h, attention_mode, int(kv_type), ctypes.byref(h)))
         self.h = h
         self.pos = 0
         self.token_history = []

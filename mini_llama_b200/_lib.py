@@ -82,6 +82,7 @@ SIGNATURES = [
     ("mlb_model_load_gguf", _c_int, [ctypes.c_char_p, _c_int, _c_int, _c_int, _vp, _c_int,
                                      ctypes.POINTER(_vp), ctypes.POINTER(_c_size_t)]),
     ("mlb_context_create", _c_int, [_vp, _c_int, ctypes.POINTER(_vp)]),
+    ("mlb_context_create_kv", _c_int, [_vp, _c_int, _c_int, ctypes.POINTER(_vp)]),
     ("mlb_context_destroy", _c_int, [_vp]),
     ("mlb_context_reset", _c_int, [_vp]),
     ("mlb_context_fill_kv", _c_int, [_vp, _c_int, _c_u64, _c_float]),

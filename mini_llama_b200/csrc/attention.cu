@@ -317,31 +317,6 @@ __device__ __forceinline__ void rows_multi_sum(float (&v)[NV], int lane) {
 // splits in split order. head_dim is a multiple of 4 and at most 128.
 // Four consecutive K or V elements of a row as fp32 (BF: stored as bf16,
 // widened exactly).
-// Four consecutive K or V elements of a row as loaded (fp32: a float4; bf16:
-// a uint2, widened only when the block is used, so a prefetch does not wait
-// for its own data) and as fp32.
-template <bool BF>
-struct KvRaw {
-  using T = float4;
-  static __device__ __forceinline__ T load(const void* p) {
-    return __ldcs(static_cast<const float4*>(p));
-  }
-  static __device__ __forceinline__ T zero() { return make_float4(0.f, 0.f, 0.f, 0.f); }
-  static __device__ __forceinline__ float4 widen(const T& v) { return v; }
-};
-template <>
-struct KvRaw<true> {
-  using T = uint2;
-  static __device__ __forceinline__ T load(const void* p) {
-    return __ldcs(static_cast<const uint2*>(p));
-  }
-  static __device__ __forceinline__ T zero() { return make_uint2(0u, 0u); }
-  static __device__ __forceinline__ float4 widen(const T& u) {
-    return make_float4(__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xffff0000u),
-                       __uint_as_float(u.y << 16), __uint_as_float(u.y & 0xffff0000u));
-  }
-};
-
 template <int G, int PB, bool BF>
 __global__ void __launch_bounds__(kRowsThreads, 2) attn_rows_kernel(const AttnKArgs a) {
   constexpr int NV = G * PB;

@@ -536,7 +536,7 @@ void context_forward_batch(ContextImpl& c, int n, const int* toks, const int* po
     const int k = std::min(kTcMaxMp, n - i0);
     const bool tail = i0 + k == n;
     if (tail) last.resize((size_t)k * V);
-    engine_forward(*c.batch, k, nullptr, toks + i0, poss + i0, c.keys.p, c.values.p, 0, false,
+    engine_forward(*c.batch, k, nullptr, toks + i0, poss + i0, c.keys.p, c.values.p, 0, c.kv_bf16,
                    rows.data(), tail ? last.data() : nullptr, nullptr, c.stream);
   }
   std::memcpy(logits_host, last.data() + (last.size() - V), (size_t)V * 4);

@@ -64,7 +64,7 @@ void model_set_weight(ModelImpl& m, int kind, int layer, int qtype, int rows, in
                       const void* data, size_t bytes);
 void model_synthesize(ModelImpl& m, int qtype, uint64_t seed, int with_bias);
 void model_finalize(ModelImpl& m);
-ContextImpl* context_create(ModelImpl& m, int mode);
+ContextImpl* context_create(ModelImpl& m, int mode, int kv_type);
 void context_step_async(ContextImpl& c, int token, int pos);
 void context_forward_token(ContextImpl& c, int token, int pos, float* logits_host);
 void context_decode_greedy(ContextImpl& c, int token, int pos, int n, int* tokens_host);
@@ -575,7 +575,14 @@ int mlb_model_bytes(const mlb_model* m, size_t* resident, size_t* per_step) {
 int mlb_context_create(mlb_model* m, int attention_mode, mlb_context** out) {
   return guarded([&] {
     if (!m || !out) invalid("mlb_context_create: null pointer");
-    *out = new mlb_context{context_create(*m->impl, attention_mode)};
+    *out = new mlb_context{context_create(*m->impl, attention_mode, MLB_KV_F32)};
+  });
+}
+
+int mlb_context_create_kv(mlb_model* m, int attention_mode, int kv_type, mlb_context** out) {
+  return guarded([&] {
+    if (!m || !out) invalid("mlb_context_create: null pointer");
+    *out = new mlb_context{context_create(*m->impl, attention_mode, kv_type)};
   });
 }
 

@@ -105,6 +105,31 @@ __device__ __forceinline__ void pdl_launch_dependents() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
+// Four consecutive KV-cache elements as loaded (fp32: a float4; bf16: a
+// uint2, widened only when used, so a prefetch does not wait for its own data)
+// and as fp32. bf16 -> fp32 is exact (the high half of the fp32 bits).
+template <bool BF>
+struct KvRaw {
+  using T = float4;
+  static __device__ __forceinline__ T load(const void* p) {
+    return __ldcs(static_cast<const float4*>(p));
+  }
+  static __device__ __forceinline__ T zero() { return make_float4(0.f, 0.f, 0.f, 0.f); }
+  static __device__ __forceinline__ float4 widen(const T& v) { return v; }
+};
+template <>
+struct KvRaw<true> {
+  using T = uint2;
+  static __device__ __forceinline__ T load(const void* p) {
+    return __ldcs(static_cast<const uint2*>(p));
+  }
+  static __device__ __forceinline__ T zero() { return make_uint2(0u, 0u); }
+  static __device__ __forceinline__ float4 widen(const T& u) {
+    return make_float4(__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xffff0000u),
+                       __uint_as_float(u.y << 16), __uint_as_float(u.y & 0xffff0000u));
+  }
+};
+
 __device__ __forceinline__ uint32_t smem_addr(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }

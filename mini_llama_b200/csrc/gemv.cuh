@@ -79,6 +79,7 @@ struct EpiParams {
   const int* pos;             // device scalar
   float* keys;                // cache slot base of this layer: + pos * kv_rows
   float* values;
+  int kv_bf16;                // the cache holds bf16 elements (rounded to nearest even)
   float* q_out;
   // Greedy argmax fused into a store epilogue (batch row 0): every finished
   // tile folds its rows into *argmax_key with atomicMax on

@@ -15,6 +15,8 @@
 // independent of timing.
 #pragma once
 
+#include <cuda_bf16.h>
+
 #include "gemv.cuh"
 
 namespace mlb {
@@ -265,7 +267,11 @@ __device__ float epilogue_row(const EpiParams& p, int tile, int row, int r, cons
       if (p.bias) v = __fadd_rn(v, p.bias[bias_base + L]);
       int pos = p.pos_set ? p.pos_now : *p.pos;
       if (sec == 2) {
-        p.values[(size_t)pos * p.kv_rows + L] = v;
+        if (p.kv_bf16)
+          reinterpret_cast<__nv_bfloat16*>(p.values)[(size_t)pos * p.kv_rows + L] =
+              __float2bfloat16_rn(v);
+        else
+          p.values[(size_t)pos * p.kv_rows + L] = v;
         break;
       }
       int partner = local ^ 1;
@@ -289,6 +295,9 @@ __device__ float epilogue_row(const EpiParams& p, int tile, int row, int r, cons
         out = __fadd_rn(__fmul_rn(w, cs.y), __fmul_rn(v, cs.x));
       if (sec == 0)
         p.q_out[(size_t)r * p.q_rows + L] = out;
+      else if (p.kv_bf16)
+        reinterpret_cast<__nv_bfloat16*>(p.keys)[(size_t)pos * p.kv_rows + L] =
+            __float2bfloat16_rn(out);
       else
         p.keys[(size_t)pos * p.kv_rows + L] = out;
       break;

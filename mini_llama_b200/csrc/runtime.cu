@@ -505,17 +505,27 @@ ContextImpl::~ContextImpl() {
   if (stream) cudaStreamDestroy(stream);
 }
 
-ContextImpl* context_create(ModelImpl& m, int mode) {
+float* ContextImpl::kv_layer(const DevBuf& b, int l) const {
+  const mlb_config& cf = m->cfg;
+  const size_t layer_elems = (size_t)cf.max_seq_len * m->kv_heads * cf.head_dim;
+  return reinterpret_cast<float*>(b.as<uint8_t>() + (size_t)l * layer_elems * (kv_bf16 ? 2 : 4));
+}
+
+ContextImpl* context_create(ModelImpl& m, int mode, int kv_type) {
   if (!m.finalized) invalid("mlb_context_create: model is not finalized");
   if (mode != MLB_ATTN_CPU_COMPAT && mode != MLB_ATTN_STANDARD)
     invalid("mlb_context_create: unknown attention mode");
+  if (kv_type != MLB_KV_F32 && kv_type != MLB_KV_BF16)
+    invalid("mlb_context_create: unknown KV cache type");
   set_device(m.device);
   auto c = std::make_unique<ContextImpl>();
   c->m = &m;
   c->attention_mode = mode;
   MLB_CUDA(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking));
   const mlb_config& cf = m.cfg;
-  const size_t kv = (size_t)cf.n_layers * cf.max_seq_len * m.kv_heads * cf.head_dim * 4;
+  c->kv_bf16 = kv_type == MLB_KV_BF16;
+  const size_t kv =
+      (size_t)cf.n_layers * cf.max_seq_len * m.kv_heads * cf.head_dim * (c->kv_bf16 ? 2 : 4);
   c->keys.alloc(kv);
   c->values.alloc(kv);
   zero_now(c->keys.p, kv);
@@ -561,6 +571,9 @@ ContextImpl* context_create(ModelImpl& m, int mode) {
   MLB_CUDA(cudaMallocHost(&c->h_logits, (size_t)cf.vocab_size * 4));
   MLB_CUDA(cudaMallocHost(&c->h_tokens, (size_t)cf.max_seq_len * 4));
   c->plan_step();
+  if (c->kv_bf16 && !c->step.ok)
+    invalid("mlb_context_create: a bf16 KV cache needs the decode step kernel, which this model "
+            "cannot use: " + c->step.why);
   c->use_step = c->step.ok;
   c->build_graph();
   return c.release();
@@ -614,7 +627,6 @@ void ContextImpl::plan_step() {
     return no("the step kernel does not fit on an SM");
 
   // phases
-  const size_t layer_kv = (size_t)cf.max_seq_len * m->kv_heads * D;
   std::vector<StepPhase> ph;
   auto gemv = [&](const QMatrix& q, const float* x, const float* norm_w, const EpiParams& e) {
     StepPhase p{};
@@ -666,8 +678,9 @@ void ContextImpl::plan_step() {
     e.bias = L.bias.p ? L.bias.as<float>() : nullptr;
     e.rope = m->rope.as<float2>();
     e.pos = d_pos;
-    e.keys = keys.as<float>() + (size_t)l * layer_kv;
-    e.values = values.as<float>() + (size_t)l * layer_kv;
+    e.keys = kv_layer(keys, l);
+    e.values = kv_layer(values, l);
+    e.kv_bf16 = kv_bf16;
     e.q_out = q.as<float>();
     gemv(L.qkv, x_in, L.attn_norm.as<float>(), e);
     if (l > 0) ss_in(ph.back(), ss_xa);
@@ -675,8 +688,9 @@ void ContextImpl::plan_step() {
     StepPhase a{};
     a.kind = kPhaseAttn;
     a.at.q = q.as<float>();
-    a.at.keys = keys.as<float>() + (size_t)l * layer_kv;
-    a.at.values = values.as<float>() + (size_t)l * layer_kv;
+    a.at.keys = kv_layer(keys, l);
+    a.at.values = kv_layer(values, l);
+    a.at.kv_bf16 = kv_bf16;
     a.at.out = attn.as<float>();
     a.at.H = m->q_heads;
     a.at.KV = m->kv_heads;
@@ -859,7 +873,6 @@ void ContextImpl::record_step(cudaStream_t s, bool pdl, bool full_logits) {
   int* d_pos = d_token + 1;
   int* d_step = d_token + 2;
   int* d_tokens = d_token + 4;
-  const size_t layer_kv = (size_t)cf.max_seq_len * m->kv_heads * D;
   const float scale = attn_scale(D);
   if (use_step) {
     (void)pdl;
@@ -884,8 +897,8 @@ void ContextImpl::record_step(cudaStream_t s, bool pdl, bool full_logits) {
     e.bias = L.bias.p ? L.bias.as<float>() : nullptr;
     e.rope = m->rope.as<float2>();
     e.pos = d_pos;
-    e.keys = keys.as<float>() + (size_t)l * layer_kv;
-    e.values = values.as<float>() + (size_t)l * layer_kv;
+    e.keys = kv_layer(keys, l);
+    e.values = kv_layer(values, l);
     e.q_out = q.as<float>();
     NormSpec norm{L.attn_norm.as<float>(), cf.rms_norm_eps};
     gemv_launch(L.qkv, xa.as<float>(), 1, cf.dim, norm, e, ws, s, pdl);
@@ -893,8 +906,8 @@ void ContextImpl::record_step(cudaStream_t s, bool pdl, bool full_logits) {
 
     AttnLaunch al;
     al.q = q.as<float>();
-    al.keys = keys.as<float>() + (size_t)l * layer_kv;
-    al.values = values.as<float>() + (size_t)l * layer_kv;
+    al.keys = kv_layer(keys, l);
+    al.values = kv_layer(values, l);
     al.pos_dev = d_pos;
     al.H = m->q_heads;
     al.KV = m->kv_heads;
@@ -1035,6 +1048,8 @@ void ContextImpl::replay(bool greedy) {
 
 void ContextImpl::set_use_step(bool on) {
   if (on && !step.ok) invalid("decode step kernel unavailable: " + step.why);
+  if (!on && kv_bf16)
+    invalid("mlb_context_set_step_kernel: a bf16 KV cache runs on the step kernel only");
   set_device(m->device);
   MLB_CUDA(cudaStreamSynchronize(stream));
   use_step = on;
@@ -1222,7 +1237,7 @@ void context_fill_kv(ContextImpl& c, int n_pos, uint64_t seed, float scale) {
   const mlb_config& cf = c.m->cfg;
   if (n_pos < 0 || n_pos > cf.max_seq_len) out_of_range("mlb_context_fill_kv: n_pos out of range");
   set_device(c.m->device);
-  fill_kv_rows(c.keys.p, c.values.p, false, *c.m, n_pos, seed, scale, c.stream);
+  fill_kv_rows(c.keys.p, c.values.p, c.kv_bf16, *c.m, n_pos, seed, scale, c.stream);
   MLB_CUDA(cudaStreamSynchronize(c.stream));
 }
 

@@ -102,7 +102,10 @@ struct ContextImpl {
   ModelImpl* m = nullptr;
   int attention_mode = MLB_ATTN_CPU_COMPAT;
   cudaStream_t stream = nullptr;
-  DevBuf keys, values;        // [L][S][KV_local][D]
+  DevBuf keys, values;        // [L][S][KV_local][D], fp32 or (kv_bf16) bf16 elements
+  bool kv_bf16 = false;
+  // layer l's base of the keys / values, typed as the kernels take it
+  float* kv_layer(const DevBuf& b, int l) const;
   DevBuf xa, xb, y, q, attn, hidden, logits_local, logits;
   DevBuf ss_x;  // step kernel: per-tile sums of squares of xa, then of xb
   DevBuf gemv_ws, gemv_cnt, attn_ws, attn_cnt, status;

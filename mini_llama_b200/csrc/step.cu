@@ -698,10 +698,32 @@ __device__ __forceinline__ void attn_combine(const AttnScratch& s, int D, int gq
   __syncthreads();
 }
 
+// Four K or V elements of a cache row through L2 (ld.global.cg) as loaded:
+// fp32 a float4, bf16 a uint2 widened only when the block is used.
+template <bool BF>
+struct StepKv {
+  using T = float4;
+  static __device__ __forceinline__ T load(const uint8_t* p) {
+    return __ldcg(reinterpret_cast<const float4*>(p));
+  }
+  static __device__ __forceinline__ T zero() { return make_float4(0.f, 0.f, 0.f, 0.f); }
+  static __device__ __forceinline__ float4 widen(const T& v) { return v; }
+};
+template <>
+struct StepKv<true> {
+  using T = uint2;
+  static __device__ __forceinline__ T load(const uint8_t* p) {
+    return __ldcg(reinterpret_cast<const uint2*>(p));
+  }
+  static __device__ __forceinline__ T zero() { return make_uint2(0u, 0u); }
+  static __device__ __forceinline__ float4 widen(const T& u) { return KvRaw<true>::widen(u); }
+};
+
 // One warp: positions [t0, t1) of a piece of KV head kvh, blocks of PB
 // positions round robin over warps; online softmax per query head. Query
 // heads go HG at a time (each pass re-reads the block's K/V rows, from L2).
-template <int HG>
+// BF: the cache holds bf16 elements.
+template <int HG, bool BF>
 __device__ __forceinline__ void attn_warp(const StepAttn& at, const AttnScratch& s, int gq,
                                           int kvh, int t0, int t1, int v_end, int warp,
                                           int lane) {
@@ -709,9 +731,12 @@ __device__ __forceinline__ void attn_warp(const StepAttn& at, const AttnScratch&
   constexpr unsigned kNvMask = (1u << NV) - 1u;  // lanes < NV
   const int D = at.D, nvec = D >> 2, rec = attn_rec(D);
   const bool dl = lane < nvec;
-  const size_t row = (size_t)at.KV * D;
-  const float* kbase = at.keys + (size_t)kvh * D + 4 * lane;
-  const float* vbase = at.values + (size_t)kvh * D + 4 * lane;
+  using Kv = StepKv<BF>;
+  using KvT = typename Kv::T;
+  constexpr size_t esz = BF ? 2 : 4;
+  const size_t row = (size_t)at.KV * D * esz;  // bytes from one position to the next
+  const uint8_t* kbase = reinterpret_cast<const uint8_t*>(at.keys) + ((size_t)kvh * D + 4 * lane) * esz;
+  const uint8_t* vbase = reinterpret_cast<const uint8_t*>(at.values) + ((size_t)kvh * D + 4 * lane) * esz;
   float* scw = s.sc + warp * NV;
   float* alw = s.alpha + warp * HG;
   float* wp = s.wpart + (size_t)warp * gq * rec;
@@ -729,33 +754,36 @@ __device__ __forceinline__ void attn_warp(const StepAttn& at, const AttnScratch&
     // lane i < NV keeps (m, l) of query head hg + i / PB
     float m_run = -INFINITY, l_run = 0.0f;
     // K and V rows of block tb (zero past the slice)
-    auto load_block = [&](int tb, float4 (&kx)[PB], float4 (&vx)[PB]) {
+    auto load_block = [&](int tb, KvT (&kx)[PB], KvT (&vx)[PB]) {
 #pragma unroll
       for (int j = 0; j < PB; ++j) {
         const int t = tb + j;
-        kx[j] = (dl && t < t1) ? __ldcg(reinterpret_cast<const float4*>(kbase + (size_t)t * row))
-                               : make_float4(0.f, 0.f, 0.f, 0.f);
-        vx[j] = (dl && t < t1 && t < v_end)
-                    ? __ldcg(reinterpret_cast<const float4*>(vbase + (size_t)t * row))
-                    : make_float4(0.f, 0.f, 0.f, 0.f);
+        kx[j] = (dl && t < t1) ? Kv::load(kbase + (size_t)t * row) : Kv::zero();
+        vx[j] = (dl && t < t1 && t < v_end) ? Kv::load(vbase + (size_t)t * row) : Kv::zero();
       }
     };
     // narrow passes keep the next block's rows in flight while this one is
     // computed (wider passes have no registers to spare)
     constexpr bool kPipe = HG <= 2;
-    float4 kn[PB], vn[PB];
+    KvT kn[PB], vn[PB];
     if (kPipe) load_block(t0 + warp * PB, kn, vn);
     for (int tb = t0 + warp * PB; tb < t1; tb += kStepWarps * PB) {
       float4 kx[PB], vx[PB];
       if (kPipe) {
 #pragma unroll
         for (int j = 0; j < PB; ++j) {
-          kx[j] = kn[j];
-          vx[j] = vn[j];
+          kx[j] = Kv::widen(kn[j]);
+          vx[j] = Kv::widen(vn[j]);
         }
         if (tb + kStepWarps * PB < t1) load_block(tb + kStepWarps * PB, kn, vn);
       } else {
-        load_block(tb, kx, vx);
+        KvT kr[PB], vr[PB];
+        load_block(tb, kr, vr);
+#pragma unroll
+        for (int j = 0; j < PB; ++j) {
+          kx[j] = Kv::widen(kr[j]);
+          vx[j] = Kv::widen(vr[j]);
+        }
       }
       float dv[NV];
 #pragma unroll
@@ -840,7 +868,10 @@ __device__ __noinline__ bool attn_phase(StepShared& sh, const StepPhase& cur, ui
   for (int item = blockIdx.x; item < items; item += G) {
     const int kvh = item / pph, piece = item - kvh * pph;
     const int t0 = n * piece / pph, t1 = n * (piece + 1) / pph;
-    attn_warp<HG>(at, s, gq, kvh, t0, t1, v_end, warp, lane);
+    if (at.kv_bf16)
+      attn_warp<HG, true>(at, s, gq, kvh, t0, t1, v_end, warp, lane);
+    else
+      attn_warp<HG, false>(at, s, gq, kvh, t0, t1, v_end, warp, lane);
     __syncthreads();
     float* out = at.out + (size_t)kvh * gq * D;
     if (pph == 1) {

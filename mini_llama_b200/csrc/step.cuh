@@ -45,6 +45,7 @@ struct StepAttn {
   int H, KV, D;
   float scale;
   int include_current_v;
+  int kv_bf16;          // keys/values hold bf16 elements
 };
 
 struct alignas(16) StepPhase {  // copied into shared memory 16 bytes at a time
