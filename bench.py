@@ -81,6 +81,9 @@ def parse_args():
                    help="skip the GGUF load measurement of the N=1 line")
     p.add_argument("--layers", type=int, default=0,
                    help="override the layer count (small profiling cases only; not a bench line)")
+    p.add_argument("--kv", choices=["f32", "bf16"], default="f32",
+                   help="KV cache element type of the head workload's context (bf16: not the "
+                        "reference's parity mode; its ids are not compared with the CPU path)")
     p.add_argument("--per-op", action="store_true",
                    help="run the step as one kernel per op instead of the persistent kernel")
     return p.parse_args()
@@ -435,7 +438,9 @@ def measure_workload(torch, mlb, dist, args, name, cfg, qtype, bias, rank, world
     model = mlb.CudaModel(cfg, device_id=local, tp_rank=rank, tp_size=world, nccl_id=nccl_id)
     model.synthesize(qtype, SEED, with_bias=bias)
     resident, step_weights = model.bytes()
-    ctx = model.context(mlb.ATTN_CPU_COMPAT, step_kernel=False if args.per_op else None)
+    ctx = model.context(mlb.ATTN_CPU_COMPAT, step_kernel=False if args.per_op else None,
+                        kv_type=mlb.KV_BF16 if (args.kv == "bf16" and name == args.workload)
+                        else mlb.KV_F32)
     step_kernel = ctx.step_kernel()
     stream = torch.cuda.ExternalStream(ctx.stream())
     tok0 = C.prompt_ids(SEED, 1, cfg["vocab_size"])[0]
@@ -514,7 +519,8 @@ def measure_workload(torch, mlb, dist, args, name, cfg, qtype, bias, rank, world
                         "against": "one GPU (step kernel) from the same seeded state"}
         barrier()
 
-    kv_per_pos = 2 * cfg["n_layers"] * (cfg["n_kv_heads"] // world) * cfg["head_dim"] * 4
+    kv_bytes = 2 if (args.kv == "bf16" and name == args.workload) else 4
+    kv_per_pos = 2 * cfg["n_layers"] * (cfg["n_kv_heads"] // world) * cfg["head_dim"] * kv_bytes
     mid_ctx = (ctx0 + warmup + ctx_end) / 2
     step_bytes = step_weights + kv_per_pos * mid_ctx
     step_s = ms / 1e3 / steps
@@ -732,7 +738,7 @@ def run_gpu(args, cfg, qtype, bias, rank, world, local):
         parity = {}
         if head["tp_check"]:
             parity.update(head["tp_check"])
-        if cpu and "ids_match_gpu" in cpu:
+        if cpu and "ids_match_gpu" in cpu and args.kv == "f32":
             parity["ref_ids_match"] = cpu["ids_match_gpu"]
             parity["ref_ids_compared"] = cpu["ids_compared"]
         line = {
@@ -748,6 +754,7 @@ def run_gpu(args, cfg, qtype, bias, rank, world, local):
                        "l2": "no flush: each step streams %.2f GB of weights (> 126 MB L2)"
                              % (head["step_weight_bytes"] / 1e9),
                        "attention": "cpu-compat (reference CPU path V sum)",
+                       "kv_cache": args.kv,
                        "step": "persistent kernel" if head["step_kernel"] else "one kernel per op"},
             "e2e": head["e2e"],
             "roofline": head["roofline"],
