@@ -307,6 +307,13 @@ __device__ __forceinline__ void rows_multi_sum(float (&v)[NV], int lane) {
   }
 }
 
+template <int G>
+__device__ __forceinline__ void rows_combine(const AttnKArgs& a, float (&wm)[kRowsWarps][G],
+                                             float (&wl)[kRowsWarps][G],
+                                             float (&wo)[kRowsWarps][G][128],
+                                             float (&cw)[G][kRowsWarps], int& last_flag, int kvh,
+                                             int split, float* wsrow, float* outrow, int* cnt);
+
 // Decode attention for batched rows: CTA (KV head, split, row) with 8 warps.
 // Each warp streams blocks of PB positions of the split round robin, every
 // lane holding 4 of the head_dim values of the K and V rows and of each
@@ -441,8 +448,21 @@ __global__ void __launch_bounds__(kRowsThreads, 2) attn_rows_kernel(const AttnKA
 #pragma unroll
     for (int h = 0; h < G; ++h) *reinterpret_cast<float4*>(&wo[warp][h][4 * lane]) = o[h];
   }
+  rows_combine<G>(a, wm, wl, wo, cw, last_flag, kvh, split, wsrow, outrow, cnt);
+}
+
+// The end of both batched kernels, after every warp stored its (m, l, o) per
+// query head (wm, wl, wo): the CTA's record with its warps combined in warp
+// order, then, in the last split of the KV head to finish, the heads' outputs
+// from the split records in split order.
+template <int G>
+__device__ __forceinline__ void rows_combine(const AttnKArgs& a, float (&wm)[kRowsWarps][G],
+                                             float (&wl)[kRowsWarps][G],
+                                             float (&wo)[kRowsWarps][G][128],
+                                             float (&cw)[G][kRowsWarps], int& last_flag, int kvh,
+                                             int split, float* wsrow, float* outrow, int* cnt) {
+  const int D = a.D;
   __syncthreads();
-  // the CTA's record: warps combined in warp order
   if (threadIdx.x < G) {
     const int h = threadIdx.x;
     float m = -INFINITY;
@@ -499,6 +519,225 @@ __global__ void __launch_bounds__(kRowsThreads, 2) attn_rows_kernel(const AttnKA
     outrow[(size_t)(kvh * G + h) * D + d] = acc;
   }
   if (threadIdx.x == 0) cnt[kvh] = 0;
+}
+
+// A bf16 pair of two floats rounded to nearest even, x in the low half.
+__device__ __forceinline__ uint32_t bf16x2_rn(float x, float y) {
+  const __nv_bfloat162 v = __floats2bfloat162_rn(x, y);
+  return *reinterpret_cast<const uint32_t*>(&v);
+}
+
+// hi = the bf16 pair of (x, y), lo = the bf16 pair of what hi leaves.
+__device__ __forceinline__ void bf16x2_split(float x, float y, uint32_t& hi, uint32_t& lo) {
+  hi = bf16x2_rn(x, y);
+  lo = bf16x2_rn(x - __uint_as_float(hi << 16), y - __uint_as_float(hi & 0xffff0000u));
+}
+
+// D += A B, m16n8k16, bf16 operands, fp32 accumulators.
+__device__ __forceinline__ void mma_bf16_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
+                                               uint32_t b1) {
+  asm("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ uint32_t u4_word(const uint4& v, int w) {
+  return w == 0 ? v.x : (w == 1 ? v.y : (w == 2 ? v.z : v.w));
+}
+
+constexpr int kMmaD = 128;  // head_dim of the tensor-core kernel
+
+// Tensor-core form of the batched kernel for a bf16 KV cache, head_dim 128 and
+// G = 2, 4 or 8 query heads per KV head (mma.sync m16n8k16: bf16 operands,
+// fp32 accumulators). A warp takes blocks of 16 positions of the split round
+// robin:
+//   S = Q K^T  A = the group's queries: row h holds head h rounded to bf16,
+//              row 8 + h the bf16 rounding of what that leaves, so a score is
+//              row h + row 8 + h of the accumulator (rows of heads past G are
+//              zero); B = K, 8 positions per n-tile, two n-tiles, over the 8
+//              chunks of 16 head_dim values.
+//   O += P V   A = the probabilities split the same way, taken straight from
+//              the score accumulators' registers; B = V, 16 positions by 8
+//              head_dim columns, 16 n-tiles. The output is row h + row 8 + h.
+// K and V values are exact bf16 operands, the hi/lo split keeps q and p to
+// about 16 significant bits, and products are summed in fp32. Each lane reads
+// 16 contiguous bytes of a K or V row per load: the head_dim order inside each
+// 32 K values and the column order of the V n-tiles are permuted to match (q
+// takes the same permutation; the output is stored in natural order). The
+// online softmax per query head and the combines follow attn_rows_kernel.
+template <int G>
+__global__ void __launch_bounds__(kRowsThreads, 1) attn_rows_mma_kernel(const AttnKArgs a) {
+  static_assert(G == 2 || G == 4 || G == 8, "GQA group of 2, 4 or 8 query heads");
+  __shared__ float wm[kRowsWarps][G], wl[kRowsWarps][G];
+  __shared__ __align__(16) float wo[kRowsWarps][G][128];
+  __shared__ float cw[G][kRowsWarps];
+  __shared__ uint4 qf[8][32];  // A fragments of the queries: [chunk][lane]
+  __shared__ int last_flag;
+  const int KV = a.KV;
+  const int kvh = blockIdx.x, split = blockIdx.y, row = blockIdx.z;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, tig = lane & 3;
+  pdl_launch_dependents();  // dependents still wait for this grid to complete
+  pdl_wait();
+  const int seq = a.row_seq ? a.row_seq[row] : row;
+  const float* qrow = a.q + (size_t)row * a.H * kMmaD;
+  float* outrow = a.out + (size_t)row * a.H * kMmaD;
+  float* wsrow = a.ws + (size_t)row * KV * a.nsplit * G * (kMmaD + 2);
+  int* cnt = a.counters + (size_t)row * KV;
+  const int pos = a.row_pos ? a.row_pos[row] : (a.pos_dev ? *a.pos_dev : a.pos_host);
+  const int n = pos + 1;
+  const int v_end = a.include_current_v ? n : pos;
+  // this split's positions, in whole 16-position blocks
+  const int blocks = (n + 15) / 16;
+  const int per = (blocks + a.nsplit - 1) / a.nsplit;
+  const int t_begin = min(n, split * per * 16), t_end = min(n, (split + 1) * per * 16);
+
+  // Query fragments, thread i: chunk i / 32 of lane i % 32. Lane (g, t) of
+  // chunk c holds head g's values 32 (c / 2) + 8 t + 4 (c % 2) + 0..3: the
+  // first pair as k = 2t, 2t + 1 (a0 high part, a1 low part), the second as
+  // k = 2t + 8, 2t + 9 (a2, a3).
+  {
+    const int c = threadIdx.x >> 5, lg = lane >> 2, lt = lane & 3;
+    uint4 f = make_uint4(0u, 0u, 0u, 0u);
+    if (lg < G) {
+      const int v0 = (c >> 1) * 32 + lt * 8 + (c & 1) * 4;
+      const float4 v =
+          __ldg(reinterpret_cast<const float4*>(qrow + (size_t)(kvh * G + lg) * kMmaD + v0));
+      bf16x2_split(v.x, v.y, f.x, f.y);
+      bf16x2_split(v.z, v.w, f.z, f.w);
+    }
+    qf[c][lane] = f;
+  }
+  __syncthreads();
+
+  const size_t rbytes = (size_t)KV * kMmaD * 2;  // from one position's row to the next
+  const size_t e0 = ((size_t)seq * a.seq_stride + (size_t)kvh * kMmaD) * 2;
+  const uint8_t* kb = reinterpret_cast<const uint8_t*>(a.keys) + e0 + tig * 16;
+  const uint8_t* vb = reinterpret_cast<const uint8_t*>(a.values) + e0 + g * 16;
+  const uint4 z4 = make_uint4(0u, 0u, 0u, 0u);
+  float o[16][4];
+#pragma unroll
+  for (int j = 0; j < 16; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.0f;
+  float m_run = -INFINITY, l_run = 0.0f;  // head g; l_run: this lane's positions only
+  // K of block tb, n-tile nt: position tb + 8 nt + g, values 32 cp + 8 t .. + 7
+  uint4 kr[2][4];
+  auto load_k = [&](int tb) {
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt) {
+      const int t = tb + 8 * nt + g;
+      const uint8_t* p = kb + (size_t)t * rbytes;
+#pragma unroll
+      for (int cp = 0; cp < 4; ++cp)
+        kr[nt][cp] = t < t_end ? __ldcs(reinterpret_cast<const uint4*>(p + cp * 64)) : z4;
+    }
+  };
+  // V of block tb: positions tb + 2 t + {0, 1, 8, 9}, columns 64 s + 8 g .. + 7
+  uint4 vr[2][4];
+  auto load_v = [&](int tb) {
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const int t = tb + 2 * tig + (r & 1) + 8 * (r >> 1);
+      const uint8_t* p = vb + (size_t)t * rbytes;
+      const bool in = t < t_end && t < v_end;
+#pragma unroll
+      for (int s = 0; s < 2; ++s)
+        vr[s][r] = in ? __ldcs(reinterpret_cast<const uint4*>(p + s * 128)) : z4;
+    }
+  };
+  // The next block's K is loaded once the scores have used this block's, and
+  // its V once P V has used this block's, so loads stay in flight across the
+  // arithmetic without more registers.
+  const int tb0 = t_begin + warp * 16;
+  if (tb0 < t_end) {
+    load_k(tb0);
+    load_v(tb0);
+  }
+  for (int tb = tb0; tb < t_end; tb += kRowsWarps * 16) {
+    const int tn = tb + kRowsWarps * 16;  // the warp's next block
+    // scores of head g at positions tb + 8 nt + 2 t + e: acc[nt][e] + acc[nt][2 + e]
+    float sacc[2][4];
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt) sacc[nt][0] = sacc[nt][1] = sacc[nt][2] = sacc[nt][3] = 0.0f;
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+      const uint4 f = qf[c][lane];
+      const uint32_t A[4] = {f.x, f.y, f.z, f.w};
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt) {
+        const uint4& k = kr[nt][c >> 1];
+        mma_bf16_16816(sacc[nt], A, (c & 1) ? k.z : k.x, (c & 1) ? k.w : k.y);
+      }
+    }
+    if (tn < t_end) load_k(tn);
+    float sc[2][2];
+    float bmax = -INFINITY;
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int t = tb + 8 * nt + 2 * tig + e;
+        sc[nt][e] = t < t_end ? __fmul_rn(sacc[nt][e] + sacc[nt][2 + e], a.scale) : -INFINITY;
+        bmax = fmaxf(bmax, sc[nt][e]);
+      }
+    bmax = fmaxf(bmax, __shfl_xor_sync(0xffffffffu, bmax, 1));
+    bmax = fmaxf(bmax, __shfl_xor_sync(0xffffffffu, bmax, 2));
+    const float mnew = fmaxf(m_run, bmax);
+    const float al = m_run == -INFINITY ? 0.0f : expf(m_run - mnew);
+    float psum = 0.0f, pv[2][2];
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int t = tb + 8 * nt + 2 * tig + e;
+        const float p = t < t_end ? expf(sc[nt][e] - mnew) : 0.0f;
+        psum += p;
+        pv[nt][e] = t < v_end ? p : 0.0f;  // counted in the softmax, V row summed below v_end
+      }
+    l_run = fmaf(l_run, al, psum);
+    m_run = mnew;
+    if (__any_sync(0xffffffffu, al != 1.0f)) {
+#pragma unroll
+      for (int j = 0; j < 16; ++j)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) o[j][i] *= al;
+    }
+    // A = P: rows g / 8 + g the high / low parts, k = 2 t + e (n-tile 0) and
+    // 2 t + 8 + e (n-tile 1)
+    uint32_t P[4];
+    bf16x2_split(pv[0][0], pv[0][1], P[0], P[1]);
+    bf16x2_split(pv[1][0], pv[1][1], P[2], P[3]);
+    // n-tile 8 s + e, column g: value 64 s + 8 g + e; k pairs (2 t, 2 t + 1)
+    // and (2 t + 8, 2 t + 9) from two positions' words
+#pragma unroll
+    for (int s = 0; s < 2; ++s)
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const uint32_t sel = (e & 1) ? 0x7632u : 0x5410u;
+        const uint32_t b0 = __byte_perm(u4_word(vr[s][0], e >> 1), u4_word(vr[s][1], e >> 1), sel);
+        const uint32_t b1 = __byte_perm(u4_word(vr[s][2], e >> 1), u4_word(vr[s][3], e >> 1), sel);
+        mma_bf16_16816(o[8 * s + e], P, b0, b1);
+      }
+    if (tn < t_end) load_v(tn);
+  }
+  l_run += __shfl_xor_sync(0xffffffffu, l_run, 1);
+  l_run += __shfl_xor_sync(0xffffffffu, l_run, 2);
+  if (g < G) {
+    if (tig == 0) {
+      wm[warp][g] = m_run;
+      wl[warp][g] = l_run;
+    }
+    // accumulator columns 2 t, 2 t + 1 of n-tile 8 s + e: values 64 s + 8 (2 t) + e, + 8
+#pragma unroll
+    for (int s = 0; s < 2; ++s)
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const int j = 8 * s + e;
+        wo[warp][g][64 * s + 16 * tig + e] = o[j][0] + o[j][2];
+        wo[warp][g][64 * s + 16 * tig + 8 + e] = o[j][1] + o[j][3];
+      }
+  }
+  rows_combine<G>(a, wm, wl, wo, cw, last_flag, kvh, split, wsrow, outrow, cnt);
 }
 
 // Generic path for shapes the tiled kernel does not take (head_dim not a
@@ -633,6 +872,15 @@ void attn_launch(const AttnLaunch& l, cudaStream_t stream, bool pdl) {
     // nsplit split weights in 8 x G x 128 floats)
     a.nsplit = std::max(1, std::min(l.nsplit, kRowsWarps * 128));
     const dim3 grid(l.KV, a.nsplit, l.rows);
+    if (l.kv_bf16 && l.D == kMmaD && G >= 2) {
+      // bf16 K/V, head_dim 128: the tensor-core kernel
+      switch (G) {
+        case 2: launch_pdl(attn_rows_mma_kernel<2>, grid, dim3(kRowsThreads), 0, stream, pdl, a); break;
+        case 4: launch_pdl(attn_rows_mma_kernel<4>, grid, dim3(kRowsThreads), 0, stream, pdl, a); break;
+        default: launch_pdl(attn_rows_mma_kernel<8>, grid, dim3(kRowsThreads), 0, stream, pdl, a); break;
+      }
+      return;
+    }
     auto go = [&](auto f32_kernel, auto bf16_kernel) {
       if (l.kv_bf16)
         launch_pdl(bf16_kernel, grid, dim3(kRowsThreads), 0, stream, pdl, a);

@@ -230,6 +230,113 @@ def test_batch_bf16_kv_cache_matches_oracle(cuda, port, name):
         assert np.array_equal(lg[0], lg[1])
 
 
+def _hd128(dim, heads, kv, max_seq, rope_type):
+    return {"vocab_size": 512, "dim": dim, "hidden_dim": 512, "n_layers": 2, "n_heads": heads,
+            "n_kv_heads": kv, "head_dim": 128, "max_seq_len": max_seq, "rope_theta": 1000000.0,
+            "rms_norm_eps": 1e-06, "rope_type": rope_type}
+
+
+# head_dim 128 with 8, 4 and 2 query heads per KV head: the bf16 cache's
+# tensor-core attention kernel (smaller head_dim takes the register kernel)
+HD128 = {
+    "g8_q4_1_bias": (_hd128(1024, 8, 1, 1024, 1), C.Q4_1, True),
+    "g4_q8_0": (_hd128(512, 4, 1, 512, 0), C.Q8_0, False),
+    "g2_q4_0": (_hd128(512, 4, 2, 512, 0), C.Q4_0, False),
+}
+
+
+@pytest.mark.parametrize("name", list(HD128))
+def test_batch_bf16_kv_head_dim_128(cuda, port, name):
+    """Batched decode over a bf16 cache at head_dim 128 (tensor-core attention):
+    sequences at ragged depths (empty and partial 16-position blocks, splits
+    with no positions) against the C port with bf16-rounded K and V: greedy ids
+    equal, one pass's logits within the bar."""
+    cfg, qtype, bias = HD128[name]
+    model = mlb.CudaModel(cfg).synthesize(qtype, 19, with_bias=bias)
+    n_seqs, steps = 4, 6
+    depths = [0, 37, 290, 130]
+    toks = [3, 77, 150, 9]
+    b = mlb.Batch(model, n_seqs, kv_type=mlb.KV_BF16)
+    for s in range(n_seqs):
+        b.fill_kv(s, depths[s], 200 + s)
+    got = b.decode_greedy(toks, depths, steps)
+    for s in range(n_seqs):
+        pm = port_model(port, cfg, qtype, 19, bias)
+        pm.set_kv_bf16(True)
+        port_fill_kv(pm, depths[s], 200 + s, bf16=True)
+        tok = toks[s]
+        for i in range(steps):
+            lp = pm.forward_token(tok, depths[s] + i)
+            tok = int(np.argmax(lp))
+            assert tok == int(got[i, s]), (s, i)
+    b2 = mlb.Batch(model, 2, kv_type=mlb.KV_BF16)
+    b2.fill_kv(0, 300, 9)
+    b2.fill_kv(1, 300, 9)
+    pm = port_model(port, cfg, qtype, 19, bias)
+    pm.set_kv_bf16(True)
+    port_fill_kv(pm, 300, 9, bf16=True)
+    _, lg = b2.forward([0, 1], [5, 5], [300, 300], logits=True)
+    lp = pm.forward_token(5, 300)
+    assert np.abs(lg[0] - lp).max() <= LOGIT_TOL
+    assert np.array_equal(lg[0], lg[1])
+
+
+def test_batch_bf16_kv_head_dim_128_deep(cuda, port):
+    """64 sequences at depth 3000 (G = 8, head_dim 128): 64 rows of one KV head
+    make 19 splits of about 160 positions, so warps of the tensor-core
+    attention kernel run two 16-position blocks (the online softmax's
+    rescaling between blocks). Greedy ids and logits of three sequences
+    against the port."""
+    cfg, qtype, bias = HD128["g8_q4_1_bias"]
+    cfg = dict(cfg, max_seq_len=4096)
+    model = mlb.CudaModel(cfg).synthesize(qtype, 29, with_bias=bias)
+    n_seqs, depth, steps = 64, 3000, 3
+    b = mlb.Batch(model, n_seqs, kv_type=mlb.KV_BF16)
+    for s in range(n_seqs):
+        b.fill_kv(s, depth, 500 + s)
+    toks = [(7 * s + 1) % cfg["vocab_size"] for s in range(n_seqs)]
+    _, lg = b.forward(list(range(n_seqs)), toks, [depth] * n_seqs, logits=True)
+    b.reset()
+    for s in range(n_seqs):
+        b.fill_kv(s, depth, 500 + s)
+    got = b.decode_greedy(toks, [depth] * n_seqs, steps)
+    for s in (0, 31, 63):
+        pm = port_model(port, cfg, qtype, 29, bias)
+        pm.set_kv_bf16(True)
+        port_fill_kv(pm, depth, 500 + s, bf16=True)
+        lp = pm.forward_token(toks[s], depth)
+        assert np.abs(lg[s] - lp).max() <= LOGIT_TOL, s
+        tok = int(np.argmax(lp))
+        assert tok == int(got[0, s]), s
+        for i in range(1, steps):
+            tok = int(np.argmax(pm.forward_token(tok, depth + i)))
+            assert tok == int(got[i, s]), (s, i)
+
+
+def test_prefill_bf16_kv_head_dim_128(cuda, port):
+    """A 300-token prompt through ForwardBatch into a bf16 context (G = 8,
+    head_dim 128; passes of 64 rows at growing depths), then decoding on the
+    step kernel: last-token logits and the decode against the port."""
+    cfg, qtype, bias = HD128["g8_q4_1_bias"]
+    model = mlb.CudaModel(cfg).synthesize(qtype, 23, with_bias=bias)
+    pm = port_model(port, cfg, qtype, 23, bias)
+    pm.set_kv_bf16(True)
+    rng = np.random.default_rng(11)
+    prompt = [int(t) for t in rng.integers(0, cfg["vocab_size"], 300)]
+    for pos, t in enumerate(prompt):
+        lp = pm.forward_token(t, pos)
+    ctx = model.context(mlb.ATTN_CPU_COMPAT, kv_type=mlb.KV_BF16)
+    lb = ctx.forward_batch(prompt, list(range(len(prompt))))
+    assert np.abs(lb - lp).max() <= LOGIT_TOL
+    tok = int(np.argmax(lp))
+    assert int(np.argmax(lb)) == tok
+    for pos in range(len(prompt), len(prompt) + 3):
+        la, lc = ctx.forward_token(tok, pos), pm.forward_token(tok, pos)
+        assert np.abs(la - lc).max() <= LOGIT_TOL, pos
+        tok = int(np.argmax(lc))
+    ctx.close()
+
+
 def test_batch_kv_type_validation(cuda):
     cfg = meta()["small_q4_0_gqa"]["config"]
     model = mlb.CudaModel(cfg).synthesize(C.Q4_0, 3)
