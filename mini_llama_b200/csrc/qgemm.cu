@@ -33,7 +33,7 @@ namespace {
 
 constexpr int kTcWarps = 10;
 constexpr int kTcThreads = kTcWarps * 32;
-constexpr int kDqThreads = 8 * 32;
+constexpr int kDqWarps = 8;  // one arrival per dequantising warp on afull / dempty
 constexpr int kTmemCols = 512;
 constexpr int kAStageCols = 128;  // one 128-input half chunk: hi 64 columns + lo 64 columns
 constexpr int kDCol = 256;        // accumulator columns [256, 256 + 2 Mp)
@@ -528,11 +528,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const TcArgs a) 
       mbar_init(&sh.empty[s], 1);
     }
     for (int t = 0; t < 2; ++t) {
-      mbar_init(&sh.afull[t], kDqThreads);
+      mbar_init(&sh.afull[t], kDqWarps);
       mbar_init(&sh.aempty[t], 1);
     }
     mbar_init(&sh.dfull, 1);
-    mbar_init(&sh.dempty, kDqThreads);
+    mbar_init(&sh.dempty, kDqWarps);
     mbar_init(&sh.fin, 1);
     sh.abort_flag = 0;
     fence_mbar_init();
@@ -670,7 +670,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const TcArgs a) 
       const long long run_end = min(u_end, (rt + 1) * C);
       for (; u < run_end && ok; ++u, ++it) {
         const int s = (int)(it % a.stages);
-        if (!tc_wait(&sh.full[s], (uint32_t)((it / a.stages) & 1), sh, a.status, 720)) {
+        if (!__all_sync(0xffffffffu,
+                        tc_wait(&sh.full[s], (uint32_t)((it / a.stages) & 1), sh, a.status, 720))) {
           ok = false;
           break;
         }
@@ -678,7 +679,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const TcArgs a) 
         const bool valid = rt * 8 + j < a.ntiles;
         for (int kh = 0; kh < 2; ++kh, ++ait) {
           const int t = (int)(ait & 1);
-          if (!tc_wait(&sh.aempty[t], (uint32_t)(((ait >> 1) & 1) ^ 1), sh, a.status, 721)) {
+          if (!__all_sync(0xffffffffu, tc_wait(&sh.aempty[t], (uint32_t)(((ait >> 1) & 1) ^ 1), sh,
+                                               a.status, 721))) {
             ok = false;
             break;
           }
@@ -710,12 +712,14 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const TcArgs a) 
           }
           tmem_wait_st();
           tc_fence_before();
-          mbar_arrive(&sh.afull[t]);
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&sh.afull[t]);
         }
       }
       if (!ok) break;
       // the run's accumulator: hi columns [0, MP) plus lo columns [MP, 2 MP)
-      if (!tc_wait(&sh.dfull, (uint32_t)(rit & 1), sh, a.status, 722)) break;
+      if (!__all_sync(0xffffffffu, tc_wait(&sh.dfull, (uint32_t)(rit & 1), sh, a.status, 722)))
+        break;
       tc_fence_after();
       float v[NC];
 #pragma unroll
@@ -728,7 +732,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const TcArgs a) 
           v[8 * c8 + i] = __uint_as_float(hw[i]) + __uint_as_float(lw[i]);
       }
       tc_fence_before();
-      mbar_arrive(&sh.dempty);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sh.dempty);
       const int n = (int)rt * kTcRows + lr;
       const bool whole = run_start == rt * C && run_end == (rt + 1) * C;
       if (!whole) {
