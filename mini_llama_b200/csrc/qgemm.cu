@@ -603,7 +603,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const TcArgs a) 
     if (lane == 0) {
       const uint32_t d_t = tbase + kDCol;
       constexpr uint32_t id2 = idesc_f16(2 * MP), id1 = idesc_f16(MP);
-      long long it = 0, ait = 0, rit = 0;
+      // ring stage of the next unit and its phase parity, kept as counters
+      // (no 64-bit division between units: this thread's issue rate bounds
+      // the kernel)
+      int s = 0;
+      uint32_t sph = 0u;
+      long long ait = 0, rit = 0;
       bool ok = true;
       for (long long u = u_begin; u < u_end && ok; ++rit) {
         const long long rt = u / C;
@@ -611,9 +616,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const TcArgs a) 
         if (!tc_wait(&sh.dempty, (uint32_t)((rit & 1) ^ 1), sh, a.status, 710)) break;
         tc_fence_after();
         bool first = true;
-        for (; u < run_end && ok; ++u, ++it) {
-          const int s = (int)(it % a.stages);
-          if (!tc_wait(&sh.full[s], (uint32_t)((it / a.stages) & 1), sh, a.status, 711)) {
+        for (; u < run_end && ok; ++u) {
+          if (!tc_wait(&sh.full[s], sph, sh, a.status, 711)) {
             ok = false;
             break;
           }
@@ -643,6 +647,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const TcArgs a) 
           }
           if (!ok) break;
           tc_commit(&sh.empty[s]);
+          if (++s == a.stages) {
+            s = 0;
+            sph ^= 1u;
+          }
         }
         if (!ok) break;
         tc_commit(&sh.dfull);
@@ -662,20 +670,24 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const TcArgs a) 
     const int j = lr >> 4, r16 = lr & 15, g = r16 & 7, h = r16 >> 3;
     const uint32_t lane_base = (uint32_t)(32 * q) << 16;
     const int cbase = half * NC;
-    long long it = 0, ait = 0, rit = 0;
+    int s = 0;  // ring stage of the next unit and its phase parity
+    uint32_t sph = 0u;
+    long long ait = 0, rit = 0;
     bool ok = true;
     for (long long u = u_begin; u < u_end && ok; ++rit) {
       const long long rt = u / C;
       const long long run_start = u;
       const long long run_end = min(u_end, (rt + 1) * C);
-      for (; u < run_end && ok; ++u, ++it) {
-        const int s = (int)(it % a.stages);
-        if (!__all_sync(0xffffffffu,
-                        tc_wait(&sh.full[s], (uint32_t)((it / a.stages) & 1), sh, a.status, 720))) {
+      for (; u < run_end && ok; ++u) {
+        if (!__all_sync(0xffffffffu, tc_wait(&sh.full[s], sph, sh, a.status, 720))) {
           ok = false;
           break;
         }
         const uint8_t* sb = ring + (size_t)s * a.stage_bytes + (size_t)j * a.sbb;
+        if (++s == a.stages) {
+          s = 0;
+          sph ^= 1u;
+        }
         const bool valid = rt * 8 + j < a.ntiles;
         for (int kh = 0; kh < 2; ++kh, ++ait) {
           const int t = (int)(ait & 1);
