@@ -390,16 +390,17 @@ __global__ void __launch_bounds__(kRowsThreads, 2) attn_rows_kernel(const AttnKA
       vx[j] = Raw::widen(vn[j]);
     }
     if (tb + kRowsWarps * PB < t_end) load_block(tb + kRowsWarps * PB, kn, vn);
+    // the lane's 4-value dots as two paired partial sums (paired fp32
+    // multiply and FMA: half the instructions of a scalar chain)
     float dv[NV];
 #pragma unroll
     for (int h = 0; h < G; ++h)
 #pragma unroll
       for (int j = 0; j < PB; ++j) {
-        float d = q[h].x * kx[j].x;
-        d = fmaf(q[h].y, kx[j].y, d);
-        d = fmaf(q[h].z, kx[j].z, d);
-        d = fmaf(q[h].w, kx[j].w, d);
-        dv[h * PB + j] = d;
+        const float2 d = __ffma2_rn(make_float2(q[h].z, q[h].w), make_float2(kx[j].z, kx[j].w),
+                                    __fmul2_rn(make_float2(q[h].x, q[h].y),
+                                               make_float2(kx[j].x, kx[j].y)));
+        dv[h * PB + j] = d.x + d.y;
       }
     rows_multi_sum<NV>(dv, lane);
     if ((lane & (32 / NV - 1)) == 0) scw[warp][lane / (32 / NV)] = dv[0];
@@ -425,17 +426,21 @@ __global__ void __launch_bounds__(kRowsThreads, 2) attn_rows_kernel(const AttnKA
     __syncwarp();
 #pragma unroll
     for (int h = 0; h < G; ++h) {
-      const float al = alw[warp][h];
-      float4 acc = make_float4(o[h].x * al, o[h].y * al, o[h].z * al, o[h].w * al);
+      // o = o * al + sum_j p_j v_j in paired fp32 operations (each pair
+      // rounds as two scalar ones); o * 1 is o, so al == 1 skips the scaling
+      const float al = alw[warp][h];  // the same in every lane
+      float2 lo = make_float2(o[h].x, o[h].y), hi = make_float2(o[h].z, o[h].w);
+      if (al != 1.0f) {
+        lo = __fmul2_rn(lo, make_float2(al, al));
+        hi = __fmul2_rn(hi, make_float2(al, al));
+      }
 #pragma unroll
       for (int j = 0; j < PB; ++j) {
         const float p = scw[warp][h * PB + j];
-        acc.x = fmaf(p, vx[j].x, acc.x);
-        acc.y = fmaf(p, vx[j].y, acc.y);
-        acc.z = fmaf(p, vx[j].z, acc.z);
-        acc.w = fmaf(p, vx[j].w, acc.w);
+        lo = __ffma2_rn(make_float2(p, p), make_float2(vx[j].x, vx[j].y), lo);
+        hi = __ffma2_rn(make_float2(p, p), make_float2(vx[j].z, vx[j].w), hi);
       }
-      o[h] = acc;
+      o[h] = make_float4(lo.x, lo.y, hi.x, hi.y);
     }
     __syncwarp();
   }
