@@ -282,6 +282,12 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnKAr
 
 constexpr int kRowsWarps = 8;
 constexpr int kRowsThreads = kRowsWarps * 32;
+// fp32 batched rows: blocks of PB positions in each warp's shared-memory ring
+// (8 positions per warp, 64 KB per CTA at head_dim <= 128)
+__host__ __device__ constexpr int rows_ring(int pb) { return 8 / pb; }
+__host__ __device__ constexpr size_t rows_ring_bytes(int pb) {
+  return (size_t)kRowsWarps * rows_ring(pb) * pb * 2 * 32 * 16;
+}
 
 // Sums NV values across the warp: afterwards v[0] of lane L holds the total of
 // value index L / (32 / NV) (NV a power of two <= 32); each round keeps half
@@ -369,27 +375,9 @@ __global__ void __launch_bounds__(kRowsThreads, 2) attn_rows_kernel(const AttnKA
     o[h] = make_float4(0.f, 0.f, 0.f, 0.f);
   }
   float m_run = -INFINITY, l_run = 0.0f;  // lane i < NV: head i / PB
-  using Raw = KvRaw<BF>;
-  using RawT = typename Raw::T;
-  auto load_block = [&](int tb, RawT (&kx)[PB], RawT (&vx)[PB]) {
-#pragma unroll
-    for (int j = 0; j < PB; ++j) {
-      const int t = tb + j;
-      kx[j] = (dl && t < t_end) ? Raw::load(kb + (size_t)t * rbytes) : Raw::zero();
-      vx[j] = (dl && t < t_end && t < v_end) ? Raw::load(vb + (size_t)t * rbytes) : Raw::zero();
-    }
-  };
-  RawT kn[PB], vn[PB];
-  const int tb0 = t_begin + warp * PB;
-  if (tb0 < t_end) load_block(tb0, kn, vn);
-  for (int tb = tb0; tb < t_end; tb += kRowsWarps * PB) {
-    float4 kx[PB], vx[PB];
-#pragma unroll
-    for (int j = 0; j < PB; ++j) {
-      kx[j] = Raw::widen(kn[j]);
-      vx[j] = Raw::widen(vn[j]);
-    }
-    if (tb + kRowsWarps * PB < t_end) load_block(tb + kRowsWarps * PB, kn, vn);
+  // One warp block: the scores of positions tb .. tb + PB - 1 against every
+  // query head of the group, the online softmax update and the V sum.
+  auto block = [&](int tb, const float4 (&kx)[PB], const float4 (&vx)[PB]) {
     // the lane's 4-value dots as two paired partial sums (paired fp32
     // multiply and FMA: half the instructions of a scalar chain)
     float dv[NV];
@@ -443,6 +431,79 @@ __global__ void __launch_bounds__(kRowsThreads, 2) attn_rows_kernel(const AttnKA
       o[h] = make_float4(lo.x, lo.y, hi.x, hi.y);
     }
     __syncwarp();
+  };
+  const int tb0 = t_begin + warp * PB;
+  constexpr int kStep = kRowsWarps * PB;  // from a warp's block to its next
+  if constexpr (BF) {
+    // bf16 rows: the next block's raw rows in registers while this one is
+    // computed
+    using Raw = KvRaw<BF>;
+    using RawT = typename Raw::T;
+    auto load_block = [&](int tb, RawT (&kx)[PB], RawT (&vx)[PB]) {
+#pragma unroll
+      for (int j = 0; j < PB; ++j) {
+        const int t = tb + j;
+        kx[j] = (dl && t < t_end) ? Raw::load(kb + (size_t)t * rbytes) : Raw::zero();
+        vx[j] = (dl && t < t_end && t < v_end) ? Raw::load(vb + (size_t)t * rbytes) : Raw::zero();
+      }
+    };
+    RawT kn[PB], vn[PB];
+    if (tb0 < t_end) load_block(tb0, kn, vn);
+    for (int tb = tb0; tb < t_end; tb += kStep) {
+      float4 kx[PB], vx[PB];
+#pragma unroll
+      for (int j = 0; j < PB; ++j) {
+        kx[j] = Raw::widen(kn[j]);
+        vx[j] = Raw::widen(vn[j]);
+      }
+      if (tb + kStep < t_end) load_block(tb + kStep, kn, vn);
+      block(tb, kx, vx);
+    }
+  } else {
+    // fp32 rows: a ring of rows_ring(PB) blocks per warp in shared memory,
+    // filled by cp.async, so all but one stay in flight during the arithmetic
+    // without holding registers. Each lane copies and later reads only its
+    // own 16 bytes of each row (no cross-lane ordering needed); a slot is
+    // refilled at the end of its block, after its values were used.
+    extern __shared__ uint4 kv_ring[];  // [warp][slot][j][K, V][lane]
+    constexpr int R = rows_ring(PB);
+    auto slot = [&](int r, int j, int kind) -> uint4* {
+      return kv_ring + ((((size_t)warp * R + r) * PB + j) * 2 + kind) * 32 + lane;
+    };
+    auto issue = [&](int tb, int r) {
+      if (dl) {
+#pragma unroll
+        for (int j = 0; j < PB; ++j) {
+          const int t = tb + j;
+          if (t < t_end) cp_async16(slot(r, j, 0), kb + (size_t)t * rbytes);
+          if (t < t_end && t < v_end) cp_async16(slot(r, j, 1), vb + (size_t)t * rbytes);
+        }
+      }
+      cp_async_commit();  // one group per block, empty past the split's end
+    };
+#pragma unroll
+    for (int r = 0; r < R; ++r) issue(tb0 + r * kStep, r);
+    int r = 0;
+    for (int tb = tb0; tb < t_end; tb += kStep) {
+      cp_async_wait<R - 1>();  // this block's group has landed
+      float4 kx[PB], vx[PB];
+#pragma unroll
+      for (int j = 0; j < PB; ++j) {
+        const int t = tb + j;
+        const uint4 kr = *slot(r, j, 0), vr = *slot(r, j, 1);
+        kx[j] = (dl && t < t_end) ? make_float4(__uint_as_float(kr.x), __uint_as_float(kr.y),
+                                                __uint_as_float(kr.z), __uint_as_float(kr.w))
+                                  : make_float4(0.f, 0.f, 0.f, 0.f);
+        vx[j] = (dl && t < t_end && t < v_end)
+                    ? make_float4(__uint_as_float(vr.x), __uint_as_float(vr.y),
+                                  __uint_as_float(vr.z), __uint_as_float(vr.w))
+                    : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+      block(tb, kx, vx);
+      issue(tb + R * kStep, r);
+      r = (r + 1) & (R - 1);
+    }
+    cp_async_wait<0>();
   }
   // this warp's (m, l, o) per query head
   if (lane < NV && lane % PB == 0) {
@@ -886,17 +947,26 @@ void attn_launch(const AttnLaunch& l, cudaStream_t stream, bool pdl) {
       }
       return;
     }
-    auto go = [&](auto f32_kernel, auto bf16_kernel) {
-      if (l.kv_bf16)
+    auto go = [&](auto f32_kernel, auto bf16_kernel, int pb, int gi) {
+      if (l.kv_bf16) {
         launch_pdl(bf16_kernel, grid, dim3(kRowsThreads), 0, stream, pdl, a);
-      else
-        launch_pdl(f32_kernel, grid, dim3(kRowsThreads), 0, stream, pdl, a);
+      } else {
+        // the fp32 kernel's K/V ring: dynamic shared memory above 48 KB
+        const size_t ring = rows_ring_bytes(pb);
+        static bool set[64][4] = {};
+        if (dev < 64 && !set[dev][gi]) {
+          MLB_CUDA(cudaFuncSetAttribute(f32_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        (int)ring));
+          set[dev][gi] = true;
+        }
+        launch_pdl(f32_kernel, grid, dim3(kRowsThreads), ring, stream, pdl, a);
+      }
     };
     switch (G) {
-      case 1: go(attn_rows_kernel<1, 4, false>, attn_rows_kernel<1, 4, true>); break;
-      case 2: go(attn_rows_kernel<2, 4, false>, attn_rows_kernel<2, 4, true>); break;
-      case 4: go(attn_rows_kernel<4, 4, false>, attn_rows_kernel<4, 4, true>); break;
-      default: go(attn_rows_kernel<8, 2, false>, attn_rows_kernel<8, 2, true>); break;
+      case 1: go(attn_rows_kernel<1, 4, false>, attn_rows_kernel<1, 4, true>, 4, 0); break;
+      case 2: go(attn_rows_kernel<2, 4, false>, attn_rows_kernel<2, 4, true>, 4, 1); break;
+      case 4: go(attn_rows_kernel<4, 4, false>, attn_rows_kernel<4, 4, true>, 4, 2); break;
+      default: go(attn_rows_kernel<8, 2, false>, attn_rows_kernel<8, 2, true>, 2, 3); break;
     }
     return;
   }
